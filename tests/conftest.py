@@ -1,0 +1,38 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+REPO = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+for p in (REPO, os.path.join(REPO, "lumina-studio_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+GOLDEN = os.path.join(REPO, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 and the built CUDA library")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    def load(name):
+        return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
+    return load
+
+
+@pytest.fixture(scope="session")
+def tiny_file(tmp_path_factory):
+    """The tiny int4 g64 model, quantized by the oracle and written by the
+    oracle writer (byte-identical to the reference-written file; pinned by
+    test_oracle_golden.py)."""
+    from oracle.quant import convert_arrays
+    from oracle.lumina_format import write_lumina
+    from lumina_b200 import synthetic
+    w = synthetic.host_weights(synthetic.TINY, seed=0)
+    payloads = convert_arrays(w, "int4", group_size=64, fp16_scales=True)
+    path = str(tmp_path_factory.mktemp("tiny") / "tiny.lumina")
+    write_lumina(path, payloads, name="tiny", rung="int4", group_size=64)
+    return path

@@ -1,0 +1,301 @@
+"""Generate the golden fixtures under tests/golden/ from the reference itself.
+
+Run in a container that holds the reference checkout (read-only is fine):
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+It imports the reference's own quantizer (lumina_format.codecs.ptq_ladder),
+writer (scripts/lumina_convert.py:write_lumina), loader
+(lumina_framework.adapters.load_model), decode model and drivers
+(lumina_framework.chat), tree verifier (lumina_framework.eagle / spec) and the
+TOPS self-test references (lumina_framework.tops), runs them on seeded inputs
+and stores their outputs. Nothing in the tests or on the GPU box reads the
+reference; they read these fixtures.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import shutil
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.abspath(os.path.join(HERE, "..", ".."))
+sys.path.insert(0, os.path.join(REPO, "lumina-studio_b200"))
+
+from lumina_b200 import synthetic  # noqa: E402
+
+
+class StubTok:
+    """Token ids in, token ids out: the prompt *is* the id list."""
+
+    def encode(self, prompt):
+        return [int(t) for t in prompt]
+
+    def decode(self, ids):
+        return " ".join(str(int(i)) for i in ids)
+
+
+def sha(*arrs) -> str:
+    h = hashlib.sha256()
+    for a in arrs:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode() + str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+FORMAT_CASES = {
+    # name: (rows, cols, kind, group)
+    "model.layers.0.a.weight": (37, 96, "int4", 64),
+    "model.layers.0.b.weight": (16, 200, "int4", 64),
+    "model.layers.0.c.weight": (17, 33, "int4", 64),
+    "model.layers.0.d.weight": (20, 130, "int3", 64),
+    "model.layers.1.e.weight": (24, 256, "int2", 128),
+    "model.layers.1.f.weight": (19, 70, "int2", 128),
+    "model.layers.1.g.weight": (24, 256, "binary", 128),
+    "model.layers.1.h.weight": (21, 384, "binary", 128),
+}
+
+
+def make_format(ref, tmp):
+    from lumina_format.codecs.ptq_ladder import quantize_binary, quantize_int
+    from lumina_convert import write_lumina
+    from lumina_framework.adapters import load_model
+
+    rng = np.random.default_rng(7)
+    out = {}
+    for group in (64, 128):
+        payloads, stats = {}, []
+        for name, (o, i, kind, g) in FORMAT_CASES.items():
+            if g != group:
+                continue
+            W = rng.standard_normal((o, i)) * 0.02
+            if kind == "binary":
+                q = quantize_binary(W, None, group_size=g)
+            else:
+                q = quantize_int(W, int(kind[-1]), None, group_size=g)
+            payloads[name] = (q.kind, (q.codes, q.scales))
+            out[name + "|W"] = W
+            out[name + "|codes"] = np.asarray(q.codes)
+            out[name + "|scales"] = np.asarray(q.scales)
+        path = os.path.join(tmp, f"small_g{group}.lumina")
+        write_lumina(path, payloads, stats, "golden", "mixed", group_size=group)
+        shutil.copy(path, os.path.join(HERE, f"small_g{group}.lumina"))
+        lm = load_model(path)
+        for name in payloads:
+            out[name + "|dequant"] = np.asarray(lm.tensors.tensors[name])
+    np.savez_compressed(os.path.join(HERE, "format_cases.npz"), **out)
+    print("format cases:", len(FORMAT_CASES))
+
+
+def tiny_lumina(tmp):
+    """Reference-quantized tiny model written and read by the reference."""
+    from lumina_convert import convert_arrays, write_lumina
+    from lumina_framework.adapters import load_model
+    cfg = synthetic.TINY
+    w = synthetic.host_weights(cfg, seed=0)
+    payloads, stats = convert_arrays(w, {}, "int4", group_size=64)
+    hashes = {}
+    fixed = {}
+    for name, (kind, payload) in payloads.items():
+        if kind == "raw":
+            fixed[name] = (kind, payload)
+            continue
+        codes, scales = payload
+        scales = np.asarray(scales, dtype=np.float32).astype(np.float16).astype(np.float32)
+        fixed[name] = (kind, (codes, scales))
+        hashes[name] = sha(np.asarray(codes).astype(np.uint8), scales)
+    path = os.path.join(tmp, "tiny.lumina")
+    write_lumina(path, fixed, stats, "tiny", "int4", group_size=64)
+    lm = load_model(path)
+    return lm.tensors.tensors, hashes, path
+
+
+def make_tiny(ref, tmp):
+    from lumina_framework import chat
+    from lumina_framework.chat import ChatModel, generate, generate_cached
+
+    cfg = synthetic.TINY
+    tensors, hashes, path = tiny_lumina(tmp)
+    import json
+    import struct
+    raw = open(path, "rb").read()
+    hlen = struct.unpack("<IIQ", raw[:16])[2]
+    hdr = json.loads(raw[16:16 + hlen])
+    # the tensor index and the blob area; the header's "matrices" list holds
+    # the converter's float error statistics and is not part of the payload
+    file_sha = hashlib.sha256(json.dumps(hdr["tensors"]).encode() + raw[16 + hlen:]).hexdigest()
+    hcfg = synthetic.hf_cfg(cfg)
+    model = ChatModel.from_tensors(tensors, hcfg, StubTok(), theta=cfg["rope_theta"])
+    prompt = synthetic.prompt_ids(cfg, 64, seed=0)
+
+    # logits of every step: wrap the head product through a probe of np.dot
+    r = generate(model, prompt, max_tokens=128, rng=np.random.default_rng(0))
+    toks = r["tokens"]
+
+    # teacher-forced logits at a few steps, straight from the reference layer
+    emb = model.t["model.embed_tokens.weight"].astype(np.float32)
+    head_t = model.head.T.astype(np.float32)
+    cache = {}
+    h = emb[np.array(prompt)]
+    for lyr in range(model.n_layer):
+        h = model._layer(h, lyr, cache, 0)
+    lg0 = (h[-1:] @ head_t)[0]
+    hid0 = h.copy()
+    pos = len(prompt)
+    steps = {}
+    forced = [int(t) for t in np.random.default_rng(9).integers(0, cfg["vocab_size"], 16)]
+    for s, tk in enumerate(forced):
+        hh = emb[[tk]]
+        for lyr in range(model.n_layer):
+            hh = model._layer(hh, lyr, cache, pos)
+        pos += 1
+        if s in (0, 7, 15):
+            steps[s] = (hh @ head_t)[0]
+
+    # prefix-cache scenarios (tests/test_prefix_cache.py:67-96 with id prompts)
+    rng = np.random.default_rng(3)
+    extra = lambda n: [int(t) for t in rng.integers(0, cfg["vocab_size"], n)]  # noqa: E731
+    p1 = prompt[:40]
+    r1 = generate(model, p1, max_tokens=8)["tokens"]
+    p2 = p1 + r1 + extra(10)
+    r2 = generate(model, p2, max_tokens=8)["tokens"]
+    p4 = p2 + r2 + extra(6)
+    r4 = generate(model, p4, max_tokens=8)["tokens"]
+    p3 = p1[:5] + extra(20)
+    r3 = generate(model, p3, max_tokens=6)["tokens"]
+    st = {"ids": [], "kv": {}, "pos": 0}
+    cached = []
+    for p, n in ((p1, 8), (p2, 8), (p3, 6), (p3, 6), (p4, 8)):
+        c = generate_cached(model, p, max_tokens=n, state=st)
+        cached.append((c["tokens"], c["stats"]["prefill_reused"], c["stats"]["prefill_computed"]))
+
+    out = {
+        "prompt": np.array(prompt), "tokens": np.array(toks), "forced": np.array(forced),
+        "logits_prefill_last": lg0.astype(np.float32),
+        "hidden_prefill_sha": np.array(sha(hid0.astype(np.float32))),
+        "file_sha": np.array(file_sha),
+        "quant_sha_names": np.array(sorted(hashes)),
+        "quant_sha": np.array([hashes[k] for k in sorted(hashes)]),
+        "scenario_prompts": np.array([len(p1), len(p2), len(p3), len(p4)]),
+        "p1": np.array(p1), "p2": np.array(p2), "p3": np.array(p3), "p4": np.array(p4),
+        "r1": np.array(r1), "r2": np.array(r2), "r3": np.array(r3), "r4": np.array(r4),
+    }
+    for s, lg in steps.items():
+        out[f"logits_step{s}"] = lg.astype(np.float32)
+    for j, (tk, reused, computed) in enumerate(cached):
+        out[f"cached{j}_tokens"] = np.array(tk)
+        out[f"cached{j}_stats"] = np.array([reused, computed])
+    np.savez_compressed(os.path.join(HERE, "tiny_decode.npz"), **out)
+    print("tiny tokens[:8]", toks[:8], "file", file_sha[:12])
+    return model, prompt
+
+
+def make_eagle(ref, model, prompt):
+    from lumina_framework.eagle import commit_verified, verify_tree
+    from lumina_framework.spec import SpecStats
+
+    cfg = synthetic.TINY
+    emb = model.t["model.embed_tokens.weight"].astype(np.float32)
+    head_t = model.head.T.astype(np.float32)
+    ids = prompt[:40]
+    cache = {}
+    h = emb[np.array(ids)]
+    for lyr in range(model.n_layer):
+        h = model._layer(h, lyr, cache, 0)
+    pos = len(ids)
+    root_lg = (h[-1:] @ head_t)[0]
+    # tree: root + 3 children, 2 grandchildren each, 2 great-grandchildren each
+    parents, depths = [-1], [0]
+    frontier = [0]
+    for b in (3, 2, 2):
+        nxt = []
+        for p in frontier:
+            for _ in range(b):
+                parents.append(p)
+                depths.append(depths[p] + 1)
+                nxt.append(len(parents) - 1)
+        frontier = nxt
+    rng = np.random.default_rng(5)
+    toks = [int(ids[-1])] + [int(t) for t in rng.integers(0, cfg["vocab_size"], len(parents) - 1)]
+    # make the path 0 -> 2 -> (first child of 2) -> (its first child) greedy-accepted
+    path = [0, 2]
+    toks[2] = int(np.argmax(root_lg))
+    order = [i for i in range(len(parents)) if depths[i] >= 1]
+    gidx = {old: new for new, old in enumerate(order)}
+    for _ in range(2):
+        lg, tc, _h = verify_tree(model, cache, pos, toks, parents, depths)
+        cur = path[-1]
+        kid = [i for i in range(1, len(parents)) if parents[i] == cur][0]
+        toks[kid] = int(np.argmax(lg[gidx[cur]]))
+        path.append(kid)
+    lg, tc, hv = verify_tree(model, cache, pos, toks, parents, depths)
+
+    def cur_lg(i):
+        return root_lg if i == 0 else lg[gidx[i]]
+
+    st = SpecStats()
+    out_toks: list = []
+    cache_c = dict(cache)
+    done, pos2, h2, last = commit_verified(model, cache_c, tc, pos, emb, toks, parents, depths,
+                                           cur_lg, st, 64, out_toks, ())
+    kv_sha = [sha(cache_c[l][0].astype(np.float32), cache_c[l][1].astype(np.float32))
+              for l in range(model.n_layer)]
+    res = {"ids": np.array(ids), "parents": np.array(parents), "depths": np.array(depths),
+           "toks": np.array(toks), "verify_argmax": lg.argmax(axis=1),
+           "verify_logits_rows": lg[:3].astype(np.float32),
+           "verify_norms": np.linalg.norm(lg, axis=1).astype(np.float64),
+           "accepted": np.array(out_toks), "pos_after": np.array(pos2),
+           "hidden_after": np.asarray(h2, dtype=np.float32),
+           "kv_sha": np.array(kv_sha), "kv_len": np.array(cache_c[0][0].shape[0])}
+    np.savez_compressed(os.path.join(HERE, "tiny_eagle.npz"), **res)
+    print("eagle accepted", out_toks, "pos", pos2)
+
+
+def make_tops(ref):
+    from lumina_framework import tops
+    sys.path.insert(0, os.path.join(REPO))
+    from oracle.tops import self_test_inputs
+    d = self_test_inputs()
+    out = dict(d)
+    out["ref_int8"] = tops._ref_int8(d["xq"], d["xs"], d["wq"], d["ws"])
+    out["ref_q4_0"] = tops._ref_q4_0(d["xq"], d["xs"], d["q4"], d["q4s"])
+    # fused.q8_repack on a seeded activation (fused.py:91-102)
+    from lumina_framework.fused import q8_repack
+    x = np.random.default_rng(12).standard_normal(1000).astype(np.float32)
+    xq, xs = q8_repack(x)
+    out["repack_x"], out["repack_xq"], out["repack_xs"] = x, xq, xs
+    # kernels.cpu_binary_gemv bit-exact case (tests/test_format_framework.py I2 shape)
+    from lumina_framework.kernels import cpu_binary_gemv, pack_signs
+    rng = np.random.default_rng(0)
+    S = np.where(rng.standard_normal((64, 512)) >= 0, 1, -1).astype(np.int8)
+    s = (np.abs(rng.standard_normal(64)) + 0.1).astype(np.float32)
+    xb = rng.standard_normal((1, 512)).astype(np.float32)
+    out["bin_S"], out["bin_s"], out["bin_x"] = S, s, xb
+    out["bin_y"] = cpu_binary_gemv(xb, pack_signs(S), s, 512)
+    np.savez_compressed(os.path.join(HERE, "tops_kat.npz"), **out)
+    print("tops KAT written")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    ref = args.reference
+    os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba_"))
+    sys.path.insert(0, os.path.join(ref, "src"))
+    sys.path.insert(0, os.path.join(ref, "scripts"))
+    with tempfile.TemporaryDirectory() as tmp:
+        make_format(ref, tmp)
+        model, prompt = make_tiny(ref, tmp)
+        make_eagle(ref, model, prompt)
+        make_tops(ref)
+
+
+if __name__ == "__main__":
+    main()
