@@ -1,0 +1,181 @@
+/* liblumina_cuda — C ABI of the B200 (sm_100a) Lumina decode path.
+ *
+ * The reference binds exactly one native library on this path: the TOPS
+ * kernels (src/lumina_framework/kernels/tops_int8.c) through ctypes
+ * (src/lumina_framework/tops.py:89-112). This header is the replacement
+ * surface: plain pointers and sizes, an int status on every entry (0 = ok,
+ * else a LUMINA_E_* code with text from lumina_last_error()), no C++ or
+ * framework types.
+ *
+ * Pointer conventions: arguments suffixed _dev are device pointers that the
+ * caller owns; _host arguments are host pointers; every other buffer is owned
+ * by the library (weights, KV pages, activations, scratch). `stream` is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream).
+ */
+#ifndef LUMINA_CUDA_H
+#define LUMINA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LUMINA_CUDA_VERSION 1
+
+enum {
+  LUMINA_OK = 0,
+  LUMINA_E_ARG = 1,          /* bad argument (shape, size, pointer, range)   */
+  LUMINA_E_CUDA = 2,         /* CUDA runtime error                           */
+  LUMINA_E_UNSUPPORTED = 3,  /* valid input this build does not handle       */
+  LUMINA_E_OOM = 4,          /* device allocation failed                     */
+  LUMINA_E_STATE = 5,        /* call out of order (e.g. model not finalized) */
+  LUMINA_E_NCCL = 6,         /* NCCL error                                   */
+  LUMINA_E_SELFTEST = 7      /* numeric self-test mismatch                   */
+};
+
+/* Lumina code kinds = bits per code (adapters/lumina.py:135-150). */
+enum { LUMINA_KIND_BINARY = 1, LUMINA_KIND_INT2 = 2, LUMINA_KIND_INT3 = 3, LUMINA_KIND_INT4 = 4 };
+/* The file's "packed" flag (adapters/lumina.py:50-76, lumina_convert.py:136-147). */
+enum { LUMINA_PACK_NONE = 0, LUMINA_PACK_NIBBLE = 1, LUMINA_PACK_2BIT = 2 };
+
+/* ---- library --------------------------------------------------------- */
+
+/* Replaces tops_version() (tops_int8.c:32), checked by tops._bind (tops.py:95-97). */
+int lumina_cuda_version(void);
+/* Text of the last error on this thread ("" if none). */
+const char* lumina_last_error(void);
+/* Number of visible CUDA devices. */
+int lumina_device_count(int* n);
+/* Numeric self-test on `device` (packed GEMV of every kind vs an exact
+ * integer model, int8 GEMV vs the tops KAT shape). Replaces tops._self_test
+ * (tops.py:152-238), which gates trust before first use. */
+int lumina_selftest(int device);
+
+/* ---- packed Lumina weights (dequant GEMV, hot path) -------------------- */
+
+typedef struct lumina_weight lumina_weight;
+
+/* Upload one `.lumina` tensor record exactly as stored in the file: `codes`
+ * is the codes blob (nibble / 2-bit / byte-per-code / packed sign bytes as
+ * the record's `packed` flag and kind say), `scales` the F32 scales blob
+ * (rows x ceil(cols/group)). The codes are re-tiled on the device for the
+ * GEMV and are never expanded to floating point. Replaces the per-tensor
+ * unpack + dequant of LuminaAdapter.load (adapters/lumina.py:122-151).
+ * For kind BINARY `cols` must be the logical width (the reference loader
+ * requires it to be ceil(cols/group)*group, lumina.py:143-148). */
+int lumina_weight_upload(int device, int kind, int group_size, int pack,
+                         const uint8_t* codes_host, size_t codes_len,
+                         const float* scales_host, size_t n_scales,
+                         int rows, int cols, lumina_weight** out);
+int lumina_weight_free(lumina_weight* w);
+int lumina_weight_info(const lumina_weight* w, int* kind, int* group_size, int* rows,
+                       int* cols, size_t* device_bytes, int* fp16_scales);
+
+/* Bit-exact unpack gate: codes as one byte each, (rows, cols) row-major
+ * (adapters/lumina.py:50-76; binary: the 0/1 sign bit, ptq_ladder.py:50-55). */
+int lumina_weight_unpack(const lumina_weight* w, uint8_t* codes_dev, void* stream);
+/* Bit-exact dequant gate: (float)((double)scale * linspace(-1,1,2^b)[code]),
+ * (rows, cols) fp32 (adapters/lumina.py:135-150). */
+int lumina_weight_dequant(const lumina_weight* w, float* out_dev, void* stream);
+
+/* y[b, n] = sum_k x[b, k] * W[n, k] for b < batch (1..16): the fused dequant
+ * GEMV that replaces `h @ W(name)` in ChatModel._layer (chat.py:239-243,282,
+ * 300-303; W = dequantized Lumina weight). x rows have stride ldx floats, y
+ * rows stride ldy floats. Uses the library's per-device activation scratch. */
+int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx,
+                float* y_dev, int ldy, void* stream);
+/* Same contraction with host buffers; copies in, runs, copies out, syncs. */
+int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, float* y_host);
+
+/* ---- int8 fused GEMV family (TOPS semantics, MoE-runtime path) -------- */
+/* Host-pointer entries with the exact argument meaning of the TOPS C ABI
+ * (caller owns every buffer, row-major (N, K) weights). */
+
+/* out[n] = ws[n] * sum_b xs[b] * dot32(xq_b, wq[n]_b); replaces tops_gemv_int8
+ * (tops_int8.c:41-66) and tops_gemv_int8_mt (:197-222) behind
+ * fused.fused_gemv_int8 (fused.py:186-214). */
+int lumina_gemv_int8(const int8_t* xq, const float* xs, const int8_t* wq, const float* ws,
+                     float* out, int N, int K);
+/* Q4_0: wq packed (N, K/2), byte j = weights 2j (low) and 2j+1 (high), value =
+ * code - 8, ws (N, K/32); replaces tops_gemv_q4_0 (tops_int8.c:73-106). */
+int lumina_gemv_q4_0(const int8_t* xq, const float* xs, const uint8_t* wq, const float* ws,
+                     float* out, int N, int K);
+/* fp16 x and W, fp32 out; replaces tops_gemv_fp16 (tops_int8.c:225-243). */
+int lumina_gemv_fp16(const void* x_fp16, const void* w_fp16, float* out, int N, int K);
+/* out[m, n] per row m as gemv_int8; replaces tops_gemm_int8 (tops_int8.c:300-326). */
+int lumina_gemm_int8(const int8_t* xq, const float* xs, const int8_t* wq, const float* ws,
+                     float* out, int M, int N, int K);
+
+/* ---- decode model: weights + paged KV + layer / step forward ---------- */
+
+typedef struct lumina_model lumina_model;
+
+typedef struct {
+  int n_layer, d_model, n_heads, n_kv, head_dim, ffn, vocab;
+  float eps;        /* RMSNorm eps (chat.py:63-66: 1e-6)                     */
+  float theta;      /* RoPE base (chat.py:119; pass explicitly)              */
+  int kv_fp16;      /* 0: fp32 KV pages, 1: fp16 KV pages                    */
+  int block_size;   /* KV page size in tokens (16)                           */
+  int max_seq;      /* KV capacity in tokens                                 */
+  int max_rows;     /* largest row count of one forward (prefill chunk)      */
+  int tp_rank, tp_size;  /* tensor-parallel shard of this process (0, 1)    */
+} lumina_model_config;
+
+/* Create a model shell on `device` and register its weights. Names are the
+ * HF-Llama tensor names the reference reads (chat.py:240-303). Packed
+ * weights transfer ownership to the model. Raw fp32 tensors (embed, head,
+ * norms — kept raw by lumina_convert.py:48-79) are rounded to fp16 exactly
+ * as ChatModel.from_tensors does (chat.py:138-143). */
+int lumina_model_create(int device, const lumina_model_config* cfg, lumina_model** out);
+int lumina_model_set_weight(lumina_model* m, const char* name, lumina_weight* w);
+int lumina_model_set_tensor(lumina_model* m, const char* name, const float* host,
+                            int rows, int cols);
+/* Check every tensor is present, allocate KV pages and buffers, build the
+ * fused projection layouts. */
+int lumina_model_finalize(lumina_model* m);
+int lumina_model_free(lumina_model* m);
+
+/* NCCL tensor parallelism: `unique_id` is the 128-byte ncclUniqueId that
+ * rank 0 created with lumina_nccl_unique_id and every rank received. */
+int lumina_nccl_unique_id(uint8_t* id128_host);
+int lumina_model_init_tp(lumina_model* m, const uint8_t* id128_host);
+
+/* KV contract of chat.py (cache[lyr] = (k, v), rows (T, n_heads, hd)). */
+int lumina_kv_length(const lumina_model* m, int* len);
+/* k[:n], v[:n] on every layer: prefix truncation (chat.py:438-447), spec
+ * rollback (chat.py:636-638). Pages are kept; only the length shrinks. */
+int lumina_kv_truncate(lumina_model* m, int len);
+/* Copy rows [start, start+n) of layer `layer` to host as fp32
+ * (n, n_heads, head_dim), GQA-expanded like chat.py:257-263. */
+int lumina_kv_read(const lumina_model* m, int layer, int start, int n,
+                   float* k_host, float* v_host);
+/* EAGLE commit (eagle.py:340-350): rows base+src[i] -> base+i for i < n on
+ * every layer, then length = base + n. */
+int lumina_kv_commit_rows(lumina_model* m, int base, const int* src_host, int n);
+
+/* One decoder layer over n rows of hidden state (device fp32, (n, d_model),
+ * updated in place): the drop-in for ChatModel._layer(x, lyr, cache, pos0,
+ * attn_bias, pos_override) (chat.py:232-304). Appends n KV rows at the
+ * current length. pos_override_host (n ints) and bias_host ((n, len+n) fp32,
+ * 0 / -inf) may be NULL. */
+int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int pos0,
+                         const int* pos_override_host, const float* bias_host,
+                         void* stream);
+/* Embed `tokens`, run every layer at positions pos0.. (appending KV) and
+ * write the head logits of the last row (or of every row if all_rows) to
+ * logits_host — the body of generate's prefill / decode loop (chat.py:
+ * 379-402) with the head GEMV of :388 (no final norm). */
+int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0,
+                   float* logits_host, int all_rows);
+/* One greedy decode step at the current KV length as a replayed CUDA graph:
+ * embed `token`, all layers, head; logits to logits_host (may be NULL),
+ * argmax (first max, as np.argmax in chat.py:339) to *argmax_host. */
+int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argmax_host);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUMINA_CUDA_H */

@@ -1,0 +1,107 @@
+// Shared definitions for liblumina_cuda (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "lumina_cuda.h"
+
+namespace lumina {
+
+// Per-thread last error text; every C-ABI entry sets it before returning a
+// non-zero status (the ctypes layer turns it into {"error": ...}).
+void set_error(const char* fmt, ...);
+const char* get_error();
+
+#define LUMINA_CUDA_TRY(expr)                                                   \
+  do {                                                                          \
+    cudaError_t _e = (expr);                                                    \
+    if (_e != cudaSuccess) {                                                    \
+      ::lumina::set_error("%s: %s (%s:%d)", #expr, cudaGetErrorString(_e),     \
+                          __FILE__, __LINE__);                                  \
+      return LUMINA_E_CUDA;                                                     \
+    }                                                                           \
+  } while (0)
+
+#define LUMINA_CHECK_ARG(cond, ...)                                             \
+  do {                                                                          \
+    if (!(cond)) {                                                              \
+      ::lumina::set_error(__VA_ARGS__);                                         \
+      return LUMINA_E_ARG;                                                      \
+    }                                                                           \
+  } while (0)
+
+#define LUMINA_LAUNCH_CHECK()                                                   \
+  do {                                                                          \
+    cudaError_t _e = cudaGetLastError();                                        \
+    if (_e != cudaSuccess) {                                                    \
+      ::lumina::set_error("kernel launch: %s (%s:%d)", cudaGetErrorString(_e), \
+                          __FILE__, __LINE__);                                  \
+      return LUMINA_E_CUDA;                                                     \
+    }                                                                           \
+  } while (0)
+
+// Streaming, read-only 128-bit load that does not allocate in L1 (weights are
+// touched once per GEMV).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Read-only cached 128-bit load (activations: reused by every row of a warp).
+__device__ __forceinline__ uint4 ldg_cached(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// independent prologue, and wait for the previous kernel's writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+int sm_count();
+
+// Launch a kernel with the programmatic-stream-serialization attribute so that
+// it may begin while its predecessor drains (kernels call pdl_wait() before
+// touching data the predecessor wrote).
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+}  // namespace lumina

@@ -1,0 +1,426 @@
+// Packed-weight upload, bit-exact unpack / dequant gates, lumina_gemv.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "weights.cuh"
+
+namespace lumina {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+const char* get_error() { return g_err; }
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
+// RAII device switch: entries run on the object's device and restore the
+// caller's current device on return.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// per-device activation scratch
+// ---------------------------------------------------------------------------
+struct Scratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+static std::mutex g_scratch_mu;
+static Scratch g_scratch[64];
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static size_t actq_bytes(int batch, int nblk_pad) {
+  const size_t n = (size_t)batch * nblk_pad;
+  return align256(n * 64) + align256(n * 4) + align256(n * 4);
+}
+
+static void carve_actq(void* base, int batch, int nblk_pad, ActQ* out) {
+  const size_t n = (size_t)batch * nblk_pad;
+  char* p = static_cast<char*>(base);
+  out->xq = reinterpret_cast<int16_t*>(p);
+  p += align256(n * 64);
+  out->sx = reinterpret_cast<float*>(p);
+  p += align256(n * 4);
+  out->xsum = reinterpret_cast<int*>(p);
+  out->nblk_pad = nblk_pad;
+}
+
+int scratch_actq(int device, int batch, int nblk_pad, ActQ* out) {
+  if (device < 0 || device >= 64) {
+    set_error("scratch: bad device %d", device);
+    return LUMINA_E_ARG;
+  }
+  const size_t need = actq_bytes(batch, nblk_pad);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  Scratch& s = g_scratch[device];
+  if (s.bytes < need) {
+    if (s.base) {
+      // a smaller scratch may still be read by queued work on any stream
+      cudaDeviceSynchronize();
+      cudaFree(s.base);
+      s.base = nullptr;
+      s.bytes = 0;
+    }
+    size_t want = std::max(need, (size_t)4 << 20);
+    if (cudaMalloc(&s.base, want) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("scratch: cudaMalloc(%zu) failed", want);
+      return LUMINA_E_OOM;
+    }
+    s.bytes = want;
+  }
+  carve_actq(s.base, batch, nblk_pad, out);
+  return LUMINA_OK;
+}
+
+size_t actq_scratch_bytes(int batch, int nblk_pad) { return actq_bytes(batch, nblk_pad); }
+void actq_carve(void* base, int batch, int nblk_pad, ActQ* out) { carve_actq(base, batch, nblk_pad, out); }
+
+// ---------------------------------------------------------------------------
+// level table: np.linspace(-1, 1, 2^b) in float64 (ptq_ladder.py:58-59)
+// ---------------------------------------------------------------------------
+static void linspace_levels(int bits, double* out) {
+  const int n = 1 << bits;
+  const volatile double start = -1.0, stop = 1.0;
+  const volatile double step = (stop - start) / (double)(n - 1);
+  for (int c = 0; c < n; ++c) {
+    volatile double y = (double)c * step;
+    out[c] = y + start;
+  }
+  out[n - 1] = stop;  // numpy sets the endpoint exactly
+}
+
+__constant__ double c_levels[4][16];
+
+static int ensure_levels() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool done[64] = {false};
+  if (dev >= 0 && dev < 64 && done[dev]) return LUMINA_OK;
+  double h[4][16] = {};
+  for (int b = 1; b <= 4; ++b) linspace_levels(b, h[b - 1]);
+  LUMINA_CUDA_TRY(cudaMemcpyToSymbol(c_levels, h, sizeof(h)));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return LUMINA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// unpack / dequant gates (read the device layout back to one code per byte)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int device_code(const lumina_weight w, const uint8_t* codes, int r, int k) {
+  const int blk = k >> 5, j = k & 31;
+  const int cbk = blocks_per_chunk(w.bits);
+  const int chunk = blk / cbk, cb = blk % cbk;
+  const uint8_t* row = codes + (size_t)r * w.row_bytes + (size_t)chunk * chunk_bytes(w.bits);
+  const uint32_t* bw = reinterpret_cast<const uint32_t*>(row) + cb * w.bits;
+  switch (w.bits) {
+    case 4: return (bw[j >> 3] >> (4 * (j & 7))) & 0xF;
+    case 2: return (bw[j >> 4] >> (2 * (j & 15))) & 0x3;
+    case 1: return (bw[0] >> j) & 0x1;
+    default: {  // int3
+      const int half = j >> 4, i = j & 15;
+      const int lo = (bw[half] >> (2 * i)) & 0x3;
+      const int hbit = (bw[2] >> (4 * half + (i >> 2) * 8 + (i & 3))) & 0x1;
+      return lo | (hbit << 2);
+    }
+  }
+}
+
+__global__ void unpack_kernel(const lumina_weight w, uint8_t* out) {
+  const size_t n = (size_t)w.rows * w.cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / w.cols), k = (int)(i % w.cols);
+    out[i] = (uint8_t)device_code(w, w.codes, r, k);
+  }
+}
+
+__global__ void dequant_kernel(const lumina_weight w, float* out) {
+  const size_t n = (size_t)w.rows * w.cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / w.cols), k = (int)(i % w.cols);
+    const int c = device_code(w, w.codes, r, k);
+    const size_t si = (size_t)r * w.n_groups + k / w.group;
+    const float s = w.fp16_scales ? __half2float(reinterpret_cast<const __half*>(w.scales)[si])
+                                  : reinterpret_cast<const float*>(w.scales)[si];
+    // adapters/lumina.py:138-139 (int) / :145-148 (binary, levels are -1/+1)
+    out[i] = __double2float_rn(__dmul_rn((double)s, c_levels[w.bits - 1][c]));
+  }
+}
+
+}  // namespace lumina
+
+using namespace lumina;
+
+// ---------------------------------------------------------------------------
+// host-side re-tiling of one file record into the device layout
+// ---------------------------------------------------------------------------
+static int file_code(int kind, int pack, const uint8_t* rowp, int k) {
+  if (pack == LUMINA_PACK_NIBBLE) return (rowp[k >> 1] >> (4 * (k & 1))) & 0xF;
+  if (pack == LUMINA_PACK_2BIT) return (rowp[k >> 2] >> (2 * (k & 3))) & 0x3;
+  if (kind == LUMINA_KIND_BINARY) return (rowp[k >> 3] >> (k & 7)) & 0x1;
+  return rowp[k];
+}
+
+extern "C" {
+
+int lumina_cuda_version(void) { return LUMINA_CUDA_VERSION; }
+
+const char* lumina_last_error(void) { return lumina::get_error(); }
+
+int lumina_device_count(int* n) {
+  LUMINA_CHECK_ARG(n, "device_count: null out");
+  int v = 0;
+  cudaError_t e = cudaGetDeviceCount(&v);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *n = 0;
+    set_error("cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  *n = v;
+  return LUMINA_OK;
+}
+
+int lumina_weight_upload(int device, int kind, int group_size, int pack, const uint8_t* codes_host,
+                         size_t codes_len, const float* scales_host, size_t n_scales, int rows, int cols,
+                         lumina_weight** out) {
+  LUMINA_CHECK_ARG(out && codes_host && scales_host, "weight_upload: null pointer");
+  *out = nullptr;
+  LUMINA_CHECK_ARG(kind >= 1 && kind <= 4, "weight_upload: kind %d not in 1..4", kind);
+  LUMINA_CHECK_ARG(rows > 0 && cols > 0, "weight_upload: bad shape (%d, %d)", rows, cols);
+  if (group_size <= 0 || group_size % 32) {
+    set_error("weight_upload: group_size %d must be a positive multiple of 32", group_size);
+    return LUMINA_E_UNSUPPORTED;
+  }
+  const int expect_pack = kind == 4 ? LUMINA_PACK_NIBBLE : (kind == 2 ? LUMINA_PACK_2BIT : LUMINA_PACK_NONE);
+  // the reader honours the flag; int4/int2 may also arrive unpacked (legacy
+  // files without the flag, adapters/lumina.py:51,76)
+  LUMINA_CHECK_ARG(pack == expect_pack || pack == LUMINA_PACK_NONE,
+                   "weight_upload: packed flag %d does not match kind %d", pack, kind);
+  const int n_groups = (cols + group_size - 1) / group_size;
+  LUMINA_CHECK_ARG(n_scales == (size_t)rows * n_groups,
+                   "weight_upload: %zu scales for (%d, %d) at group %d (want %zu)", n_scales, rows, cols,
+                   group_size, (size_t)rows * n_groups);
+  // file row stride: derived from the blob length like unpack_codes
+  // (adapters/lumina.py:53-60) for packed kinds
+  int per_byte = 1;
+  if (pack == LUMINA_PACK_NIBBLE) per_byte = 2;
+  else if (pack == LUMINA_PACK_2BIT) per_byte = 4;
+  else if (kind == LUMINA_KIND_BINARY) per_byte = 8;
+  LUMINA_CHECK_ARG(codes_len % rows == 0, "weight_upload: codes blob %zu not divisible by %d rows",
+                   codes_len, rows);
+  const size_t stride = codes_len / rows;
+  LUMINA_CHECK_ARG(stride * per_byte >= (size_t)cols, "weight_upload: codes blob too short for %d columns",
+                   cols);
+  if (pack == LUMINA_PACK_NONE && kind != LUMINA_KIND_BINARY)
+    LUMINA_CHECK_ARG(stride == (size_t)cols, "weight_upload: byte-per-code blob is not (%d, %d)", rows, cols);
+  if (kind == LUMINA_KIND_BINARY)
+    LUMINA_CHECK_ARG(stride == (size_t)(cols + 7) / 8, "weight_upload: sign blob stride %zu for %d columns",
+                     stride, cols);
+
+  const int bits = kind;
+  const int nblk = (cols + 31) / 32;
+  const int cbk = blocks_per_chunk(bits);
+  const int n_chunks = (nblk + cbk - 1) / cbk;
+  const int row_bytes = n_chunks * chunk_bytes(bits);
+
+  // re-tile on the host: for int4/int2/binary the device row is the file row
+  // zero-padded to whole chunks; int3 is packed to 3 bits per code
+  std::vector<uint8_t> dev((size_t)rows * row_bytes, 0);
+  const bool same_layout = (bits == 4 && pack == LUMINA_PACK_NIBBLE) ||
+                           (bits == 2 && pack == LUMINA_PACK_2BIT) || bits == 1;
+  for (int r = 0; r < rows; ++r) {
+    const uint8_t* src = codes_host + (size_t)r * stride;
+    uint8_t* dst = dev.data() + (size_t)r * row_bytes;
+    if (same_layout) {
+      const size_t nb = ((size_t)cols * bits + 7) / 8;
+      memcpy(dst, src, nb);
+      // clear bits past the last column inside the final byte
+      const int tail = (cols * bits) % 8;
+      if (tail) dst[nb - 1] &= (uint8_t)((1u << tail) - 1);
+      continue;
+    }
+    uint32_t* dw = reinterpret_cast<uint32_t*>(dst);
+    for (int k = 0; k < cols; ++k) {
+      int c = file_code(kind, pack, src, k);
+      if (c > (1 << bits) - 1) {
+        set_error("weight_upload: code %d out of range for int%d at (%d, %d)", c, bits, r, k);
+        return LUMINA_E_ARG;
+      }
+      const int blk = k >> 5, j = k & 31;
+      uint32_t* bw = dw + (size_t)(blk / cbk) * (chunk_bytes(bits) / 4) + (blk % cbk) * bits;
+      switch (bits) {
+        case 4: bw[j >> 3] |= (uint32_t)c << (4 * (j & 7)); break;
+        case 2: bw[j >> 4] |= (uint32_t)c << (2 * (j & 15)); break;
+        case 1: bw[0] |= (uint32_t)c << j; break;
+        default: {
+          const int half = j >> 4, i = j & 15;
+          bw[half] |= (uint32_t)(c & 3) << (2 * i);
+          bw[2] |= (uint32_t)((c >> 2) & 1) << (4 * half + (i >> 2) * 8 + (i & 3));
+        }
+      }
+    }
+  }
+  // scales: fp16 when lossless
+  bool fp16 = true;
+  std::vector<__half> hs(n_scales);
+  for (size_t i = 0; i < n_scales; ++i) {
+    const float s = scales_host[i];
+    if (!std::isfinite(s)) {
+      set_error("weight_upload: non-finite scale at %zu", i);
+      return LUMINA_E_ARG;
+    }
+    hs[i] = __float2half_rn(s);
+    if (__half2float(hs[i]) != s) fp16 = false;
+  }
+
+  DeviceGuard g(device);
+  lumina_weight* w = new lumina_weight();
+  w->device = device;
+  w->bits = bits;
+  w->group = group_size;
+  w->rows = rows;
+  w->cols = cols;
+  w->nblk = nblk;
+  w->n_chunks = n_chunks;
+  w->row_bytes = row_bytes;
+  w->n_groups = n_groups;
+  w->fp16_scales = fp16 ? 1 : 0;
+  const size_t sbytes = n_scales * (fp16 ? 2 : 4);
+  w->bytes = dev.size() + sbytes;
+  if (cudaMalloc(&w->codes, dev.size()) != cudaSuccess || cudaMalloc(&w->scales, sbytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (w->codes) cudaFree(w->codes);
+    delete w;
+    set_error("weight_upload: cudaMalloc of %zu bytes failed", dev.size() + sbytes);
+    return LUMINA_E_OOM;
+  }
+  cudaError_t e1 = cudaMemcpy(w->codes, dev.data(), dev.size(), cudaMemcpyHostToDevice);
+  cudaError_t e2 = fp16 ? cudaMemcpy(w->scales, hs.data(), sbytes, cudaMemcpyHostToDevice)
+                        : cudaMemcpy(w->scales, scales_host, sbytes, cudaMemcpyHostToDevice);
+  if (e1 != cudaSuccess || e2 != cudaSuccess) {
+    cudaFree(w->codes);
+    cudaFree(w->scales);
+    delete w;
+    set_error("weight_upload: copy failed: %s", cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+    return LUMINA_E_CUDA;
+  }
+  *out = w;
+  return LUMINA_OK;
+}
+
+int lumina_weight_free(lumina_weight* w) {
+  if (!w) return LUMINA_OK;
+  DeviceGuard g(w->device);
+  cudaFree(w->codes);
+  cudaFree(w->scales);
+  delete w;
+  return LUMINA_OK;
+}
+
+int lumina_weight_info(const lumina_weight* w, int* kind, int* group_size, int* rows, int* cols,
+                       size_t* device_bytes, int* fp16_scales) {
+  LUMINA_CHECK_ARG(w, "weight_info: null weight");
+  if (kind) *kind = w->bits;
+  if (group_size) *group_size = w->group;
+  if (rows) *rows = w->rows;
+  if (cols) *cols = w->cols;
+  if (device_bytes) *device_bytes = w->bytes;
+  if (fp16_scales) *fp16_scales = w->fp16_scales;
+  return LUMINA_OK;
+}
+
+int lumina_weight_unpack(const lumina_weight* w, uint8_t* codes_dev, void* stream) {
+  LUMINA_CHECK_ARG(w && codes_dev, "weight_unpack: null pointer");
+  DeviceGuard g(w->device);
+  unpack_kernel<<<4 * sm_count(), 256, 0, (cudaStream_t)stream>>>(*w, codes_dev);
+  LUMINA_LAUNCH_CHECK();
+  return LUMINA_OK;
+}
+
+int lumina_weight_dequant(const lumina_weight* w, float* out_dev, void* stream) {
+  LUMINA_CHECK_ARG(w && out_dev, "weight_dequant: null pointer");
+  DeviceGuard g(w->device);
+  int rc = ensure_levels();
+  if (rc) return rc;
+  dequant_kernel<<<4 * sm_count(), 256, 0, (cudaStream_t)stream>>>(*w, out_dev);
+  LUMINA_LAUNCH_CHECK();
+  return LUMINA_OK;
+}
+
+int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx, float* y_dev, int ldy,
+                void* stream) {
+  LUMINA_CHECK_ARG(w && x_dev && y_dev, "gemv: null pointer");
+  LUMINA_CHECK_ARG(batch >= 1 && batch <= 16, "gemv: batch %d not in 1..16", batch);
+  LUMINA_CHECK_ARG(ldx >= w->cols && ldy >= w->rows, "gemv: ldx %d / ldy %d smaller than (%d, %d)", ldx,
+                   ldy, w->cols, w->rows);
+  DeviceGuard g(w->device);
+  const int nblk_pad = w->n_chunks * blocks_per_chunk(w->bits);
+  ActQ q;
+  int rc = scratch_actq(w->device, batch, nblk_pad, &q);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = act_quant(x_dev, ldx, batch, w->cols, nullptr, 0.f, w->bits, q, s);
+  if (rc) return rc;
+  return gemv_launch(w, q, batch, y_dev, ldy, EPI_STORE, nullptr, 0, s);
+}
+
+int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, float* y_host) {
+  LUMINA_CHECK_ARG(w && x_host && y_host, "gemv_host: null pointer");
+  LUMINA_CHECK_ARG(batch >= 1 && batch <= 16, "gemv_host: batch %d not in 1..16", batch);
+  DeviceGuard g(w->device);
+  float *xd = nullptr, *yd = nullptr;
+  const size_t xb = (size_t)batch * w->cols * 4, yb = (size_t)batch * w->rows * 4;
+  if (cudaMalloc(&xd, xb) != cudaSuccess || cudaMalloc(&yd, yb) != cudaSuccess) {
+    cudaGetLastError();
+    if (xd) cudaFree(xd);
+    set_error("gemv_host: cudaMalloc failed");
+    return LUMINA_E_OOM;
+  }
+  int rc = LUMINA_OK;
+  if (cudaMemcpy(xd, x_host, xb, cudaMemcpyHostToDevice) != cudaSuccess) {
+    set_error("gemv_host: H2D copy failed");
+    rc = LUMINA_E_CUDA;
+  }
+  if (!rc) rc = lumina_gemv(w, xd, batch, w->cols, yd, w->rows, nullptr);
+  if (!rc && cudaMemcpy(y_host, yd, yb, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    set_error("gemv_host: D2H copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+    rc = LUMINA_E_CUDA;
+  }
+  cudaFree(xd);
+  cudaFree(yd);
+  return rc;
+}
+
+}  // extern "C"
