@@ -143,7 +143,9 @@ int lumina_nccl_unique_id(uint8_t* id128_host);
 int lumina_model_init_tp(lumina_model* m, const uint8_t* id128_host);
 
 /* KV contract of chat.py (cache[lyr] = (k, v), rows (T, n_heads, hd)). */
-int lumina_kv_length(const lumina_model* m, int* len);
+/* Rows held by `layer` (layer = -1: every layer, which must agree; layers
+ * differ only while a caller runs a forward layer by layer). */
+int lumina_kv_length(const lumina_model* m, int layer, int* len);
 /* k[:n], v[:n] on every layer: prefix truncation (chat.py:438-447), spec
  * rollback (chat.py:636-638). Pages are kept; only the length shrinks. */
 int lumina_kv_truncate(lumina_model* m, int len);
@@ -166,13 +168,32 @@ int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int po
 /* Embed `tokens`, run every layer at positions pos0.. (appending KV) and
  * write the head logits of the last row (or of every row if all_rows) to
  * logits_host — the body of generate's prefill / decode loop (chat.py:
- * 379-402) with the head GEMV of :388 (no final norm). */
+ * 379-402) with the head GEMV of :388 (no final norm). With
+ * pos_override_host (n positions) and bias_host ((n, len+n) additive, 0 /
+ * -inf) it is the tree-verification forward of eagle.verify_tree
+ * (eagle.py:259-291); both may be NULL. */
 int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0,
+                   const int* pos_override_host, const float* bias_host,
                    float* logits_host, int all_rows);
 /* One greedy decode step at the current KV length as a replayed CUDA graph:
  * embed `token`, all layers, head; logits to logits_host (may be NULL),
  * argmax (first max, as np.argmax in chat.py:339) to *argmax_host. */
 int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argmax_host);
+
+/* n greedy decode steps with the argmax of each step fed to the next on
+ * the device (no host round trip per token): the same per-token work as n
+ * calls of lumina_decode_step with argmax sampling (chat.py:339, temperature
+ * 0), generated tokens to tokens_host. The first step embeds `token`. */
+int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host);
+
+/* Measurement: replay the packed-weight GEMVs of one decode token (every
+ * layer's q/k/v, o, gate/up and down in decode order, on this model's
+ * weights and buffers) `iters` times as one CUDA graph, timed with CUDA
+ * events on the model's stream. Returns the mean duration of one GEMV
+ * launch (ms), the launches per token, and the packed bytes (codes + scales)
+ * those launches read per token. */
+int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* launches_per_token,
+                        double* bytes_per_token);
 
 #ifdef __cplusplus
 }

@@ -63,15 +63,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
                     "-I", INCLUDE, "-I", CSRC, "-I", nccl_inc, "--expt-relaxed-constexpr"]
     if os.environ.get("LUMINA_PTXAS_VERBOSE"):
         flags += ["-Xptxas", "-v"]
+    todo = []
     for s in srcs:
         o = os.path.join(BUILD, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
         if (not force and os.path.exists(o) and os.path.getmtime(o) > os.path.getmtime(s)
                 and os.path.getmtime(o) > newest_hdr):
             continue
-        r = run([nvcc, "-c", s, "-o", o] + flags, verbose)
-        if os.environ.get("LUMINA_PTXAS_VERBOSE"):
-            sys.stdout.write(r.stderr)
+        todo.append((s, o))
+    # translation units compile in parallel (the per-bit GEMV units dominate)
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(todo), os.cpu_count() or 4))) as ex:
+        for r in ex.map(lambda so: run([nvcc, "-c", so[0], "-o", so[1]] + flags, verbose), todo):
+            if os.environ.get("LUMINA_PTXAS_VERBOSE"):
+                sys.stdout.write(r.stderr)
     if force or not os.path.exists(OUT) or any(os.path.getmtime(o) > os.path.getmtime(OUT) for o in objs):
         run([nvcc, "-shared", "-o", OUT] + objs + ARCH +
             ["-L", nccl_lib, "-l:libnccl.so.2", "-Xlinker", "-rpath," + nccl_lib], verbose)

@@ -1,0 +1,7 @@
+// Packed GEMV kernels for 2-bit codes (one translation unit per bit width).
+#include "gemv_impl.cuh"
+
+namespace lumina {
+template int gemv_bits<2>(const GemvArgs&, int, int, int, cudaStream_t);
+template int gemv_fused_bits<2>(FusedArgs&, const lumina_weight*, int, int, bool, cudaStream_t);
+}  // namespace lumina

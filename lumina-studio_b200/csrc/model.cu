@@ -1,27 +1,1148 @@
-// Decode model: placeholder entries until the model runtime lands.
-#include "common.cuh"
+// Decode model: weight registry, paged KV, the dense decoder layer of
+// chat.py:_layer (232-304) on the device, whole forwards and a graph-replayed
+// greedy decode step. Optional NCCL tensor parallelism (column-parallel
+// q/k/v/gate/up/head, row-parallel o/down with an all-reduce after each).
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "model.cuh"
 
 using namespace lumina;
 
-#define NOT_YET(fn)                                   \
-  do {                                                \
-    set_error("%s: not implemented in this build", fn); \
-    return LUMINA_E_UNSUPPORTED;                      \
+namespace {
+
+struct Layer {
+  lumina_weight *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+  lumina_weight *gate = nullptr, *up = nullptr, *down = nullptr;
+  lumina_weight *qkv = nullptr, *gu = nullptr;  // fused layouts built at finalize
+  float *in_norm = nullptr, *post_norm = nullptr;
+};
+
+size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+struct lumina_model {
+  int device = 0;
+  lumina_model_config c{};
+  int nh = 0, nkv = 0, hd = 0, ffn = 0, vocab = 0, d = 0;  // local (this shard) sizes
+  std::vector<Layer> L;
+  std::vector<float> in_norm_h, post_norm_h;
+  __half* embed = nullptr;
+  int embed_rows = 0;
+  __half* head = nullptr;
+  int head_rows = 0;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  std::vector<float> rope_cos_h, rope_sin_h;
+
+  // paged KV
+  void *kpool = nullptr, *vpool = nullptr;
+  size_t layer_elems = 0;  // elements of one layer's K (or V) pool
+  int n_blocks = 0;
+  std::vector<int> bt_host;
+  std::vector<int> free_blocks;
+  int* bt_dev = nullptr;
+  std::vector<int> layer_len;
+
+  // activations
+  float *x = nullptr, *qkv_buf = nullptr, *q_buf = nullptr, *attn = nullptr, *ffn_buf = nullptr;
+  float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  int max_splits = 32, split_rows = 64;
+  ActQ aq{};
+  void* kv_tmp = nullptr;
+  float* bias_dev = nullptr;
+  int bias_rows = 64;
+  DevParams* P_dev = nullptr;
+  DevParams* P_host = nullptr;  // pinned
+  int *rowpos_dev = nullptr, *rowpos_host = nullptr, *tokens_dev = nullptr, *tokens_host = nullptr;
+  int *argmax_dev = nullptr, *argmax_host = nullptr, *src_dev = nullptr;
+  unsigned long long* amax_key_dev = nullptr;   // fused head argmax (value, index) key
+  unsigned long long* amax_key_host = nullptr;  // pinned
+  int* fault_host = nullptr;                     // pinned copy of the device fault word
+  int* attn_counters = nullptr;
+  float* logits_host = nullptr;  // pinned
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t step_graph = nullptr;
+  cudaGraphExec_t chain_graph = nullptr;  // greedy steps with on-device token feedback
+  int* chain_tokens = nullptr;            // [max_seq] generated tokens
+  int* chain_count = nullptr;
+  int graph_splits = 0;
+  bool finalized = false;
+  ncclComm_t comm = nullptr;
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+struct Guard {
+  int prev = -1;
+  explicit Guard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~Guard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int dalloc(lumina_model* m, void** p, size_t bytes) {
+  if (cudaMalloc(p, std::max<size_t>(bytes, 256)) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("model: cudaMalloc(%zu) failed", bytes);
+    return LUMINA_E_OOM;
+  }
+  m->allocs.push_back(*p);
+  return LUMINA_OK;
+}
+
+int parse_layer_name(const char* name, int* layer, std::string* what) {
+  int l = -1, n = 0;
+  if (sscanf(name, "model.layers.%d.%n", &l, &n) == 1 && n > 0) {
+    *layer = l;
+    *what = std::string(name + n);
+    return 1;
+  }
+  return 0;
+}
+
+// fused [a; b; c] rows (same kind / group / width / scale type)
+bool compatible(const lumina_weight* a, const lumina_weight* b) {
+  return a && b && a->bits == b->bits && a->group == b->group && a->cols == b->cols &&
+         a->fp16_scales == b->fp16_scales && a->row_bytes == b->row_bytes && a->spr == b->spr &&
+         a->mma == b->mma;
+}
+
+// A new tiled weight with the geometry of `a` and `rows` rows (zeroed).
+lumina_weight* alloc_like(const lumina_weight* a, int rows, int* rc) {
+  lumina_weight* w = new lumina_weight(*a);
+  w->rows = rows;
+  w->rows_pad = (rows + ROW_PAD - 1) / ROW_PAD * ROW_PAD;
+  if (a->mma) w->rows_pad = (rows + 31) / 32 * 32;
+  const size_t cb = (size_t)w->rows_pad * a->row_bytes;
+  const size_t sb = a->mma ? (size_t)w->rows_pad * a->n_groups * (a->fp16_scales ? 2 : 4)
+                           : (size_t)w->rows_pad * a->spr;
+  w->codes = nullptr;
+  w->scales = nullptr;
+  if (cudaMalloc(&w->codes, cb) != cudaSuccess || cudaMalloc(&w->scales, sb) != cudaSuccess ||
+      cudaMemset(w->codes, 0, cb) != cudaSuccess || cudaMemset(w->scales, 0, sb) != cudaSuccess) {
+    cudaGetLastError();
+    if (w->codes) cudaFree(w->codes);
+    if (w->scales) cudaFree(w->scales);
+    delete w;
+    set_error("model: fused weight allocation failed");
+    *rc = LUMINA_E_OOM;
+    return nullptr;
+  }
+  w->bytes = cb + sb;
+  *rc = LUMINA_OK;
+  return w;
+}
+
+// out row r <- row srow[r] of source sel[r] (up to three sources)
+lumina_weight* gather_rows(const std::vector<const lumina_weight*>& srcs, const std::vector<int>& sel,
+                           const std::vector<int>& srow, int* rc) {
+  lumina_weight* w = alloc_like(srcs[0], (int)sel.size(), rc);
+  if (!w) return nullptr;
+  int* d = nullptr;
+  if (cudaMalloc(&d, sel.size() * 8) != cudaSuccess) {
+    cudaGetLastError();
+    lumina_weight_free(w);
+    set_error("model: gather index allocation failed");
+    *rc = LUMINA_E_OOM;
+    return nullptr;
+  }
+  cudaMemcpy(d, sel.data(), sel.size() * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(d + sel.size(), srow.data(), sel.size() * 4, cudaMemcpyHostToDevice);
+  const lumina_weight& s0 = *srcs[0];
+  const lumina_weight& s1 = *srcs[std::min<size_t>(1, srcs.size() - 1)];
+  const lumina_weight& s2 = *srcs[std::min<size_t>(2, srcs.size() - 1)];
+  *rc = launch_gather_rows(*w, s0, s1, s2, d, d + sel.size(), nullptr);
+  const cudaError_t e = cudaDeviceSynchronize();
+  cudaFree(d);
+  if (!*rc && e != cudaSuccess) {
+    set_error("model: gather failed: %s", cudaGetErrorString(e));
+    *rc = LUMINA_E_CUDA;
+  }
+  if (*rc) {
+    lumina_weight_free(w);
+    return nullptr;
+  }
+  return w;
+}
+
+// fused q/k/v with each head's rotation pairs (j, j + hd/2) as adjacent rows
+lumina_weight* build_qkv(const lumina_weight* q, const lumina_weight* k, const lumina_weight* v, int hd, int* rc) {
+  std::vector<int> sel, srow;
+  const lumina_weight* parts[2] = {q, k};
+  for (int pi = 0; pi < 2; ++pi)
+    for (int h = 0; h < parts[pi]->rows / hd; ++h)
+      for (int p = 0; p < hd / 2; ++p)
+        for (int e = 0; e < 2; ++e) {
+          sel.push_back(pi);
+          srow.push_back(h * hd + p + e * (hd / 2));
+        }
+  for (int r = 0; r < v->rows; ++r) {
+    sel.push_back(2);
+    srow.push_back(r);
+  }
+  return gather_rows({q, k, v}, sel, srow, rc);
+}
+
+// gate/up interleaved: row 2i = gate_i, 2i+1 = up_i (SwiGLU epilogue)
+lumina_weight* build_gu(const lumina_weight* g, const lumina_weight* u, int* rc) {
+  std::vector<int> sel, srow;
+  for (int i = 0; i < g->rows; ++i)
+    for (int e = 0; e < 2; ++e) {
+      sel.push_back(e);
+      srow.push_back(i);
+    }
+  return gather_rows({g, u}, sel, srow, rc);
+}
+
+// rope tables: cos/sin(float32(p) * freq_i) with freq_i =
+// 1 / theta^(float32(2i) / hd) (chat.py:69-85), computed in double and rounded
+// once; callers wanting numpy's float32 cos/sin bit for bit pass their own
+// tables as the "rope.cos" / "rope.sin" tensors.
+void default_rope(lumina_model* m) {
+  const int half = m->hd / 2, npos = m->c.max_seq + 1;
+  m->rope_cos_h.assign((size_t)npos * half, 0.f);
+  m->rope_sin_h.assign((size_t)npos * half, 0.f);
+  for (int i = 0; i < half; ++i) {
+    const float e = (float)(2 * i) / (float)m->hd;
+    const float freq = 1.0f / powf(m->c.theta, e);
+    for (int p = 0; p < npos; ++p) {
+      const float a = (float)p * freq;
+      m->rope_cos_h[(size_t)p * half + i] = (float)cos((double)a);
+      m->rope_sin_h[(size_t)p * half + i] = (float)sin((double)a);
+    }
+  }
+}
+
+int ensure_blocks(lumina_model* m, int len) {
+  const int need = (len + m->c.block_size - 1) / m->c.block_size;
+  if (need > m->n_blocks) {
+    set_error("KV capacity exceeded: %d tokens > max_seq %d", len, m->n_blocks * m->c.block_size);
+    return LUMINA_E_OOM;
+  }
+  bool changed = false;
+  const int first = (int)m->bt_host.size();
+  while ((int)m->bt_host.size() < need) {
+    m->bt_host.push_back(m->free_blocks.back());
+    m->free_blocks.pop_back();
+    changed = true;
+  }
+  if (changed) {
+    const cudaError_t e = cudaMemcpyAsync(m->bt_dev + first, m->bt_host.data() + first,
+                                          (m->bt_host.size() - first) * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) {
+      set_error("block table upload: %s", cudaGetErrorString(e));
+      return LUMINA_E_CUDA;
+    }
+    // the pageable source must stay valid until the copy ran
+    cudaStreamSynchronize(m->stream);
+  }
+  return LUMINA_OK;
+}
+
+void release_blocks(lumina_model* m, int len) {
+  const int keep = (len + m->c.block_size - 1) / m->c.block_size;
+  while ((int)m->bt_host.size() > keep) {
+    m->free_blocks.push_back(m->bt_host.back());
+    m->bt_host.pop_back();
+  }
+}
+
+int n_splits_for(int n, int t_tot, int max_splits, int split_rows) {
+  if (n > split_rows) return 1;
+  int s = (t_tot + 63) / 64;
+  return std::max(1, std::min(s, max_splits));
+}
+
+size_t kv_es(const lumina_model* m) { return m->c.kv_fp16 ? 2 : 4; }
+
+char* layer_k(lumina_model* m, int l) { return (char*)m->kpool + (size_t)l * m->layer_elems * kv_es(m); }
+char* layer_v(lumina_model* m, int l) { return (char*)m->vpool + (size_t)l * m->layer_elems * kv_es(m); }
+
+int allreduce(lumina_model* m, float* buf, size_t n) {
+  if (!m->comm) return LUMINA_OK;
+  ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream);
+  if (r != ncclSuccess) {
+    set_error("ncclAllReduce: %s", ncclGetErrorString(r));
+    return LUMINA_E_NCCL;
+  }
+  return LUMINA_OK;
+}
+
+__global__ void add_inplace_kernel(float* x, const float* a, size_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] += a[i];
+}
+
+int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 1024);
+  cudaError_t e = launch_pdl(add_inplace_kernel, dim3(std::max(grid, 1)), dim3(256), 0, m->stream, x, a, n);
+  if (e != cudaSuccess) {
+    set_error("add launch: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+#define TRY(expr)            \
+  do {                       \
+    int _rc = (expr);        \
+    if (_rc) return _rc;     \
   } while (0)
 
-extern "C" {
-int lumina_model_create(int, const lumina_model_config*, lumina_model**) { NOT_YET("model_create"); }
-int lumina_model_set_weight(lumina_model*, const char*, lumina_weight*) { NOT_YET("model_set_weight"); }
-int lumina_model_set_tensor(lumina_model*, const char*, const float*, int, int) { NOT_YET("model_set_tensor"); }
-int lumina_model_finalize(lumina_model*) { NOT_YET("model_finalize"); }
-int lumina_model_free(lumina_model*) { return LUMINA_OK; }
-int lumina_nccl_unique_id(uint8_t*) { NOT_YET("nccl_unique_id"); }
-int lumina_model_init_tp(lumina_model*, const uint8_t*) { NOT_YET("model_init_tp"); }
-int lumina_kv_length(const lumina_model*, int*) { NOT_YET("kv_length"); }
-int lumina_kv_truncate(lumina_model*, int) { NOT_YET("kv_truncate"); }
-int lumina_kv_read(const lumina_model*, int, int, int, float*, float*) { NOT_YET("kv_read"); }
-int lumina_kv_commit_rows(lumina_model*, int, const int*, int) { NOT_YET("kv_commit_rows"); }
-int lumina_layer_forward(lumina_model*, int, float*, int, int, const int*, const float*, void*) { NOT_YET("layer_forward"); }
-int lumina_forward(lumina_model*, const int*, int, int, float*, int) { NOT_YET("forward"); }
-int lumina_decode_step(lumina_model*, int, float*, int*) { NOT_YET("decode_step"); }
+// y = W x (+ epilogue): the fused decode GEMV for 1, 2 or 4 rows, else (or
+// when the shape does not fit it) act_quant + the global-activation GEMV.
+int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
+             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk) {
+  if (w->mma) {
+    const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
+    if (rc != LUMINA_E_UNSUPPORTED) return rc;
+  }
+  if (n == 1 || n == 2 || n == 4) {
+    const int rc = gemv_fused_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
+    if (rc != LUMINA_E_UNSUPPORTED) return rc;
+  }
+  TRY(act_quant(x, ldx, n, w->cols, norm, m->c.eps, w->bits, m->aq, m->stream));
+  return gemv_launch(w, m->aq, n, y, ldy, epi, resid, ldr, m->stream, rk);
 }
+
+// One decoder layer over n rows of m->x (device params already uploaded).
+int run_layer(lumina_model* m, int l, int n, const float* bias) {
+  Layer& Ly = m->L[l];
+  const int d = m->d, nh = m->nh, nkv = m->nkv, hd = m->hd;
+  const int qw = nh * hd, kw = nkv * hd, width = qw + 2 * kw;
+  cudaStream_t s = m->stream;
+  const bool tp = m->comm != nullptr;
+  // 1) h = rmsnorm(x) -> q, k, v; RoPE; K/V appended (chat.py:240-263)
+  if (Ly.qkv) {
+    RopeKV rk{};
+    rk.nh = nh;
+    rk.nkv = nkv;
+    rk.hd = hd;
+    rk.cos_t = m->rope_cos;
+    rk.sin_t = m->rope_sin;
+    rk.row_pos = m->rowpos_dev;
+    rk.t_prev = &m->P_dev->t_prev;
+    rk.block_table = m->bt_dev;
+    rk.bs = m->c.block_size;
+    rk.kcache = layer_k(m, l);
+    rk.vcache = layer_v(m, l);
+    rk.kv_fp16 = m->c.kv_fp16;
+    rk.q_out = m->q_buf;
+    rk.row_base = 0;
+    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk));
+  } else {
+    lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
+    const int off[3] = {0, qw, qw + kw};
+    for (int i = 0; i < 3; ++i)
+      TRY(gemv_any(m, ws[i], m->x, d, n, Ly.in_norm, m->qkv_buf + off[i], width, EPI_STORE, nullptr, 0, nullptr));
+    TRY(launch_rope_append(m->c.kv_fp16, m->qkv_buf, nh, nkv, hd, m->rope_cos, m->rope_sin, m->rowpos_dev, m->P_dev,
+                           m->bt_dev, m->c.block_size, layer_k(m, l), layer_v(m, l), m->q_buf, n, s));
+  }
+  // 2) attention (chat.py:264-281)
+  const int splits = n > m->split_rows ? 1 : m->max_splits;
+  TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev, m->c.block_size,
+                       m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml, m->attn_counters, n, splits,
+                       s));
+  // 3) o_proj + residual (chat.py:282-283)
+  if (tp) {
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->part, d, EPI_STORE, nullptr, 0, nullptr));
+    TRY(allreduce(m, m->part, (size_t)n * d));
+    TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
+  } else {
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+  }
+  // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
+  if (Ly.gu) {
+    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr));
+  } else {
+    TRY(gemv_any(m, Ly.gate, m->x, d, n, Ly.post_norm, m->g_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
+    TRY(gemv_any(m, Ly.up, m->x, d, n, Ly.post_norm, m->u_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
+    TRY(launch_swiglu(m->g_buf, m->u_buf, m->ffn_buf, n, m->ffn, m->ffn, s));
+  }
+  if (tp) {
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->part, d, EPI_STORE, nullptr, 0, nullptr));
+    TRY(allreduce(m, m->part, (size_t)n * d));
+    TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
+  } else {
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+  }
+  return LUMINA_OK;
+}
+
+// head logits of `rows` rows starting at x row `first` (chat.py:388: no final
+// norm). Vocab-parallel under TP: each rank computes its slice, then an
+// all-gather assembles [rank0 | rank1 | ...].
+int run_head(lumina_model* m, int first, int rows, unsigned long long* amax = nullptr) {
+  const int V = m->head_rows;
+  if (!m->comm) {
+    return launch_dense_gemv(m->head, V, m->d, m->x + (size_t)first * m->d, m->d, rows, m->logits, V, nullptr, 0,
+                             m->stream, amax);
+  }
+  const int tp = m->c.tp_size;
+  for (int r = 0; r < rows; ++r) {
+    TRY(launch_dense_gemv(m->head, V, m->d, m->x + (size_t)(first + r) * m->d, m->d, 1, m->part, V, nullptr, 0,
+                          m->stream));
+    ncclResult_t e = ncclAllGather(m->part, m->logits + (size_t)r * V * tp, V, ncclFloat32, m->comm, m->stream);
+    if (e != ncclSuccess) {
+      set_error("ncclAllGather: %s", ncclGetErrorString(e));
+      return LUMINA_E_NCCL;
+    }
+  }
+  return LUMINA_OK;
+}
+
+int upload_params(lumina_model* m, int n, int t_prev, const int* positions, const int* tokens, int bias_ld) {
+  DevParams& P = *m->P_host;
+  P.n = n;
+  P.t_prev = t_prev;
+  P.t_tot = t_prev + n;
+  P.n_splits = n_splits_for(n, t_prev + n, m->max_splits, m->split_rows);
+  P.bias_ld = bias_ld;
+  for (int i = 0; i < n; ++i) m->rowpos_host[i] = positions[i];
+  if (tokens)
+    for (int i = 0; i < n; ++i) m->tokens_host[i] = tokens[i];
+  cudaStream_t s = m->stream;
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, s));
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->rowpos_dev, m->rowpos_host, n * sizeof(int), cudaMemcpyHostToDevice, s));
+  if (tokens) LUMINA_CUDA_TRY(cudaMemcpyAsync(m->tokens_dev, m->tokens_host, n * sizeof(int), cudaMemcpyHostToDevice, s));
+  return LUMINA_OK;
+}
+
+int check_ready(const lumina_model* m) {
+  if (!m) {
+    set_error("null model");
+    return LUMINA_E_ARG;
+  }
+  if (!m->finalized) {
+    set_error("model not finalized");
+    return LUMINA_E_STATE;
+  }
+  return LUMINA_OK;
+}
+
+int uniform_len(const lumina_model* m, int* len) {
+  const int v = m->layer_len.empty() ? 0 : m->layer_len[0];
+  for (int x : m->layer_len)
+    if (x != v) {
+      set_error("KV layers have different lengths (a layer-by-layer forward is in progress)");
+      return LUMINA_E_STATE;
+    }
+  *len = v;
+  return LUMINA_OK;
+}
+
+// Whole forward of n tokens at positions pos0.. (chunked by max_rows); head
+// logits of the last row or every row go to m->logits.
+int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int* pos_override, const float* bias,
+                 int all_rows, float* logits_host) {
+  int len = 0;
+  TRY(uniform_len(m, &len));
+  if (bias && n > m->bias_rows) {
+    set_error("forward: a bias matrix needs n <= %d rows (got %d)", m->bias_rows, n);
+    return LUMINA_E_ARG;
+  }
+  if (bias && n > m->c.max_rows) {
+    set_error("forward: a bias matrix needs one chunk (n <= max_rows %d)", m->c.max_rows);
+    return LUMINA_E_ARG;
+  }
+  for (int t : std::vector<int>(tokens, tokens + n))
+    if (t < 0 || t >= m->embed_rows) {
+      set_error("token id %d out of range [0, %d)", t, m->embed_rows);
+      return LUMINA_E_ARG;
+    }
+  const int V = m->head_rows * std::max(1, m->c.tp_size);
+  std::vector<int> pos(m->c.max_rows);
+  for (int c0 = 0; c0 < n; c0 += m->c.max_rows) {
+    const int cn = std::min(m->c.max_rows, n - c0);
+    TRY(ensure_blocks(m, len + cn));
+    for (int i = 0; i < cn; ++i) pos[i] = pos_override ? pos_override[c0 + i] : pos0 + c0 + i;
+    for (int i = 0; i < cn; ++i)
+      LUMINA_CHECK_ARG(pos[i] >= 0 && pos[i] <= m->c.max_seq, "forward: position %d beyond the RoPE table", pos[i]);
+    TRY(upload_params(m, cn, len, pos.data(), tokens + c0, bias ? len + cn : 0));
+    if (bias)
+      LUMINA_CUDA_TRY(cudaMemcpyAsync(m->bias_dev, bias, (size_t)cn * (len + cn) * 4, cudaMemcpyHostToDevice,
+                                      m->stream));
+    TRY(launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, cn, nullptr, m->stream));
+    for (int l = 0; l < m->c.n_layer; ++l) TRY(run_layer(m, l, cn, bias ? m->bias_dev : nullptr));
+    len += cn;
+    for (auto& v : m->layer_len) v = len;
+    if (logits_host && (all_rows || c0 + cn == n)) {
+      const int first = all_rows ? 0 : cn - 1, rows = all_rows ? cn : 1;
+      for (int r0 = 0; r0 < rows; r0 += m->c.max_rows) {
+        TRY(run_head(m, first + r0, std::min(rows - r0, m->c.max_rows)));
+        const int rr = std::min(rows - r0, m->c.max_rows);
+        float* dst = logits_host + (size_t)((all_rows ? c0 : 0) + r0) * V;
+        LUMINA_CUDA_TRY(cudaMemcpyAsync(dst, m->logits, (size_t)rr * V * 4, cudaMemcpyDeviceToHost, m->stream));
+      }
+    }
+  }
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return LUMINA_OK;
+}
+
+int capture_step(lumina_model* m) {
+  cudaStream_t s = m->stream;
+  cudaGraph_t g = nullptr;
+  LUMINA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = LUMINA_OK;
+  const int V = m->head_rows * std::max(1, m->c.tp_size);
+  do {
+    if (cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->rowpos_dev, m->rowpos_host, sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->tokens_dev, m->tokens_host, sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+      set_error("capture: param copy");
+      rc = LUMINA_E_CUDA;
+      break;
+    }
+    const bool fused_argmax = m->comm == nullptr;
+    if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
+                           fused_argmax ? m->amax_key_dev : nullptr, s)))
+      break;
+    for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
+    if (rc) break;
+    if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
+    if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
+    if (cudaMemcpyAsync(m->logits_host, m->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->argmax_host, m->argmax_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->amax_key_host, m->amax_key_dev, 8, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->fault_host, fault_flag_ptr(), sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+      set_error("capture: result copy");
+      rc = LUMINA_E_CUDA;
+    }
+  } while (0);
+  const cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error("capture: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  const cudaError_t ei = cudaGraphInstantiate(&m->step_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ei != cudaSuccess) {
+    set_error("graph instantiate: %s", cudaGetErrorString(ei));
+    m->step_graph = nullptr;
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+// End of a chained greedy step: the argmax becomes the next step's token
+// and every per-step value advances by one row.
+__global__ void greedy_commit_kernel(const unsigned long long* key, const int* argmax, int* tokens, DevParams* P,
+                                     int* rowpos, int* out, int* count, int max_splits) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int tok = key ? (int)(0xFFFFFFFFu - (unsigned)(*key & 0xFFFFFFFFull)) : *argmax;
+  tokens[0] = tok;
+  out[*count] = tok;
+  *count += 1;
+  P->t_prev += 1;
+  P->t_tot += 1;
+  rowpos[0] += 1;
+  const int s = (P->t_tot + 63) / 64;  // n_splits_for(1, t_tot)
+  P->n_splits = s < 1 ? 1 : (s > max_splits ? max_splits : s);
+}
+
+int capture_chain(lumina_model* m) {
+  cudaStream_t s = m->stream;
+  cudaGraph_t g = nullptr;
+  LUMINA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = LUMINA_OK;
+  const int V = m->head_rows * std::max(1, m->c.tp_size);
+  const bool fused_argmax = m->comm == nullptr;
+  do {
+    if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
+                           fused_argmax ? m->amax_key_dev : nullptr, s)))
+      break;
+    for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
+    if (rc) break;
+    if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
+    if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
+    const cudaError_t e =
+        launch_pdl(greedy_commit_kernel, dim3(1), dim3(32), 0, s, (const unsigned long long*)(fused_argmax ? m->amax_key_dev : nullptr),
+                   (const int*)m->argmax_dev, m->tokens_dev, m->P_dev, m->rowpos_dev, m->chain_tokens, m->chain_count,
+                   m->max_splits);
+    if (e != cudaSuccess) {
+      set_error("capture: commit launch: %s", cudaGetErrorString(e));
+      rc = LUMINA_E_CUDA;
+    }
+  } while (0);
+  const cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error("capture: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  const cudaError_t ei = cudaGraphInstantiate(&m->chain_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ei != cudaSuccess) {
+    set_error("graph instantiate: %s", cudaGetErrorString(ei));
+    m->chain_graph = nullptr;
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+size_t packed_bytes(const lumina_weight* w) {
+  return (size_t)w->rows * (((size_t)w->cols * w->bits + 7) / 8) +
+         (size_t)w->rows * w->n_groups * (w->fp16_scales ? 2 : 4);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lumina_model_create(int device, const lumina_model_config* cfg, lumina_model** out) {
+  LUMINA_CHECK_ARG(cfg && out, "model_create: null pointer");
+  *out = nullptr;
+  const lumina_model_config& c = *cfg;
+  LUMINA_CHECK_ARG(c.n_layer > 0 && c.d_model > 0 && c.n_heads > 0 && c.n_kv > 0 && c.head_dim > 0 && c.ffn > 0 &&
+                       c.vocab > 0,
+                   "model_create: non-positive dimension");
+  LUMINA_CHECK_ARG(c.n_heads % c.n_kv == 0, "model_create: n_heads %d not a multiple of n_kv %d", c.n_heads, c.n_kv);
+  LUMINA_CHECK_ARG(c.head_dim % 2 == 0, "model_create: odd head_dim %d", c.head_dim);
+  LUMINA_CHECK_ARG(c.block_size > 0 && c.max_seq > 0 && c.max_rows > 0, "model_create: bad KV / row capacity");
+  const int tp = std::max(1, c.tp_size);
+  LUMINA_CHECK_ARG(c.tp_rank >= 0 && c.tp_rank < tp, "model_create: tp_rank %d of %d", c.tp_rank, tp);
+  LUMINA_CHECK_ARG(c.n_kv % tp == 0 && c.n_heads % tp == 0, "model_create: heads not divisible by tp %d", tp);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    set_error("model_create: device %d not available", device);
+    return LUMINA_E_ARG;
+  }
+  lumina_model* m = new lumina_model();
+  m->device = device;
+  m->c = c;
+  m->c.tp_size = tp;
+  m->nh = c.n_heads / tp;
+  m->nkv = c.n_kv / tp;
+  m->hd = c.head_dim;
+  m->d = c.d_model;
+  m->ffn = 0;  // from the shard shapes
+  m->L.resize(c.n_layer);
+  m->layer_len.assign(c.n_layer, 0);
+  *out = m;
+  return LUMINA_OK;
+}
+
+int lumina_model_set_weight(lumina_model* m, const char* name, lumina_weight* w) {
+  LUMINA_CHECK_ARG(m && name && w, "model_set_weight: null pointer");
+  LUMINA_CHECK_ARG(!m->finalized, "model_set_weight: model already finalized");
+  LUMINA_CHECK_ARG(w->device == m->device, "model_set_weight: weight on device %d, model on %d", w->device, m->device);
+  int l = -1;
+  std::string what;
+  if (!parse_layer_name(name, &l, &what) || l < 0 || l >= m->c.n_layer) {
+    set_error("model_set_weight: %s is not a layer projection", name);
+    return LUMINA_E_ARG;
+  }
+  Layer& Ly = m->L[l];
+  lumina_weight** slot = nullptr;
+  if (what == "self_attn.q_proj.weight") slot = &Ly.q;
+  else if (what == "self_attn.k_proj.weight") slot = &Ly.k;
+  else if (what == "self_attn.v_proj.weight") slot = &Ly.v;
+  else if (what == "self_attn.o_proj.weight") slot = &Ly.o;
+  else if (what == "mlp.gate_proj.weight") slot = &Ly.gate;
+  else if (what == "mlp.up_proj.weight") slot = &Ly.up;
+  else if (what == "mlp.down_proj.weight") slot = &Ly.down;
+  if (!slot) {
+    set_error("model_set_weight: unknown projection %s (virtual-MoE layers are not built)", name);
+    return LUMINA_E_UNSUPPORTED;
+  }
+  if (*slot) lumina_weight_free(*slot);
+  *slot = w;
+  return LUMINA_OK;
+}
+
+int lumina_model_set_tensor(lumina_model* m, const char* name, const float* host, int rows, int cols) {
+  LUMINA_CHECK_ARG(m && name && host && rows > 0 && cols > 0, "model_set_tensor: bad arguments");
+  LUMINA_CHECK_ARG(!m->finalized, "model_set_tensor: model already finalized");
+  Guard g(m->device);
+  const std::string n(name);
+  const size_t cnt = (size_t)rows * cols;
+  if (n == "model.embed_tokens.weight" || n == "lm_head.weight") {
+    LUMINA_CHECK_ARG(cols == m->d, "%s: %d columns, d_model %d", name, cols, m->d);
+    std::vector<__half> h(cnt);
+    for (size_t i = 0; i < cnt; ++i) h[i] = __float2half_rn(host[i]);  // chat.py:140
+    void* p = nullptr;
+    TRY(dalloc(m, &p, cnt * 2));
+    LUMINA_CUDA_TRY(cudaMemcpy(p, h.data(), cnt * 2, cudaMemcpyHostToDevice));
+    if (n[0] == 'm') {
+      m->embed = (__half*)p;
+      m->embed_rows = rows;
+    } else {
+      m->head = (__half*)p;
+      m->head_rows = rows;
+    }
+    return LUMINA_OK;
+  }
+  if (n == "rope.cos" || n == "rope.sin") {
+    LUMINA_CHECK_ARG(cols == m->hd / 2 && rows >= m->c.max_seq + 1, "%s: want (>= %d, %d)", name, m->c.max_seq + 1,
+                     m->hd / 2);
+    auto& v = n == "rope.cos" ? m->rope_cos_h : m->rope_sin_h;
+    v.assign(host, host + (size_t)(m->c.max_seq + 1) * cols);
+    return LUMINA_OK;
+  }
+  int l = -1;
+  std::string what;
+  if (parse_layer_name(name, &l, &what) && l >= 0 && l < m->c.n_layer &&
+      (what == "input_layernorm.weight" || what == "post_attention_layernorm.weight")) {
+    LUMINA_CHECK_ARG(cnt == (size_t)m->d, "%s: %zu values, d_model %d", name, cnt, m->d);
+    std::vector<float> f(cnt);
+    for (size_t i = 0; i < cnt; ++i) f[i] = __half2float(__float2half_rn(host[i]));  // fp16 model copy
+    void* p = nullptr;
+    TRY(dalloc(m, &p, cnt * 4));
+    LUMINA_CUDA_TRY(cudaMemcpy(p, f.data(), cnt * 4, cudaMemcpyHostToDevice));
+    (what[0] == 'i' ? m->L[l].in_norm : m->L[l].post_norm) = (float*)p;
+    return LUMINA_OK;
+  }
+  set_error("model_set_tensor: %s is not a raw tensor this model uses (raw projections are not built)", name);
+  return LUMINA_E_UNSUPPORTED;
+}
+
+int lumina_model_finalize(lumina_model* m) {
+  LUMINA_CHECK_ARG(m, "model_finalize: null model");
+  if (m->finalized) return LUMINA_OK;
+  Guard g(m->device);
+  const lumina_model_config& c = m->c;
+  if (!m->embed) {
+    set_error("model_finalize: missing model.embed_tokens.weight");
+    return LUMINA_E_STATE;
+  }
+  if (!m->head) {  // tied head (chat.py:194-195)
+    if (c.tp_size > 1) {
+      set_error("model_finalize: a tied head needs lm_head.weight shards under TP");
+      return LUMINA_E_STATE;
+    }
+    m->head = m->embed;
+    m->head_rows = m->embed_rows;
+  }
+  const int qw = m->nh * m->hd, kw = m->nkv * m->hd;
+  for (int l = 0; l < c.n_layer; ++l) {
+    Layer& Ly = m->L[l];
+    if (!Ly.q || !Ly.k || !Ly.v || !Ly.o || !Ly.gate || !Ly.up || !Ly.down || !Ly.in_norm || !Ly.post_norm) {
+      set_error("model_finalize: layer %d is missing a tensor", l);
+      return LUMINA_E_STATE;
+    }
+    if (Ly.q->rows != qw || Ly.k->rows != kw || Ly.v->rows != kw || Ly.q->cols != m->d || Ly.o->rows != m->d ||
+        Ly.o->cols != qw || Ly.gate->cols != m->d || Ly.up->rows != Ly.gate->rows || Ly.down->rows != m->d ||
+        Ly.down->cols != Ly.gate->rows) {
+      set_error("model_finalize: layer %d shapes do not match the config", l);
+      return LUMINA_E_ARG;
+    }
+    if (l == 0) m->ffn = Ly.gate->rows;
+    if (Ly.gate->rows != m->ffn) {
+      set_error("model_finalize: layer %d ffn %d != %d", l, Ly.gate->rows, m->ffn);
+      return LUMINA_E_ARG;
+    }
+    int rc = LUMINA_OK;
+    if (compatible(Ly.q, Ly.k) && compatible(Ly.q, Ly.v)) {
+      Ly.qkv = build_qkv(Ly.q, Ly.k, Ly.v, m->hd, &rc);
+      if (rc) return rc;
+      lumina_weight_free(Ly.q);
+      lumina_weight_free(Ly.k);
+      lumina_weight_free(Ly.v);
+      Ly.q = Ly.k = Ly.v = Ly.qkv;  // keep non-null for the shape checks; freed once
+    }
+    if (compatible(Ly.gate, Ly.up)) {
+      Ly.gu = build_gu(Ly.gate, Ly.up, &rc);
+      if (rc) return rc;
+      lumina_weight_free(Ly.gate);
+      lumina_weight_free(Ly.up);
+      Ly.gate = Ly.up = Ly.gu;
+    }
+  }
+  // rope tables
+  if (m->rope_cos_h.empty() || m->rope_sin_h.empty()) default_rope(m);
+  const size_t rbytes = m->rope_cos_h.size() * 4;
+  TRY(dalloc(m, (void**)&m->rope_cos, rbytes));
+  TRY(dalloc(m, (void**)&m->rope_sin, rbytes));
+  LUMINA_CUDA_TRY(cudaMemcpy(m->rope_cos, m->rope_cos_h.data(), rbytes, cudaMemcpyHostToDevice));
+  LUMINA_CUDA_TRY(cudaMemcpy(m->rope_sin, m->rope_sin_h.data(), rbytes, cudaMemcpyHostToDevice));
+  // KV pool [layer][block][nkv][bs][hd]
+  m->n_blocks = (c.max_seq + c.block_size - 1) / c.block_size;
+  m->layer_elems = (size_t)m->n_blocks * m->nkv * c.block_size * m->hd;
+  TRY(dalloc(m, &m->kpool, m->layer_elems * c.n_layer * kv_es(m)));
+  TRY(dalloc(m, &m->vpool, m->layer_elems * c.n_layer * kv_es(m)));
+  TRY(dalloc(m, (void**)&m->bt_dev, (size_t)m->n_blocks * 4));
+  m->free_blocks.clear();
+  for (int b = m->n_blocks - 1; b >= 0; --b) m->free_blocks.push_back(b);
+  // activations
+  const int R = c.max_rows, V = m->head_rows * c.tp_size;
+  TRY(dalloc(m, (void**)&m->x, (size_t)R * m->d * 4));
+  TRY(dalloc(m, (void**)&m->qkv_buf, (size_t)R * (qw + 2 * kw) * 4));
+  TRY(dalloc(m, (void**)&m->q_buf, (size_t)R * qw * 4));
+  TRY(dalloc(m, (void**)&m->attn, (size_t)R * qw * 4));
+  TRY(dalloc(m, (void**)&m->ffn_buf, (size_t)R * m->ffn * 4));
+  TRY(dalloc(m, (void**)&m->g_buf, (size_t)R * m->ffn * 4));
+  TRY(dalloc(m, (void**)&m->u_buf, (size_t)R * m->ffn * 4));
+  TRY(dalloc(m, (void**)&m->part, (size_t)std::max(R * m->d, m->head_rows) * 4));
+  TRY(dalloc(m, (void**)&m->logits, (size_t)R * V * 4));
+  m->split_rows = std::min(64, R);
+  TRY(dalloc(m, (void**)&m->part_o, (size_t)m->max_splits * m->split_rows * qw * 4));
+  TRY(dalloc(m, (void**)&m->part_ml, (size_t)m->max_splits * m->split_rows * m->nh * 2 * 4));
+  const int kmax = std::max(std::max(m->d, qw), m->ffn);
+  const int nblk_pad = ((kmax + 31) / 32 + 4) / 4 * 4;  // whole chunks for every kind
+  void* aqb = nullptr;
+  TRY(dalloc(m, &aqb, actq_scratch_bytes(R, nblk_pad)));
+  actq_carve(aqb, R, nblk_pad, &m->aq);
+  TRY(dalloc(m, &m->kv_tmp, (size_t)R * 2 * m->nkv * m->hd * kv_es(m)));
+  m->bias_rows = std::min(64, R);
+  TRY(dalloc(m, (void**)&m->bias_dev, (size_t)m->bias_rows * (c.max_seq + 1) * 4));
+  TRY(dalloc(m, (void**)&m->P_dev, sizeof(DevParams)));
+  TRY(dalloc(m, (void**)&m->rowpos_dev, (size_t)R * 4));
+  TRY(dalloc(m, (void**)&m->tokens_dev, (size_t)R * 4));
+  TRY(dalloc(m, (void**)&m->argmax_dev, 4));
+  TRY(dalloc(m, (void**)&m->amax_key_dev, 8));
+  TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
+  TRY(dalloc(m, (void**)&m->chain_count, 4));
+  TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
+  LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
+  if (!fault_flag_ptr()) {
+    set_error("model_finalize: fault flag unavailable");
+    return LUMINA_E_CUDA;
+  }
+  TRY(dalloc(m, (void**)&m->src_dev, (size_t)R * 4));
+  if (cudaMallocHost(&m->P_host, sizeof(DevParams)) != cudaSuccess ||
+      cudaMallocHost(&m->rowpos_host, (size_t)R * 4) != cudaSuccess ||
+      cudaMallocHost(&m->tokens_host, (size_t)R * 4) != cudaSuccess ||
+      cudaMallocHost(&m->argmax_host, 4) != cudaSuccess ||
+      cudaMallocHost(&m->amax_key_host, 8) != cudaSuccess || cudaMallocHost(&m->fault_host, 4) != cudaSuccess ||
+      cudaMallocHost(&m->logits_host, (size_t)V * 4) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("model_finalize: pinned host allocation failed");
+    return LUMINA_E_OOM;
+  }
+  LUMINA_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  m->finalized = true;
+  return LUMINA_OK;
+}
+
+int lumina_model_free(lumina_model* m) {
+  if (!m) return LUMINA_OK;
+  Guard g(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+  if (m->chain_graph) cudaGraphExecDestroy(m->chain_graph);
+  if (m->comm) ncclCommDestroy(m->comm);
+  for (Layer& Ly : m->L) {
+    if (Ly.qkv) {
+      lumina_weight_free(Ly.qkv);
+    } else {
+      lumina_weight_free(Ly.q);
+      lumina_weight_free(Ly.k);
+      lumina_weight_free(Ly.v);
+    }
+    if (Ly.gu) {
+      lumina_weight_free(Ly.gu);
+    } else {
+      lumina_weight_free(Ly.gate);
+      lumina_weight_free(Ly.up);
+    }
+    lumina_weight_free(Ly.o);
+    lumina_weight_free(Ly.down);
+  }
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->P_host) cudaFreeHost(m->P_host);
+  if (m->rowpos_host) cudaFreeHost(m->rowpos_host);
+  if (m->tokens_host) cudaFreeHost(m->tokens_host);
+  if (m->argmax_host) cudaFreeHost(m->argmax_host);
+  if (m->amax_key_host) cudaFreeHost(m->amax_key_host);
+  if (m->fault_host) cudaFreeHost(m->fault_host);
+  if (m->logits_host) cudaFreeHost(m->logits_host);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+  return LUMINA_OK;
+}
+
+int lumina_nccl_unique_id(uint8_t* id128) {
+  LUMINA_CHECK_ARG(id128, "nccl_unique_id: null out");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) {
+    set_error("ncclGetUniqueId: %s", ncclGetErrorString(r));
+    return LUMINA_E_NCCL;
+  }
+  static_assert(sizeof(id.internal) == 128, "ncclUniqueId size");
+  memcpy(id128, id.internal, 128);
+  return LUMINA_OK;
+}
+
+int lumina_model_init_tp(lumina_model* m, const uint8_t* id128) {
+  LUMINA_CHECK_ARG(m && id128, "model_init_tp: null pointer");
+  if (m->c.tp_size <= 1) return LUMINA_OK;
+  Guard g(m->device);
+  ncclUniqueId id;
+  memcpy(id.internal, id128, 128);
+  ncclResult_t r = ncclCommInitRank(&m->comm, m->c.tp_size, id, m->c.tp_rank);
+  if (r != ncclSuccess) {
+    m->comm = nullptr;
+    set_error("ncclCommInitRank: %s", ncclGetErrorString(r));
+    return LUMINA_E_NCCL;
+  }
+  return LUMINA_OK;
+}
+
+int lumina_kv_length(const lumina_model* m, int layer, int* len) {
+  LUMINA_CHECK_ARG(m && len, "kv_length: null pointer");
+  if (layer < 0) return uniform_len(m, len);
+  LUMINA_CHECK_ARG(layer < m->c.n_layer, "kv_length: layer %d", layer);
+  *len = m->layer_len[layer];
+  return LUMINA_OK;
+}
+
+int lumina_kv_truncate(lumina_model* m, int len) {
+  TRY(check_ready(m));
+  int cur = 0;
+  for (int v : m->layer_len) cur = std::max(cur, v);
+  LUMINA_CHECK_ARG(len >= 0 && len <= cur, "kv_truncate: %d not in [0, %d]", len, cur);
+  for (auto& v : m->layer_len) v = std::min(v, len);
+  release_blocks(m, len);
+  return LUMINA_OK;
+}
+
+int lumina_kv_read(const lumina_model* mc, int layer, int start, int n, float* k_host, float* v_host) {
+  lumina_model* m = const_cast<lumina_model*>(mc);
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(k_host && v_host, "kv_read: null output");
+  LUMINA_CHECK_ARG(layer >= 0 && layer < m->c.n_layer, "kv_read: layer %d", layer);
+  LUMINA_CHECK_ARG(start >= 0 && n >= 0 && start + n <= m->layer_len[layer], "kv_read: rows [%d, %d) beyond %d", start,
+                   start + n, m->layer_len[layer]);
+  if (n == 0) return LUMINA_OK;
+  Guard g(m->device);
+  float* tmp = nullptr;
+  const size_t cnt = (size_t)n * m->nh * m->hd;
+  LUMINA_CUDA_TRY(cudaMallocAsync((void**)&tmp, cnt * 8, m->stream));
+  int rc = launch_kv_read(m->c.kv_fp16, layer_k(m, layer), layer_v(m, layer), m->bt_dev, m->c.block_size, m->nh,
+                          m->nkv, m->hd, start, n, tmp, tmp + cnt, m->stream);
+  if (!rc) {
+    cudaMemcpyAsync(k_host, tmp, cnt * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(v_host, tmp + cnt, cnt * 4, cudaMemcpyDeviceToHost, m->stream);
+  }
+  cudaFreeAsync(tmp, m->stream);
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return rc;
+}
+
+int lumina_kv_commit_rows(lumina_model* m, int base, const int* src_host, int n) {
+  TRY(check_ready(m));
+  int len = 0;
+  TRY(uniform_len(m, &len));
+  LUMINA_CHECK_ARG(n >= 0 && n <= m->c.max_rows && base >= 0 && base + n <= len, "kv_commit_rows: bad range");
+  LUMINA_CHECK_ARG(n == 0 || src_host, "kv_commit_rows: null src");
+  for (int i = 0; i < n; ++i)
+    LUMINA_CHECK_ARG(src_host[i] >= 0 && base + src_host[i] < len, "kv_commit_rows: src[%d]=%d out of range", i,
+                     src_host[i]);
+  Guard g(m->device);
+  if (n) {
+    for (int i = 0; i < n; ++i) m->tokens_host[i] = src_host[i];
+    LUMINA_CUDA_TRY(cudaMemcpyAsync(m->src_dev, m->tokens_host, n * 4, cudaMemcpyHostToDevice, m->stream));
+    for (int l = 0; l < m->c.n_layer; ++l)
+      TRY(launch_kv_gather(m->c.kv_fp16, layer_k(m, l), layer_v(m, l), m->bt_dev, m->c.block_size, m->nkv, m->hd, base,
+                           m->src_dev, n, m->kv_tmp, m->stream));
+    LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  }
+  for (auto& v : m->layer_len) v = base + n;
+  release_blocks(m, base + n);
+  return LUMINA_OK;
+}
+
+int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int pos0, const int* pos_override_host,
+                         const float* bias_host, void* stream) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(x_dev, "layer_forward: null x");
+  LUMINA_CHECK_ARG(layer >= 0 && layer < m->c.n_layer, "layer_forward: layer %d", layer);
+  LUMINA_CHECK_ARG(n >= 1 && n <= m->c.max_rows, "layer_forward: %d rows not in [1, %d]", n, m->c.max_rows);
+  LUMINA_CHECK_ARG(!bias_host || n <= m->bias_rows, "layer_forward: bias with %d rows > %d", n, m->bias_rows);
+  Guard g(m->device);
+  cudaStream_t user = (cudaStream_t)stream;
+  const int t_prev = m->layer_len[layer];
+  TRY(ensure_blocks(m, t_prev + n));
+  std::vector<int> pos(n);
+  for (int i = 0; i < n; ++i) pos[i] = pos_override_host ? pos_override_host[i] : pos0 + i;
+  for (int i = 0; i < n; ++i)
+    LUMINA_CHECK_ARG(pos[i] >= 0 && pos[i] <= m->c.max_seq, "layer_forward: position %d beyond RoPE table", pos[i]);
+  // order the model stream after the caller's work on x
+  cudaEvent_t ev;
+  LUMINA_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  cudaEventRecord(ev, user);
+  cudaStreamWaitEvent(m->stream, ev, 0);
+  TRY(upload_params(m, n, t_prev, pos.data(), nullptr, t_prev + n));
+  if (bias_host) {
+    LUMINA_CUDA_TRY(cudaMemcpy2DAsync(m->bias_dev, (size_t)(t_prev + n) * 4, bias_host, (size_t)(t_prev + n) * 4,
+                                      (size_t)(t_prev + n) * 4, n, cudaMemcpyHostToDevice, m->stream));
+  }
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->x, x_dev, (size_t)n * m->d * 4, cudaMemcpyDeviceToDevice, m->stream));
+  int rc = run_layer(m, layer, n, bias_host ? m->bias_dev : nullptr);
+  if (!rc) {
+    cudaMemcpyAsync(x_dev, m->x, (size_t)n * m->d * 4, cudaMemcpyDeviceToDevice, m->stream);
+    cudaEventRecord(ev, m->stream);
+    cudaStreamWaitEvent(user, ev, 0);
+    m->layer_len[layer] = t_prev + n;
+  }
+  // pinned params / host bias must outlive the copies that read them
+  cudaStreamSynchronize(m->stream);
+  cudaEventDestroy(ev);
+  return rc;
+}
+
+int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0, const int* pos_override_host,
+                   const float* bias_host, float* logits_host, int all_rows) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(tokens_host && n >= 1, "forward: no tokens");
+  Guard g(m->device);
+  return forward_rows(m, tokens_host, n, pos0, pos_override_host, bias_host, all_rows, logits_host);
+}
+
+int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argmax_host) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(token >= 0 && token < m->embed_rows, "decode_step: token %d out of range", token);
+  Guard g(m->device);
+  int len = 0;
+  TRY(uniform_len(m, &len));
+  TRY(ensure_blocks(m, len + 1));
+  DevParams& P = *m->P_host;
+  P.n = 1;
+  P.t_prev = len;
+  P.t_tot = len + 1;
+  P.n_splits = n_splits_for(1, len + 1, m->max_splits, m->split_rows);
+  P.bias_ld = 0;
+  m->rowpos_host[0] = len;
+  m->tokens_host[0] = token;
+  if (!m->step_graph) TRY(capture_step(m));
+  LUMINA_CUDA_TRY(cudaGraphLaunch(m->step_graph, m->stream));
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  for (auto& v : m->layer_len) v = len + 1;
+  if (*m->fault_host) {
+    set_error("decode_step: a device wait timed out (fault word %#x)", *m->fault_host);
+    return LUMINA_E_CUDA;
+  }
+  const int V = m->head_rows * m->c.tp_size;
+  if (logits_host) memcpy(logits_host, m->logits_host, (size_t)V * 4);
+  if (argmax_host)
+    *argmax_host = m->comm ? *m->argmax_host : (int)(0xFFFFFFFFu - (unsigned)(*m->amax_key_host & 0xFFFFFFFFull));
+  return LUMINA_OK;
+}
+
+int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(token >= 0 && token < m->embed_rows, "decode_greedy: token %d out of range", token);
+  LUMINA_CHECK_ARG(n >= 1 && tokens_host, "decode_greedy: bad n / output");
+  Guard g(m->device);
+  int len = 0;
+  TRY(uniform_len(m, &len));
+  TRY(ensure_blocks(m, len + n));
+  std::vector<int> pos(1, len);
+  TRY(upload_params(m, 1, len, pos.data(), &token, 0));
+  LUMINA_CUDA_TRY(cudaMemsetAsync(m->chain_count, 0, 4, m->stream));
+  LUMINA_CUDA_TRY(cudaMemsetAsync(fault_flag_ptr(), 0, 4, m->stream));
+  if (!m->chain_graph) TRY(capture_chain(m));
+  for (int i = 0; i < n; ++i) LUMINA_CUDA_TRY(cudaGraphLaunch(m->chain_graph, m->stream));
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(tokens_host, m->chain_tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->fault_host, fault_flag_ptr(), 4, cudaMemcpyDeviceToHost, m->stream));
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  for (auto& v : m->layer_len) v = len + n;
+  if (*m->fault_host) {
+    set_error("decode_greedy: a device wait timed out (fault word %#x)", *m->fault_host);
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* launches_per_token,
+                        double* bytes_per_token) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(iters >= 1 && ms_per_launch, "profile_gemv: bad arguments");
+  Guard g(m->device);
+  const int d = m->d, qw = m->nh * m->hd, width = qw + 2 * m->nkv * m->hd;
+  int launches = 0;
+  double bytes = 0.0;
+  // the decode token's packed GEMVs, epilogues that write only scratch
+  auto one_token = [&](bool count) -> int {
+    for (int l = 0; l < m->c.n_layer; ++l) {
+      Layer& Ly = m->L[l];
+      const lumina_weight* ws[4] = {Ly.qkv ? Ly.qkv : Ly.q, Ly.o, Ly.gu ? Ly.gu : Ly.gate, Ly.down};
+      const float* xs[4] = {m->x, m->attn, m->x, m->ffn_buf};
+      const float* norms[4] = {Ly.in_norm, nullptr, Ly.post_norm, nullptr};
+      float* ys[4] = {m->qkv_buf, m->part, m->ffn_buf, m->part};
+      const int epis[4] = {EPI_STORE, EPI_STORE, Ly.gu ? EPI_SWIGLU : EPI_STORE, EPI_STORE};
+      const int lds[4] = {width, d, m->ffn, d};
+      const int ldx[4] = {d, qw, d, m->ffn};
+      for (int i = 0; i < 4; ++i) {
+        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr));
+        if (count) {
+          ++launches;
+          const int out_rows = epis[i] == EPI_SWIGLU ? ws[i]->rows / 2 : ws[i]->rows;
+          bytes += (double)packed_bytes(ws[i]) + (double)ws[i]->cols * 4 + (double)out_rows * 4;
+        }
+      }
+    }
+    return LUMINA_OK;
+  };
+  // warm (attributes, first-use setup) outside the capture
+  TRY(one_token(true));
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  cudaGraph_t gr = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  LUMINA_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = LUMINA_OK;
+  for (int i = 0; i < iters && !rc; ++i) rc = one_token(false);
+  const cudaError_t ec = cudaStreamEndCapture(m->stream, &gr);
+  if (rc || ec != cudaSuccess) {
+    if (gr) cudaGraphDestroy(gr);
+    if (!rc) set_error("profile_gemv capture: %s", cudaGetErrorString(ec));
+    return rc ? rc : LUMINA_E_CUDA;
+  }
+  if (cudaGraphInstantiate(&ge, gr, 0) != cudaSuccess) {
+    cudaGraphDestroy(gr);
+    set_error("profile_gemv: instantiate failed");
+    return LUMINA_E_CUDA;
+  }
+  cudaGraphDestroy(gr);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaGraphLaunch(ge, m->stream);  // warm replay
+  cudaEventRecord(e0, m->stream);
+  cudaGraphLaunch(ge, m->stream);
+  cudaEventRecord(e1, m->stream);
+  const cudaError_t es = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaGraphExecDestroy(ge);
+  if (es != cudaSuccess) {
+    set_error("profile_gemv: %s", cudaGetErrorString(es));
+    return LUMINA_E_CUDA;
+  }
+  *ms_per_launch = ms / (float)(iters * launches);
+  if (launches_per_token) *launches_per_token = launches;
+  if (bytes_per_token) *bytes_per_token = bytes;
+  return LUMINA_OK;
+}
+
+}  // extern "C"

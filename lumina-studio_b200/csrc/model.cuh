@@ -1,0 +1,76 @@
+// Decode model internals shared by model.cu and model_kernels.cu.
+#pragma once
+#include "weights.cuh"
+
+namespace lumina {
+
+// Per-forward values the kernels read from device memory, so that one
+// captured CUDA graph serves every decode position.
+struct DevParams {
+  int n;         // rows in this forward
+  int t_prev;    // KV length before the append
+  int t_tot;     // t_prev + n
+  int n_splits;  // active attention splits
+  int bias_ld;   // columns of the bias matrix (= t_tot)
+  int pad[3];
+};
+
+template <typename KT>
+__device__ __forceinline__ KT to_kv(float v);
+template <>
+__device__ __forceinline__ float to_kv<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
+
+__device__ __forceinline__ float from_kv(float v) { return v; }
+__device__ __forceinline__ float from_kv(__half v) { return __half2float(v); }
+
+// DL consecutive KV elements -> fp32 (16-byte loads).
+template <typename KT, int DL>
+__device__ __forceinline__ void load_kv(const KT* p, float* out) {
+  if constexpr (sizeof(KT) == 2) {
+    static_assert(DL % 8 == 0, "fp16 KV slice must be a multiple of 8");
+#pragma unroll
+    for (int q = 0; q < DL / 8; ++q) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + q);
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        out[q * 8 + 2 * e] = f.x;
+        out[q * 8 + 2 * e + 1] = f.y;
+      }
+    }
+  } else {
+    static_assert(DL % 4 == 0, "fp32 KV slice must be a multiple of 4");
+#pragma unroll
+    for (int q = 0; q < DL / 4; ++q) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p) + q);
+      out[4 * q] = v.x;
+      out[4 * q + 1] = v.y;
+      out[4 * q + 2] = v.z;
+      out[4 * q + 3] = v.w;
+    }
+  }
+}
+
+int launch_embed(const __half* emb, int d, int vocab, const int* tokens, const DevParams* P, float* x, int max_n,
+                 unsigned long long* argmax_key, cudaStream_t s);
+int launch_rope_append(bool fp16, const float* qkv, int nh, int nkv, int hd, const float* cos_t, const float* sin_t,
+                       const int* row_pos, const DevParams* P, const int* bt, int bs, void* kc, void* vc,
+                       float* q_out, int max_n, cudaStream_t s);
+int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
+                     const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
+                     float* part_o, float* part_ml, int* counters, int max_n, int max_splits, cudaStream_t s);
+int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, int batch, float* y, int ldy,
+                      const float* resid, int ldr, cudaStream_t s, unsigned long long* amax = nullptr);
+int launch_gather_rows(const lumina_weight& out, const lumina_weight& s0, const lumina_weight& s1,
+                       const lumina_weight& s2, const int* sel, const int* srow, cudaStream_t s);
+int launch_swiglu(const float* g, const float* u, float* o, int n, int ffn, int ld, cudaStream_t s);
+int launch_argmax(const float* v, int n, int* out, cudaStream_t s);
+int launch_kv_read(bool fp16, const void* kc, const void* vc, const int* bt, int bs, int nh, int nkv, int hd,
+                   int start, int n, float* ko, float* vo, cudaStream_t s);
+int launch_kv_gather(bool fp16, void* kc, void* vc, const int* bt, int bs, int nkv, int hd, int base, const int* src,
+                     int n, void* tmp, cudaStream_t s);
+
+}  // namespace lumina

@@ -2,6 +2,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -123,6 +124,35 @@ static void linspace_levels(int bits, double* out) {
 
 __constant__ double c_levels[4][16];
 
+// bit 0: a bounded mbarrier wait in a GEMV gave up
+__device__ int g_fault_flag;
+
+int* fault_flag_ptr() {
+  static int* p[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!p[dev]) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_fault_flag) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    p[dev] = static_cast<int*>(a);
+  }
+  return p[dev];
+}
+
+int read_fault_flag(int* out) {
+  int* p = fault_flag_ptr();
+  if (!p) {
+    set_error("fault flag: symbol address unavailable");
+    return LUMINA_E_CUDA;
+  }
+  LUMINA_CUDA_TRY(cudaMemcpy(out, p, sizeof(int), cudaMemcpyDeviceToHost));
+  return LUMINA_OK;
+}
+
 static int ensure_levels() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -138,12 +168,16 @@ static int ensure_levels() {
 // ---------------------------------------------------------------------------
 // unpack / dequant gates (read the device layout back to one code per byte)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int device_code(const lumina_weight w, const uint8_t* codes, int r, int k) {
+__device__ __forceinline__ int device_code(const lumina_weight& w, int r, int k) {
+  if (w.mma) {
+    int nib = 0;
+    const size_t o = mma_code_byte(w, r, k, &nib);
+    return (w.codes[o] >> (4 * nib)) & 0xF;
+  }
   const int blk = k >> 5, j = k & 31;
   const int cbk = blocks_per_chunk(w.bits);
-  const int chunk = blk / cbk, cb = blk % cbk;
-  const uint8_t* row = codes + (size_t)r * w.row_bytes + (size_t)chunk * chunk_bytes(w.bits);
-  const uint32_t* bw = reinterpret_cast<const uint32_t*>(row) + cb * w.bits;
+  const uint8_t* chunk = w.codes + code_offset(w, r, blk / cbk);
+  const uint32_t* bw = reinterpret_cast<const uint32_t*>(chunk) + (blk % cbk) * w.bits;
   switch (w.bits) {
     case 4: return (bw[j >> 3] >> (4 * (j & 7))) & 0xF;
     case 2: return (bw[j >> 4] >> (2 * (j & 15))) & 0x3;
@@ -157,11 +191,16 @@ __device__ __forceinline__ int device_code(const lumina_weight w, const uint8_t*
   }
 }
 
+__device__ __forceinline__ float device_scale(const lumina_weight& w, int r, int g) {
+  const uint8_t* p = w.scales + (w.mma ? mma_scale_offset(w, r, g) : scale_offset(w, r, g));
+  return w.fp16_scales ? __half2float(*reinterpret_cast<const __half*>(p)) : *reinterpret_cast<const float*>(p);
+}
+
 __global__ void unpack_kernel(const lumina_weight w, uint8_t* out) {
   const size_t n = (size_t)w.rows * w.cols;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / w.cols), k = (int)(i % w.cols);
-    out[i] = (uint8_t)device_code(w, w.codes, r, k);
+    out[i] = (uint8_t)device_code(w, r, k);
   }
 }
 
@@ -169,10 +208,8 @@ __global__ void dequant_kernel(const lumina_weight w, float* out) {
   const size_t n = (size_t)w.rows * w.cols;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / w.cols), k = (int)(i % w.cols);
-    const int c = device_code(w, w.codes, r, k);
-    const size_t si = (size_t)r * w.n_groups + k / w.group;
-    const float s = w.fp16_scales ? __half2float(reinterpret_cast<const __half*>(w.scales)[si])
-                                  : reinterpret_cast<const float*>(w.scales)[si];
+    const int c = device_code(w, r, k);
+    const float s = device_scale(w, r, k / w.group);
     // adapters/lumina.py:138-139 (int) / :145-148 (binary, levels are -1/+1)
     out[i] = __double2float_rn(__dmul_rn((double)s, c_levels[w.bits - 1][c]));
   }
@@ -250,36 +287,42 @@ int lumina_weight_upload(int device, int kind, int group_size, int pack, const u
                      stride, cols);
 
   const int bits = kind;
-  const int nblk = (cols + 31) / 32;
-  const int cbk = blocks_per_chunk(bits);
-  const int n_chunks = (nblk + cbk - 1) / cbk;
-  const int row_bytes = n_chunks * chunk_bytes(bits);
-
-  // re-tile on the host: for int4/int2/binary the device row is the file row
-  // zero-padded to whole chunks; int3 is packed to 3 bits per code
-  std::vector<uint8_t> dev((size_t)rows * row_bytes, 0);
+  lumina_weight L{};
+  L.device = device;
+  L.bits = bits;
+  L.group = group_size;
+  L.rows = rows;
+  L.cols = cols;
+  L.rows_pad = (rows + ROW_PAD - 1) / ROW_PAD * ROW_PAD;
+  L.nblk = (cols + 31) / 32;
+  const int cbk = blocks_per_chunk(bits), chb = chunk_bytes(bits);
+  L.n_chunks = (L.nblk + cbk - 1) / cbk;
+  L.row_bytes = L.n_chunks * chb;
+  L.n_groups = n_groups;
+  // codes: each file row re-packed into device chunks (a plain copy for the
+  // kinds whose file layout is the device layout)
+  std::vector<uint8_t> dev((size_t)L.rows_pad * L.row_bytes, 0);
   const bool same_layout = (bits == 4 && pack == LUMINA_PACK_NIBBLE) ||
                            (bits == 2 && pack == LUMINA_PACK_2BIT) || bits == 1;
   for (int r = 0; r < rows; ++r) {
     const uint8_t* src = codes_host + (size_t)r * stride;
-    uint8_t* dst = dev.data() + (size_t)r * row_bytes;
+    uint8_t* dst = dev.data() + (size_t)r * L.row_bytes;
     if (same_layout) {
       const size_t nb = ((size_t)cols * bits + 7) / 8;
       memcpy(dst, src, nb);
-      // clear bits past the last column inside the final byte
-      const int tail = (cols * bits) % 8;
+      const int tail = (cols * bits) % 8;  // clear bits past the last column
       if (tail) dst[nb - 1] &= (uint8_t)((1u << tail) - 1);
       continue;
     }
     uint32_t* dw = reinterpret_cast<uint32_t*>(dst);
     for (int k = 0; k < cols; ++k) {
-      int c = file_code(kind, pack, src, k);
+      const int c = file_code(kind, pack, src, k);
       if (c > (1 << bits) - 1) {
         set_error("weight_upload: code %d out of range for int%d at (%d, %d)", c, bits, r, k);
         return LUMINA_E_ARG;
       }
       const int blk = k >> 5, j = k & 31;
-      uint32_t* bw = dw + (size_t)(blk / cbk) * (chunk_bytes(bits) / 4) + (blk % cbk) * bits;
+      uint32_t* bw = dw + (size_t)(blk / cbk) * (chb / 4) + (blk % cbk) * bits;
       switch (bits) {
         case 4: bw[j >> 3] |= (uint32_t)c << (4 * (j & 7)); break;
         case 2: bw[j >> 4] |= (uint32_t)c << (2 * (j & 15)); break;
@@ -292,43 +335,86 @@ int lumina_weight_upload(int device, int kind, int group_size, int pack, const u
       }
     }
   }
-  // scales: fp16 when lossless
+  // scales: fp16 when lossless; rows padded to 16 bytes
   bool fp16 = true;
-  std::vector<__half> hs(n_scales);
   for (size_t i = 0; i < n_scales; ++i) {
     const float s = scales_host[i];
     if (!std::isfinite(s)) {
       set_error("weight_upload: non-finite scale at %zu", i);
       return LUMINA_E_ARG;
     }
-    hs[i] = __float2half_rn(s);
-    if (__half2float(hs[i]) != s) fp16 = false;
+    if (__half2float(__float2half_rn(s)) != s) fp16 = false;
+  }
+  L.fp16_scales = fp16 ? 1 : 0;
+  const int es = fp16 ? 2 : 4;
+  L.spr = (n_groups * es + 15) / 16 * 16;
+  std::vector<uint8_t> sdev;
+  // int4 goes to the tensor-core fragment layout when LUMINA_INT4_LAYOUT=mma
+  // (gemv_mma.cu: ahead at batch >= 4, behind the CUDA-core path at batch 1)
+  const char* lay = getenv("LUMINA_INT4_LAYOUT");
+  const bool want_mma = lay && strcmp(lay, "mma") == 0;
+  if (bits == 4 && group_size % 64 == 0 && want_mma) {
+    // tensor-core fragment layout (gemv_mma.cu): built from the row-major codes
+    L.mma = 1;
+    const int nbp = (L.nblk + 1) / 2 * 2;
+    const int rows32 = (rows + 31) / 32 * 32;
+    std::vector<uint8_t> m((size_t)rows32 * nbp * 16, 0);
+    lumina_weight M = L;
+    M.n_chunks = nbp;
+    M.row_bytes = nbp * 16;
+    M.rows_pad = rows32;
+    for (int r = 0; r < rows; ++r) {
+      const uint8_t* src = dev.data() + (size_t)r * L.row_bytes;  // nibble row
+      for (int k = 0; k < cols; ++k) {
+        const int c = (src[k >> 1] >> (4 * (k & 1))) & 0xF;
+        int nib = 0;
+        const size_t o = mma_code_byte(M, r, k, &nib);
+        m[o] |= (uint8_t)(c << (4 * nib));
+      }
+    }
+    sdev.assign((size_t)rows32 * n_groups * es, 0);
+    for (int r = 0; r < rows; ++r)
+      for (int gi = 0; gi < n_groups; ++gi) {
+        const float s = scales_host[(size_t)r * n_groups + gi];
+        uint8_t* d = sdev.data() + mma_scale_offset(M, r, gi);
+        if (fp16) {
+          const __half h = __float2half_rn(s);
+          memcpy(d, &h, 2);
+        } else {
+          memcpy(d, &s, 4);
+        }
+      }
+    dev.swap(m);
+    L = M;
+  } else {
+    sdev.assign((size_t)L.rows_pad * L.spr, 0);
+    for (int r = 0; r < rows; ++r)
+      for (int gi = 0; gi < n_groups; ++gi) {
+        const float s = scales_host[(size_t)r * n_groups + gi];
+        uint8_t* d = sdev.data() + scale_offset(L, r, gi);
+        if (fp16) {
+          const __half h = __float2half_rn(s);
+          memcpy(d, &h, 2);
+        } else {
+          memcpy(d, &s, 4);
+        }
+      }
   }
 
   DeviceGuard g(device);
-  lumina_weight* w = new lumina_weight();
-  w->device = device;
-  w->bits = bits;
-  w->group = group_size;
-  w->rows = rows;
-  w->cols = cols;
-  w->nblk = nblk;
-  w->n_chunks = n_chunks;
-  w->row_bytes = row_bytes;
-  w->n_groups = n_groups;
-  w->fp16_scales = fp16 ? 1 : 0;
-  const size_t sbytes = n_scales * (fp16 ? 2 : 4);
-  w->bytes = dev.size() + sbytes;
-  if (cudaMalloc(&w->codes, dev.size()) != cudaSuccess || cudaMalloc(&w->scales, sbytes) != cudaSuccess) {
+  lumina_weight* w = new lumina_weight(L);
+  w->codes = nullptr;
+  w->scales = nullptr;
+  w->bytes = dev.size() + sdev.size();
+  if (cudaMalloc(&w->codes, dev.size()) != cudaSuccess || cudaMalloc(&w->scales, sdev.size()) != cudaSuccess) {
     cudaGetLastError();
     if (w->codes) cudaFree(w->codes);
     delete w;
-    set_error("weight_upload: cudaMalloc of %zu bytes failed", dev.size() + sbytes);
+    set_error("weight_upload: cudaMalloc of %zu bytes failed", dev.size() + sdev.size());
     return LUMINA_E_OOM;
   }
   cudaError_t e1 = cudaMemcpy(w->codes, dev.data(), dev.size(), cudaMemcpyHostToDevice);
-  cudaError_t e2 = fp16 ? cudaMemcpy(w->scales, hs.data(), sbytes, cudaMemcpyHostToDevice)
-                        : cudaMemcpy(w->scales, scales_host, sbytes, cudaMemcpyHostToDevice);
+  cudaError_t e2 = cudaMemcpy(w->scales, sdev.data(), sdev.size(), cudaMemcpyHostToDevice);
   if (e1 != cudaSuccess || e2 != cudaSuccess) {
     cudaFree(w->codes);
     cudaFree(w->scales);
@@ -386,11 +472,16 @@ int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx, 
   LUMINA_CHECK_ARG(ldx >= w->cols && ldy >= w->rows, "gemv: ldx %d / ldy %d smaller than (%d, %d)", ldx,
                    ldy, w->cols, w->rows);
   DeviceGuard g(w->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (w->mma) return gemv_mma_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);
+  if (batch <= 4) {
+    const int rc = gemv_fused_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);
+    if (rc != LUMINA_E_UNSUPPORTED) return rc;
+  }
   const int nblk_pad = w->n_chunks * blocks_per_chunk(w->bits);
   ActQ q;
   int rc = scratch_actq(w->device, batch, nblk_pad, &q);
   if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
   rc = act_quant(x_dev, ldx, batch, w->cols, nullptr, 0.f, w->bits, q, s);
   if (rc) return rc;
   return gemv_launch(w, q, batch, y_dev, ldy, EPI_STORE, nullptr, 0, s);

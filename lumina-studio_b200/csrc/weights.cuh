@@ -1,8 +1,7 @@
 // Device layout of packed Lumina weights and of quantized activations.
 //
-// Weights: row-major, each row padded to a whole number of 16-byte "chunks"
-// (48-byte chunks for int3). One 32-column "block" of a row is BITS 32-bit
-// words:
+// Codes of one row are cut into 16-byte "chunks" (48-byte for int3). A
+// 32-column "block" of codes is BITS 32-bit words:
 //   int4   4 words, byte j of a word = columns 2j (low nibble), 2j+1 (high)
 //          -- the file's nibble layout (adapters/lumina.py:20-27) unchanged
 //   int2   2 words, byte j = columns 4j..4j+3 in bits 0-1..6-7
@@ -13,27 +12,39 @@
 //          (columns 0-15, 16-31) and one plane of the high bits where bit t
 //          of byte j is column 4j+t and bit 4+t is column 16+4j+t
 //          -- re-packed from the file's byte-per-code layout (3 bits/code)
-// Scales: (rows, n_groups) fp16 when every F32 scale is exactly an fp16
-// value (then bit-identical), else fp32.
+// Rows are row-major, each padded to a whole number of chunks, and the row
+// count is padded to a multiple of 4 with zero rows. Scales are row-major
+// too, each row padded to a multiple of 16 bytes so that the scales of R
+// consecutive rows are one contiguous, bulk-copyable span. Scales are fp16
+// when every F32 scale is exactly an fp16 value (then bit-identical), else
+// fp32.
 //
 // Activations (int16, per 32-column block, in the order the dp2a code paths
 // consume): P8 for int4, P16 for int2/int3, P32 for binary.
 #pragma once
 #include "common.cuh"
 
+constexpr int ROW_PAD = 4;
+
 struct lumina_weight {
   int device;
-  int bits;         // 1, 2, 3, 4
-  int group;        // columns per scale (multiple of 32)
+  int bits;          // 1, 2, 3, 4
+  int group;         // columns per scale (a multiple of 32)
   int rows, cols;
-  int nblk;         // ceil(cols / 32)
-  int n_chunks;     // ceil(nblk / blocks_per_chunk)
-  int row_bytes;    // n_chunks * chunk_bytes
-  int n_groups;     // ceil(cols / group)
-  int fp16_scales;  // 1: half scales, 0: float scales
-  uint8_t* codes;   // rows * row_bytes
-  void* scales;     // rows * n_groups
-  size_t bytes;     // device bytes held
+  int rows_pad;      // rows rounded up to ROW_PAD
+  int nblk;          // ceil(cols / 32)
+  int n_chunks;      // chunks per row
+  int row_bytes;     // n_chunks * chunk bytes
+  int n_groups;      // ceil(cols / group)
+  int spr;           // scale bytes per row (16-byte multiple)
+  int fp16_scales;   // 1: half scales, 0: float scales
+  int mma;           // 1: int4 in the tensor-core fragment layout (gemv_mma.cu):
+                     //    rows_pad % 32 == 0, n_chunks = 32-column blocks
+                     //    rounded up to pairs, codes [tile16][pair][lane][16 B],
+                     //    scales [tile16][group][g][2]
+  uint8_t* codes;    // rows_pad * row_bytes
+  uint8_t* scales;   // rows_pad * spr
+  size_t bytes;      // device bytes held
 };
 
 namespace lumina {
@@ -50,7 +61,31 @@ __host__ __device__ inline int chunk_bytes(int bits) { return bits == 3 ? 48 : 1
 __host__ __device__ inline int blocks_per_chunk(int bits) { return bits == 3 ? 4 : 4 / bits; }
 inline int perm_kind(int bits) { return bits == 4 ? 8 : (bits == 1 ? 32 : 16); }
 
-// Quantized activation scratch for one GEMV input.
+// code of (row, col) in the tensor-core fragment layout
+__host__ __device__ inline size_t mma_code_byte(const lumina_weight& w, int row, int col, int* nibble) {
+  const int T = row >> 4, rr = row & 15, g = rr & 7;
+  const int b = col >> 5, cc = col & 31;
+  const int lane = g * 4 + ((cc & 15) >> 2);
+  const int j = (b & 1) * 2 + (cc >> 4);
+  *nibble = rr >> 3;
+  return (((size_t)T * (w.n_chunks / 2) + (b >> 1)) * 32 + lane) * 16 + j * 4 + (cc & 3);
+}
+__host__ __device__ inline size_t mma_scale_offset(const lumina_weight& w, int row, int grp) {
+  const int es = w.fp16_scales ? 2 : 4;
+  return ((((size_t)(row >> 4) * w.n_groups + grp) * 8 + (row & 7)) * 2 + ((row & 15) >> 3)) * es;
+}
+
+// byte offset of chunk `c` of row `row` (row-major layout)
+__host__ __device__ inline size_t code_offset(const lumina_weight& w, int row, int c) {
+  return (size_t)row * w.row_bytes + (size_t)c * chunk_bytes(w.bits);
+}
+
+// byte offset of the scale of (row, group g)
+__host__ __device__ inline size_t scale_offset(const lumina_weight& w, int row, int g) {
+  return (size_t)row * w.spr + (size_t)g * (w.fp16_scales ? 2 : 4);
+}
+
+// Quantized activation scratch for one GEMV input (global memory layout).
 struct ActQ {
   int16_t* xq;   // [batch][nblk_pad][32], permuted
   float* sx;     // [batch][nblk_pad]: amax / 32767
@@ -60,15 +95,31 @@ struct ActQ {
 
 // Activation quantization (optionally fused with RMSNorm). `x` rows have
 // stride ldx; `norm_w` may be null.
-int act_quant(const float* x, int ldx, int batch, int K, const float* norm_w, float eps,
-              int bits, const ActQ& q, cudaStream_t s);
+int act_quant(const float* x, int ldx, int batch, int K, const float* norm_w, float eps, int bits,
+              const ActQ& q, cudaStream_t s);
 
-enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ROPE_KV = 3 };
+
+// RoPE + paged KV append for the fused q/k/v projection (EPI_ROPE_KV). The
+// q and k rows of the weight are permuted so that rotation pairs (j,
+// j + hd/2) of a head are adjacent rows (2j', 2j'+1).
+struct RopeKV {
+  int nh, nkv, hd;
+  const float* cos_t;
+  const float* sin_t;
+  const int* row_pos;   // per batch row
+  const int* t_prev;    // device: KV length before this forward
+  const int* block_table;
+  int bs;
+  void* kcache;         // this layer's pool
+  void* vcache;
+  int kv_fp16;
+  float* q_out;         // (batch, nh*hd) rotated queries
+  int row_base;         // KV slot of batch row b is *t_prev + row_base + b
+};
 
 struct GemvArgs {
-  const uint8_t* codes;
-  const void* scales;
-  int rows, row_bytes, n_chunks, n_groups, group;
+  lumina_weight w;
   const int16_t* xq;
   const float* sx;
   const int* xsum;
@@ -77,12 +128,38 @@ struct GemvArgs {
   int ldy;
   const float* resid;
   int ldr;
+  RopeKV rk;
 };
 
+// Packed GEMV reading pre-quantized activations from global memory (any
+// batch; the path for prefill chunks).
 int gemv_launch(const lumina_weight* w, const ActQ& q, int batch, float* y, int ldy, int epi,
-                const float* resid, int ldr, cudaStream_t s);
+                const float* resid, int ldr, cudaStream_t s, const RopeKV* rk = nullptr);
+
+// Decode GEMV: 128-bit code loads software-pipelined in registers, scale
+// rows bulk-copied (TMA) into shared memory, activations quantized (and RMS-
+// normalized when norm_w is given) inside each CTA. batch 1, 2 or 4. Returns
+// LUMINA_E_UNSUPPORTED when the shape does not fit (callers then use
+// act_quant + gemv_launch).
+int gemv_fused_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
+                      float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s,
+                      const RopeKV* rk = nullptr);
+
+// int4 GEMV on the tensor pipe (weights in the fragment layout), any batch
+// in tiles of 8. LUMINA_E_UNSUPPORTED when the weight is not in that layout
+// or the shape does not fit.
+int gemv_mma_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
+                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s,
+                    const RopeKV* rk = nullptr);
 
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);
+// Bytes of, and carving of, one activation scratch region at `base`.
+size_t actq_scratch_bytes(int batch, int nblk_pad);
+void actq_carve(void* base, int batch, int nblk_pad, ActQ* out);
+
+// Device-side error word: bounded waits that give up set a bit here.
+int read_fault_flag(int* out);
+int* fault_flag_ptr();
 
 }  // namespace lumina

@@ -87,13 +87,15 @@ SIGNATURES = {
     "lumina_model_free": [_VP],
     "lumina_nccl_unique_id": [_U8P],
     "lumina_model_init_tp": [_VP, _U8P],
-    "lumina_kv_length": [_VP, _IP],
+    "lumina_kv_length": [_VP, _I, _IP],
     "lumina_kv_truncate": [_VP, _I],
     "lumina_kv_read": [_VP, _I, _I, _I, _FP, _FP],
     "lumina_kv_commit_rows": [_VP, _I, _IP, _I],
     "lumina_layer_forward": [_VP, _I, _VP, _I, _I, _IP, _FP, _VP],
-    "lumina_forward": [_VP, _IP, _I, _I, _FP, _I],
+    "lumina_forward": [_VP, _IP, _I, _I, _IP, _FP, _FP, _I],
     "lumina_decode_step": [_VP, _I, _FP, _IP],
+    "lumina_decode_greedy": [_VP, _I, _I, _IP],
+    "lumina_profile_gemv": [_VP, _I, _FP, _IP, ctypes.POINTER(ctypes.c_double)],
 }
 _RESTYPE = {"lumina_last_error": ctypes.c_char_p}
 
