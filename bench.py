@@ -1,0 +1,377 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the Lumina decode path on B200.
+
+Workload (the reference's headline decode configuration): a Llama-2-7B-shape
+decoder (32 layers, d_model 4096, 32 heads x 128, SwiGLU 11008, vocab 32000,
+RoPE theta 1e4), every projection Lumina int4 with groups of 64 and
+fp16-valued scales, embedding and lm_head raw; batch 1; a 512-token random
+prompt is prefilled, then greedy decode tokens follow with an fp16 KV cache
+paged in 16-token blocks. Weights are N(0, 0.02), seeded, quantized on the
+GPU with the reference's round-to-nearest + MSE scale search (synthetic: no
+checkpoint is involved).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+A step is one decode token. The timed region is K device-chained greedy
+steps (one CUDA-graph replay each, the argmax fed back on the device),
+bracketed by barriers and synchronizes and timed with CUDA events on the
+model's stream; the max over ranks is reported. With N > 1 (torchrun, one
+rank per GPU) the model is tensor-parallel over the N GPUs (NCCL all-reduce
+after o_proj and down_proj, vocab-sharded head): one sequence, fixed total
+work, so scaling is strong.
+
+Besides the device-chained loop the line carries
+  * e2e: the same K tokens through the public per-token call
+    (``CudaChatModel.decode_step`` + the host greedy sampler, as
+    ``generate`` runs them): host->device token/position parameters and the
+    device->host logits every step, wall clock;
+  * roofline: the packed-weight GEMV kernels (the dominant kernel) replayed
+    alone for one token's 128 launches, CUDA events on their stream;
+    algorithmic bytes (codes + scales + activations + outputs) / time
+    against the measured HBM copy bandwidth;
+  * cpu_baseline (N = 1): the reference's CPU decode path (the oracle's
+    numpy restatement of ChatModel._layer with fp32 weights converted once,
+    all BLAS threads) timed on a bounded sample of the same workload;
+  * clocks: nvidia-smi samples taken during the timed region.
+
+``--impl reference`` runs only that CPU path (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "lumina-studio_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "decode tokens/s and dequant-GEMV HBM GB/s (% peak), 7B int4, 1/2/4/8 B200"
+UNIT = "tokens/s"
+PROMPT = 512
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 2 ** 20
+# kv rows a 7B decode token reads per layer-row: k and v, 4096 fp16 each
+KV_BYTES_PER_ROW = 32 * 2 * 4096 * 2
+
+
+def workload(cfg, tp):
+    return {"workload": "llama2-7b-shape decoder, Lumina int4 g64 fp16 scales, batch 1, "
+                        "512-token random prompt prefill then greedy decode, fp16 KV paged in 16-token blocks",
+            "layers": cfg["num_hidden_layers"], "d_model": cfg["hidden_size"],
+            "heads": cfg["num_attention_heads"], "head_dim": cfg["hidden_size"] // cfg["num_attention_heads"],
+            "ffn": cfg["intermediate_size"], "vocab": cfg["vocab_size"], "batch": 1, "prompt": PROMPT,
+            "l2": "no flush: each token streams 3.7 GB of weights, > 126 MB L2",
+            "parallelism": f"tp{tp}"}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.path = gpu, None, None
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.5)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(self.NAMES, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# the reference's CPU decode path (oracle restatement), bounded sample
+# ---------------------------------------------------------------------------
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else (os.cpu_count() or 1)
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
+
+
+class CpuDecodeSample:
+    """ChatModel._layer decode steps (chat.py:232-304: fp32 weights converted
+    once, chat.py:223-230; numpy BLAS on every host core) over `n_layers` of
+    the 7B shape plus the 32000 x 4096 head GEMV (chat.py:322,388), the KV
+    cache starting at the 512 prompt rows. One token of the full model costs
+    32 / n_layers x the sampled layers + the head."""
+
+    def __init__(self, cfg, n_layers=4, seed=0):
+        from oracle.decode import OracleModel
+        from lumina_b200 import synthetic
+        self.full_layers = cfg["num_hidden_layers"]
+        self.n_layers = n_layers
+        scfg = dict(cfg, num_hidden_layers=n_layers)
+        rng = np.random.default_rng(seed)
+        one = {}  # one layer's values, reused under each sampled layer's names
+        t = {}
+        for name, shape in synthetic.tensor_order(scfg):
+            if len(shape) == 1:
+                t[name] = np.ones(shape, np.float16)
+                continue
+            key = name.split(".")[-2] if name.startswith("model.layers.") else name
+            if key not in one:
+                # std 0.02 (uniform): the CPU path's time does not depend on values
+                one[key] = ((rng.random(shape, dtype=np.float32) - 0.5) * 0.0693).astype(np.float16)
+            t[name] = one[key]
+        self.m = OracleModel(t, scfg, theta=1e4)
+        self.head_t = self.m.head_t()
+        self.emb = self.m.embed()
+        nh, hd = self.m.n_heads, self.m.hd
+        self.cache = {l: ((rng.random((PROMPT, nh, hd), dtype=np.float32) - 0.5),
+                          (rng.random((PROMPT, nh, hd), dtype=np.float32) - 0.5)) for l in range(n_layers)}
+        self.pos = PROMPT
+        self.tok = 1
+        self.buf = np.empty((1, self.head_t.shape[1]), np.float32)
+
+    def step(self) -> float:
+        """One decode token through the sampled layers + head; returns the
+        full-model seconds (layers scaled to 32)."""
+        t0 = time.perf_counter()
+        h = self.emb[[self.tok]]
+        for l in range(self.n_layers):
+            h = self.m.layer(h, l, self.cache, self.pos)
+        t1 = time.perf_counter()
+        np.dot(h[-1:], self.head_t, out=self.buf)
+        self.tok = int(np.argmax(self.buf[0].astype(np.float64)))
+        t2 = time.perf_counter()
+        self.pos += 1
+        return (t1 - t0) * self.full_layers / self.n_layers + (t2 - t1)
+
+    def describe(self, tokens):
+        return (f"{self.n_layers} of {self.full_layers} 7B-shape layers + the 32000x4096 head, "
+                f"{tokens} decode tokens from KV length {PROMPT}, layer time scaled x{self.full_layers // self.n_layers}; "
+                "numpy fp32 BLAS over weights converted once")
+
+
+def cpu_baseline(cfg, tokens=16, budget_s=20.0):
+    s = CpuDecodeSample(cfg)
+    s.step()  # converts the fp32 weights (outside the timing, as the reference caches them)
+    tot, n = 0.0, 0
+    t0 = time.perf_counter()
+    while n < tokens and time.perf_counter() - t0 < budget_s:
+        tot += s.step()
+        n += 1
+    return {"value": n / tot, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+            "sample": s.describe(n)}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    s = CpuDecodeSample(cfg)
+    for _ in range(max(1, args.warmup)):
+        s.step()
+    tot = 0.0
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tot += s.step()
+    wall = time.perf_counter() - t0
+    value = args.steps / tot
+    cb = {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port", "sample": s.describe(args.steps)}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random weights of the 7B shape)", "config": workload(cfg, 1),
+            "cpu_baseline": cb, "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0},
+            "sample_wall_s": wall}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# the B200 path
+# ---------------------------------------------------------------------------
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        try:
+            return float(json.load(open(p))["hbm_gbs"]), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_ratio():
+    """DRAM bytes / algorithmic bytes of the packed GEMV from the committed
+    ncu summary (profiles/gemv_fused_7b_int4_traffic.json), or None."""
+    p = os.path.join(REPO, "profiles", "gemv_fused_7b_int4_traffic.json")
+    try:
+        d = json.load(open(p))
+        return float(d["dram_bytes"]) / float(d["algorithmic_bytes"]), d.get("source", p)
+    except Exception:  # noqa: BLE001
+        return None, None
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (development only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    from lumina_b200 import synthetic
+    cfg = dict(synthetic.LLAMA7B)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from lumina_b200.engine import CudaChatModel, make_pick
+    max_seq = max(4608, PROMPT + max(args.warmup, args.steps) + 16)
+    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=local)
+    t0 = time.perf_counter()
+    model = CudaChatModel._from_records(recs, synthetic.hf_cfg(cfg), None, 32, 32, 1e-6, 1e4, local, True,
+                                        max_seq, 512, 16, rank, world)
+    build_s = time.perf_counter() - t0
+    model.init_tp()
+    try:
+        prompt = synthetic.prompt_ids(cfg, PROMPT, seed=0)
+        lg = model.forward(prompt, 0)[0]
+        first = int(np.argmax(lg.astype(np.float64)))
+        # warm-up: W chained steps (captures the step graph), then back to the prompt
+        model.decode_greedy(first, args.warmup)
+        model.kv_truncate(PROMPT)
+        clocks = ClockSampler(local)
+        barrier()
+        torch.cuda.synchronize()
+        clocks.start()
+        toks, dev_ms, kernels = model.decode_greedy(first, args.steps, timed=True)
+        torch.cuda.synchronize()
+        barrier()
+        clk = clocks.stop()
+        dev_ms = max_over_ranks(dev_ms)
+        value = args.steps / (dev_ms / 1e3)
+
+        # e2e: the public per-token call with host buffers, greedy host pick
+        model.kv_truncate(PROMPT)
+        pick = make_pick()
+        model.decode_step(first, want_logits=True)  # warm the per-token graph
+        model.kv_truncate(PROMPT)
+        barrier()
+        lg, tok, e2e_toks = None, first, []
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            lg, _ = model.decode_step(tok)
+            tok = pick(lg, e2e_toks)
+            e2e_toks.append(tok)
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+        # both loops decode the same greedy sequence
+        same = toks == e2e_toks
+        h2d = 32 + 4 + 4          # DevParams, row position, token
+        d2h = model.vocab * 4 + 4 + 8 + 4  # logits, argmax, argmax key, fault word
+
+        # roofline of the dominant kernel (packed GEMV), replayed alone
+        ms_launch, launches, alg_bytes = model.profile_gemv(4)
+        per_launch = alg_bytes / launches
+        achieved = per_launch / (ms_launch * 1e-3) / 1e9
+        peak, peak_kind = peaks()
+        ratio, tsrc = traffic_ratio()
+        kv_mean = PROMPT + args.steps / 2
+        tok_bytes = alg_bytes + model.vocab // world * 4096 * 2 + KV_BYTES_PER_ROW // world * kv_mean
+        cb = None
+        if world == 1 and not args.no_cpu_baseline:
+            model.close()
+            cb = cpu_baseline(cfg)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights x int16 activations, int32 dot, f32",
+                "data": "synthetic (seeded N(0,0.02) weights quantized to Lumina int4 g64; random prompt)",
+                "config": workload(cfg, world),
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_kind": peak_kind,
+                             "traffic": (ratio * per_launch) if ratio else None,
+                             "traffic_source": tsrc,
+                             "kernel": "gemv_fused (packed int4 dequant GEMV, 128 launches per token)",
+                             "algorithmic_bytes_per_launch": per_launch, "ms_per_launch": ms_launch},
+                "cpu_baseline": cb,
+                "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "api": "CudaChatModel.decode_step + host greedy pick",
+                        "same_tokens_as_chained": same},
+                "clocks": clk, "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
+                "token_hbm_bytes": tok_bytes, "token_hbm_frac": tok_bytes / (dev_ms / args.steps * 1e-3) / 1e9 / peak,
+                "model_build_s": build_s}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        model.close()
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

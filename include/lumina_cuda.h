@@ -183,15 +183,20 @@ int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argm
 /* n greedy decode steps with the argmax of each step fed to the next on
  * the device (no host round trip per token): the same per-token work as n
  * calls of lumina_decode_step with argmax sampling (chat.py:339, temperature
- * 0), generated tokens to tokens_host. The first step embeds `token`. */
-int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host);
+ * 0), generated tokens to tokens_host. The first step embeds `token`.
+ * Optional outputs (may be NULL): device_ms = CUDA-event time of the n
+ * steps on the model's stream; kernels_per_step = kernel launches in one
+ * step's graph. */
+int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, float* device_ms,
+                         int* kernels_per_step);
 
 /* Measurement: replay the packed-weight GEMVs of one decode token (every
  * layer's q/k/v, o, gate/up and down in decode order, on this model's
  * weights and buffers) `iters` times as one CUDA graph, timed with CUDA
  * events on the model's stream. Returns the mean duration of one GEMV
- * launch (ms), the launches per token, and the packed bytes (codes + scales)
- * those launches read per token. */
+ * launch (ms), the launches per token, and the algorithmic bytes of those
+ * launches per token (packed codes + scales read, fp32 activations read,
+ * fp32 outputs written). */
 int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* launches_per_token,
                         double* bytes_per_token);
 

@@ -73,6 +73,8 @@ struct lumina_model {
   cudaGraphExec_t chain_graph = nullptr;  // greedy steps with on-device token feedback
   int* chain_tokens = nullptr;            // [max_seq] generated tokens
   int* chain_count = nullptr;
+  int chain_kernels = 0;                  // kernel nodes in chain_graph
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int graph_splits = 0;
   bool finalized = false;
   ncclComm_t comm = nullptr;
@@ -596,6 +598,15 @@ int capture_chain(lumina_model* m) {
     set_error("capture: %s", cudaGetErrorString(e));
     return LUMINA_E_CUDA;
   }
+  size_t n_nodes = 0;
+  cudaGraphGetNodes(g, nullptr, &n_nodes);
+  std::vector<cudaGraphNode_t> nodes(n_nodes);
+  if (n_nodes) cudaGraphGetNodes(g, nodes.data(), &n_nodes);
+  m->chain_kernels = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++m->chain_kernels;
+  }
   const cudaError_t ei = cudaGraphInstantiate(&m->chain_graph, g, 0);
   cudaGraphDestroy(g);
   if (ei != cudaSuccess) {
@@ -836,6 +847,8 @@ int lumina_model_finalize(lumina_model* m) {
     set_error("model_finalize: pinned host allocation failed");
     return LUMINA_E_OOM;
   }
+  LUMINA_CUDA_TRY(cudaEventCreate(&m->ev0));
+  LUMINA_CUDA_TRY(cudaEventCreate(&m->ev1));
   LUMINA_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
   m->finalized = true;
   return LUMINA_OK;
@@ -847,6 +860,8 @@ int lumina_model_free(lumina_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
   if (m->chain_graph) cudaGraphExecDestroy(m->chain_graph);
+  if (m->ev0) cudaEventDestroy(m->ev0);
+  if (m->ev1) cudaEventDestroy(m->ev1);
   if (m->comm) ncclCommDestroy(m->comm);
   for (Layer& Ly : m->L) {
     if (Ly.qkv) {
@@ -1047,7 +1062,8 @@ int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argm
   return LUMINA_OK;
 }
 
-int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host) {
+int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, float* device_ms,
+                         int* kernels_per_step) {
   TRY(check_ready(m));
   LUMINA_CHECK_ARG(token >= 0 && token < m->embed_rows, "decode_greedy: token %d out of range", token);
   LUMINA_CHECK_ARG(n >= 1 && tokens_host, "decode_greedy: bad n / output");
@@ -1060,11 +1076,15 @@ int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host) {
   LUMINA_CUDA_TRY(cudaMemsetAsync(m->chain_count, 0, 4, m->stream));
   LUMINA_CUDA_TRY(cudaMemsetAsync(fault_flag_ptr(), 0, 4, m->stream));
   if (!m->chain_graph) TRY(capture_chain(m));
+  if (device_ms) LUMINA_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
   for (int i = 0; i < n; ++i) LUMINA_CUDA_TRY(cudaGraphLaunch(m->chain_graph, m->stream));
+  if (device_ms) LUMINA_CUDA_TRY(cudaEventRecord(m->ev1, m->stream));
   LUMINA_CUDA_TRY(cudaMemcpyAsync(tokens_host, m->chain_tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
   LUMINA_CUDA_TRY(cudaMemcpyAsync(m->fault_host, fault_flag_ptr(), 4, cudaMemcpyDeviceToHost, m->stream));
   LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
   for (auto& v : m->layer_len) v = len + n;
+  if (device_ms) LUMINA_CUDA_TRY(cudaEventElapsedTime(device_ms, m->ev0, m->ev1));
+  if (kernels_per_step) *kernels_per_step = m->chain_kernels;
   if (*m->fault_host) {
     set_error("decode_greedy: a device wait timed out (fault word %#x)", *m->fault_host);
     return LUMINA_E_CUDA;

@@ -94,7 +94,7 @@ SIGNATURES = {
     "lumina_layer_forward": [_VP, _I, _VP, _I, _I, _IP, _FP, _VP],
     "lumina_forward": [_VP, _IP, _I, _I, _IP, _FP, _FP, _I],
     "lumina_decode_step": [_VP, _I, _FP, _IP],
-    "lumina_decode_greedy": [_VP, _I, _I, _IP],
+    "lumina_decode_greedy": [_VP, _I, _I, _IP, _FP, _IP],
     "lumina_profile_gemv": [_VP, _I, _FP, _IP, ctypes.POINTER(ctypes.c_double)],
 }
 _RESTYPE = {"lumina_last_error": ctypes.c_char_p}

@@ -248,6 +248,22 @@ class CudaChatModel:
             raise
         return obj
 
+    def init_tp(self, group=None):
+        """Join this model's NCCL communicator: rank 0 of the torch.distributed
+        group makes the NCCL id, every rank receives it over the group and
+        joins (the library's all-reduces after o_proj / down_proj and the
+        logits all-gather use it). No-op when the model is not sharded."""
+        if self.tp_size <= 1:
+            return
+        import torch.distributed as dist
+        uid = (ctypes.c_uint8 * 128)()
+        if dist.get_rank(group) == 0:
+            check(self.lib.lumina_nccl_unique_id(uid), self.lib)
+        box = [bytes(uid)]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(box[0])
+        check(self.lib.lumina_model_init_tp(self.h, uid), self.lib)
+
     def close(self):
         if getattr(self, "h", None):
             self.lib.lumina_model_free(self.h)
@@ -327,14 +343,20 @@ class CudaChatModel:
                                           ctypes.byref(am)), self.lib)
         return (self._logits if want_logits else None), am.value
 
-    def decode_greedy(self, token: int, n: int) -> list:
+    def decode_greedy(self, token: int, n: int, timed: bool = False):
         """n greedy steps with the argmax fed back on the device: one graph
         replay per token and one host copy of the n tokens at the end. Token
         i+1 is the argmax of the logits after token i (the first one is
-        `token`); the KV grows by n rows."""
-        out = (ctypes.c_int * int(n))()
-        check(self.lib.lumina_decode_greedy(self.h, int(token), int(n), out), self.lib)
-        return list(out)
+        `token`); the KV grows by n rows. With ``timed`` also returns the
+        CUDA-event time of the n steps (ms) and the kernels per step."""
+        out = (ctypes.c_int * max(1, int(n)))()
+        ms = ctypes.c_float()
+        nk = ctypes.c_int()
+        check(self.lib.lumina_decode_greedy(self.h, int(token), int(n), out,
+                                            ctypes.byref(ms) if timed else None,
+                                            ctypes.byref(nk) if timed else None), self.lib)
+        toks = list(out)[:int(n)]
+        return (toks, ms.value, nk.value) if timed else toks
 
     def profile_gemv(self, iters: int = 4):
         """Device time of the decode token's packed GEMVs, replayed alone in a

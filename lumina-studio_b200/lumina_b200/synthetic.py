@@ -68,3 +68,88 @@ def hf_cfg(cfg: dict) -> dict:
     """The HF-style config dict the reference's ChatModel reads."""
     return {k: cfg[k] for k in ("num_hidden_layers", "hidden_size", "num_attention_heads",
                                 "num_key_value_heads", "vocab_size", "intermediate_size")}
+
+
+# ---------------------------------------------------------------------------
+# Full-size quantized workloads, generated on the GPU
+# ---------------------------------------------------------------------------
+_MULTIPLIERS = (1.0, 0.8, 0.65, 0.5, 0.4, 0.3, 0.2)  # ptq_ladder.py:235
+
+
+def _quantize_gpu(w, bits: int, group: int):
+    """Lumina round-to-nearest codes with the MSE scale search of
+    ptq_ladder.py:215-249 (seven absmax multipliers, first minimum wins) in
+    fp32 on the GPU, scales rounded to fp16 values. `w` is a (rows, cols)
+    float32 CUDA tensor with cols a multiple of `group`. Returns (codes
+    uint8 (rows, cols), scales float32 (rows, cols/group)). This makes
+    benchmark inputs: it is the reference's quantizer restated in torch,
+    not code under test."""
+    import torch
+    L = (1 << bits) - 1
+    rows, cols = w.shape
+    wg = w.view(rows, cols // group, group)
+    amax = wg.abs().amax(-1).clamp_min(1e-12)
+    best_e = best_s = None
+    for f in _MULTIPLIERS:
+        s = (amax * f).clamp_min(1e-12)
+        wn = wg / s[..., None]
+        c = torch.clamp(torch.round((wn + 1.0) * (L / 2.0)), 0, L)
+        e = ((wn - (c * (2.0 / L) - 1.0)) ** 2).mean(-1)
+        if best_e is None:
+            best_e, best_s = e, s
+        else:
+            take = e < best_e
+            best_e = torch.where(take, e, best_e)
+            best_s = torch.where(take, s, best_s)
+    s16 = best_s.half().float()
+    c = torch.clamp(torch.round((wg / s16[..., None] + 1.0) * (L / 2.0)), 0, L).to(torch.uint8)
+    return c.view(rows, cols), s16
+
+
+def _pack_gpu(c, bits: int):
+    """Codes (rows, cols) uint8 -> the file's packed bytes: int4 nibbles with
+    the even column in the low nibble (adapters/lumina.py:20-27), int2 four
+    per byte from bit 0 (adapters/lumina.py:30-40), int3 one byte per code."""
+    if bits == 4:
+        return c[:, 0::2] | (c[:, 1::2] << 4)
+    if bits == 2:
+        return c[:, 0::4] | (c[:, 1::4] << 2) | (c[:, 2::4] << 4) | (c[:, 3::4] << 6)
+    if bits == 3:
+        return c
+    raise ValueError(f"bits {bits}")
+
+
+class QuantizedRecords:
+    """Lazily generated records of a seeded random decoder (every 2-D matrix
+    N(0, 0.02), projections Lumina-quantized with fp16-valued group scales,
+    embedding and lm_head raw fp32, RMSNorm weights ones), as the mapping
+    ``CudaChatModel._from_records`` reads. Each tensor is drawn on the GPU
+    from its own seed (seed, index in ``tensor_order``) when first asked for
+    and is not kept, so a 7B model never sits on the host as a whole."""
+
+    def __init__(self, cfg: dict, bits: int = 4, group: int = 64, seed: int = 0, device: int = 0):
+        self.cfg, self.bits, self.group, self.seed, self.device = cfg, bits, group, seed, device
+        self.order = {n: (i, s) for i, (n, s) in enumerate(tensor_order(cfg))}
+
+    def __contains__(self, name):
+        return name in self.order
+
+    def get(self, name, default=None):
+        return self[name] if name in self.order else default
+
+    def __getitem__(self, name):
+        import torch
+        from .loader import Record
+        idx, shape = self.order[name]
+        if len(shape) == 1:
+            return Record(name, "raw", shape, data=np.ones(shape, np.float32))
+        g = torch.Generator(device=f"cuda:{self.device}")
+        g.manual_seed(self.seed * 100003 + idx)
+        w = torch.randn(shape, generator=g, device=f"cuda:{self.device}", dtype=torch.float32) * 0.02
+        if "embed" in name or "lm_head" in name:
+            return Record(name, "raw", shape, data=w.cpu().numpy())
+        c, s = _quantize_gpu(w, self.bits, self.group)
+        packed = _pack_gpu(c, self.bits).contiguous().cpu().numpy().reshape(-1)
+        pack = {4: "nibble", 2: "2bit", 3: "none"}[self.bits]
+        return Record(name, f"int{self.bits}", shape, group=self.group, pack=pack, codes=packed,
+                      scales=s.cpu().numpy())

@@ -100,6 +100,7 @@ class OracleModel:
         self.n_kv = int(cfg.get("num_key_value_heads", self.n_heads))
         self.n_layer = int(cfg.get("num_hidden_layers", 24))
         self.eps, self.theta = eps, theta
+        self._wcache = {}
         self.hd = self.t["model.embed_tokens.weight"].shape[1] // self.n_heads
         head = self.t.get("lm_head.weight")
         self.head = self.t["model.embed_tokens.weight"] if head is None else head
@@ -113,7 +114,11 @@ class OracleModel:
                                  "top_k": int(mm["top_k"])}
 
     def W(self, name):
-        return self.t[name].T.astype(np.float32)
+        """fp32 transposed weight, converted once and kept (chat.py:223-230)."""
+        w = self._wcache.get(name)
+        if w is None:
+            w = self._wcache[name] = self.t[name].T.astype(np.float32)
+        return w
 
     def layer(self, x, lyr, cache, pos0, attn_bias=None, pos_override=None):
         t, hd, nh, nk, W = self.t, self.hd, self.n_heads, self.n_kv, self.W
