@@ -89,6 +89,24 @@ int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx,
 /* Same contraction with host buffers; copies in, runs, copies out, syncs. */
 int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, float* y_host);
 
+/* lumina_gemv for callers that cannot allocate device memory (a runtime that
+ * owns every allocation through its own pool, or one that must not trigger
+ * the device-wide synchronisation of a cudaFree). It has no counterpart in
+ * the reference. Same arguments and the same arithmetic as lumina_gemv (the
+ * batched path: activation quantization, then the packed GEMV); it makes no
+ * cudaMalloc or cudaFree call of any kind. Its activation scratch is a fixed
+ * 1 MiB array in the library's device image (LUMINA_NOALLOC_SCRATCH_BYTES),
+ * held on every GPU that loads the library until the process exits; calls
+ * whose batch x padded columns need more (batch * ceil(cols/32) * 72 bytes,
+ * roughly) fail with LUMINA_E_ARG. The first call on each device looks up
+ * the array's device address and keeps it, so make that first call outside
+ * any stream capture. All calls share the one array: two calls that overlap
+ * on the GPU (different streams, no ordering between them) race on it and
+ * produce wrong results. Weights in the tensor-core fragment layout are not
+ * supported (LUMINA_E_UNSUPPORTED). */
+int lumina_gemv_noalloc(const lumina_weight* w, const float* x_dev, int batch, int ldx,
+                        float* y_dev, int ldy, void* stream);
+
 /* ---- int8 fused GEMV family (TOPS semantics, MoE-runtime path) -------- */
 /* Host-pointer entries with the exact argument meaning of the TOPS C ABI
  * (caller owns every buffer, row-major (N, K) weights). */

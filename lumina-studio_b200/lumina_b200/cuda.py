@@ -76,6 +76,7 @@ SIGNATURES = {
     "lumina_weight_dequant": [_VP, _VP, _VP],
     "lumina_gemv": [_VP, _VP, _I, _I, _VP, _I, _VP],
     "lumina_gemv_host": [_VP, _FP, _I, _FP],
+    "lumina_gemv_noalloc": [_VP, _VP, _I, _I, _VP, _I, _VP],
     "lumina_gemv_int8": [_I8P, _FP, _I8P, _FP, _FP, _I, _I],
     "lumina_gemv_q4_0": [_I8P, _FP, _U8P, _FP, _FP, _I, _I],
     "lumina_gemv_fp16": [_VP, _VP, _FP, _I, _I],
@@ -242,6 +243,12 @@ class Weight:
 
     def gemv(self, x_dev: int, batch: int, ldx: int, y_dev: int, ldy: int, stream: int = 0):
         check(bound_lib().lumina_gemv(self.handle, x_dev, int(batch), int(ldx), y_dev, int(ldy), stream))
+
+    def gemv_noalloc(self, x_dev: int, batch: int, ldx: int, y_dev: int, ldy: int, stream: int = 0):
+        """``gemv`` without any device allocation: the activation scratch is
+        the library's fixed 1 MiB device array (for callers that cannot
+        allocate; calls that overlap on the GPU race on that array)."""
+        check(bound_lib().lumina_gemv_noalloc(self.handle, x_dev, int(batch), int(ldx), y_dev, int(ldy), stream))
 
     def gemv_host(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
