@@ -1,0 +1,108 @@
+"""Tensor-parallel shard rules and the exchange step, on the CPU.
+
+Two gloo ranks (world size 2, 127.0.0.1) each take their shard of the tiny
+int4 model's projections with ``sharding.shard_record`` and dequantize it
+with the oracle. Column-parallel shards (q/k/v by heads, gate/up by
+group-aligned FFN rows, lm_head by vocab) concatenate to the full output;
+row-parallel shards (o_proj, down by group-aligned K ranges) give partial
+products whose all-reduce (sum, the same step the library runs through
+NCCL after o_proj and down_proj) equals the full product. Uneven splits
+(FFN 688 = 10.75 groups of 64) are covered, and at TP 8 the 7B FFN split
+(172 groups) is checked for group alignment and coverage.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from oracle import lumina_format as lf
+from lumina_b200 import sharding
+from lumina_b200.loader import LuminaFile
+
+HD = 64
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _deq(rec):
+    if rec.kind == "binary":
+        codes = rec.codes.reshape(rec.shape[0], -1)
+    else:
+        codes = lf.unpack_codes(rec.codes, rec.shape, rec.pack)
+    return lf.dequant(rec.kind, codes, rec.scales, rec.group, rec.shape[1])
+
+
+def _worker(rank, world, port, path, out):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        f = LuminaFile(path)
+        rng = np.random.default_rng(0)
+        x = rng.standard_normal((2, 688)).astype(np.float32)
+        h = rng.standard_normal((2, 256)).astype(np.float32)
+        res = {}
+        p = "model.layers.1."
+        for nm, inp in (("self_attn.o_proj.weight", h), ("mlp.down_proj.weight", x)):
+            rec = f.record(p + nm)
+            sh = sharding.shard_record(rec, nm, rank, world, HD)
+            c0 = (rank * rec.shape[1] // world) if "o_proj" in nm else \
+                sharding.ffn_bounds(rec.shape[1], rec.group, rank, world)[0]
+            part = torch.from_numpy(inp[:, c0:c0 + sh.shape[1]] @ _deq(sh).T)
+            dist.all_reduce(part)  # the row-parallel exchange step
+            res[nm] = part.numpy()
+        for nm in ("self_attn.q_proj.weight", "mlp.gate_proj.weight"):
+            sh = sharding.shard_record(f.record(p + nm), nm, rank, world, HD)
+            y = torch.from_numpy(h @ _deq(sh).T)
+            parts = [None] * world
+            dist.all_gather_object(parts, y.numpy())
+            res[nm] = np.concatenate(parts, axis=1)
+        head = f.record("lm_head.weight").data
+        parts = [None] * world
+        dist.all_gather_object(parts, h @ sharding.vocab_shard(head, rank, world).T)
+        res["lm_head.weight"] = np.concatenate(parts, axis=1)
+        if rank == 0:
+            np.savez(out, **res)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_shards_reassemble_full_products(tiny_file, tmp_path):
+    out = str(tmp_path / "tp.npz")
+    mp.start_processes(_worker, args=(2, _free_port(), tiny_file, out), nprocs=2, start_method="spawn")
+    got = np.load(out)
+    full = lf.load_dequant(tiny_file)
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((2, 688)).astype(np.float32)
+    h = rng.standard_normal((2, 256)).astype(np.float32)
+    p = "model.layers.1."
+    np.testing.assert_allclose(got["self_attn.o_proj.weight"], h @ full[p + "self_attn.o_proj.weight"].T,
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(got["mlp.down_proj.weight"], x @ full[p + "mlp.down_proj.weight"].T,
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(got["self_attn.q_proj.weight"], h @ full[p + "self_attn.q_proj.weight"].T,
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(got["mlp.gate_proj.weight"], h @ full[p + "mlp.gate_proj.weight"].T,
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(got["lm_head.weight"], h @ full["lm_head.weight"].T, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("ffn,group,tp", [(11008, 64, 8), (11008, 64, 4), (11008, 128, 2), (688, 64, 2),
+                                          (11008, 128, 8)])
+def test_ffn_bounds_cover_group_aligned(ffn, group, tp):
+    b = [sharding.ffn_bounds(ffn, group, r, tp) for r in range(tp)]
+    assert b[0][0] == 0 and b[-1][1] == ffn
+    for (a0, a1), (c0, _) in zip(b, b[1:]):
+        assert a1 == c0 and a0 % group == 0 and c0 % group == 0
+    sizes = [e - s for s, e in b]
+    # one whole group apart at most (plus the short last group)
+    assert max(sizes) - min(sizes) <= group + (-ffn % group)
