@@ -83,7 +83,9 @@ int lumina_weight_dequant(const lumina_weight* w, float* out_dev, void* stream);
 /* y[b, n] = sum_k x[b, k] * W[n, k] for b < batch (1..16): the fused dequant
  * GEMV that replaces `h @ W(name)` in ChatModel._layer (chat.py:239-243,282,
  * 300-303; W = dequantized Lumina weight). x rows have stride ldx floats, y
- * rows stride ldy floats. Uses the library's per-device activation scratch. */
+ * rows stride ldy floats. Uses the library's per-device activation scratch
+ * for batches the fused kernels do not take (calls that overlap on the GPU on
+ * one device race on it). */
 int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx,
                 float* y_dev, int ldy, void* stream);
 /* Same contraction with host buffers; copies in, runs, copies out, syncs. */

@@ -97,7 +97,7 @@ gemv_mma_kernel(MmaArgs a) {
   const int p0 = ks * np / MKS, p1 = (ks + 1) * np / MKS;
   const int nsteps = max(1, (p1 - p0 + MU - 1) / MU);
 
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   uint4* xb = reinterpret_cast<uint4*>(smem);                      // [nbp][NB][4 t]
   float* sxs = reinterpret_cast<float*>(xb + (size_t)nbp * NB * 4);  // [nbp][NB]
   int* xss = reinterpret_cast<int*>(sxs + (size_t)nbp * NB);        // [nbp][NB]

@@ -1,0 +1,545 @@
+// Decode GEMV for int4 weights on the tensor pipe (batch 1, 2 or 4).
+//
+// Arithmetic. The activation row is quantized per 64-column pair (one
+// scale group when group = 64): q = rint(x * fp32(32639/amax)), clamped to
+// +-32639, so that q = 256*qh + ql with qh = (q + 128) >> 8 and ql both
+// signed bytes. One mma.sync.m16n8k32 (u8 codes x s8) then takes the high
+// and the low bytes of a batch row as two B columns (2b, 2b+1), and a second
+// one accumulates the pair's other 32 columns, so for a 16-row tile the C
+// fragment holds Dh = sum c*qh and Dl = sum c*ql over the 64 columns, exact.
+// Per row and pair: T = 2*(256*Dh + Dl) - 15*sum(q), y += T * sx * s, and
+// y /= 15 at the end (adapters/lumina.py:135-139: level = (2c - 15) / 15).
+// The A operand takes the code bytes straight from the fragment layout
+// (weights.cuh, mma = 1): low nibbles = the tile's rows 0..7, high nibbles =
+// rows 8..15 times 16; that factor 16 is folded exactly into the fp32 scale.
+// C lane (g, t) holds rows g and g+8 of batch row t, so an epilogue lane
+// never needs another lane's value. B columns beyond the batch (lanes with
+// g >= 2*NB) read any valid column: they only feed C columns that are never
+// used, so every lane walks the tables with the same compile-time stride.
+//
+// Work split. Each CTA owns whole 16-row tiles (an equal share, with as few
+// CTAs as that share allows), so no partial sum ever leaves the SM. A unit
+// is (tile, KS pairs), KS a compile-time 8, 6 or 4 so the unrolled pair loop
+// addresses shared memory with immediate offsets; a CTA's units in
+// tile-major order are cut into equal runs, one per warp. A warp streams its
+// units through a ring of TS shared-memory stages that one lane fills with
+// cp.async.bulk (the codes and the scales of a unit are two contiguous
+// spans; completion on an mbarrier per stage); the first stages are
+// requested before griddepcontrol.wait. A tile split between warps is
+// summed in shared memory: each warp stores its partial and adds its unit
+// count to the tile's counter, and the warp that completes the count adds
+// the partials in unit order (so the result does not depend on which warp
+// finishes last) and applies the epilogue.
+#include "gemv_impl.cuh"
+
+namespace lumina {
+
+namespace {
+
+constexpr int TW = 16;          // warps per CTA
+constexpr int TW_SHIFT = 4;     // log2(TW)
+constexpr int TS = 3;           // ring stages per warp
+constexpr int TC_QMAX = 32639;  // 256 * 127 + 127
+
+__device__ __forceinline__ void mma_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  const int z = 0;
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+}
+__device__ __forceinline__ void mma_acc(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct TcArgs {
+  const uint8_t* codes;
+  const uint8_t* scales;
+  int rows, cols;
+  int P;        // 64-column pairs per row (codes padded to whole pairs)
+  int ng;       // scale groups per row
+  int gsh;      // log2(group / 64); KS is a multiple of 2^gsh
+  int T16;      // 16-row tiles
+  int UT;       // units per tile
+  int MT;       // most tiles of one CTA
+  int stage_bytes;
+  int x_bytes;  // shared bytes before the rings
+  const float* x;
+  int ldx;
+  const float* norm_w;
+  float eps;
+  float* y;
+  int ldy;
+  const float* resid;
+  int ldr;
+  RopeKV rk;
+  int nb;       // live batch rows (<= NB)
+  int* fault;
+};
+
+template <typename ST>
+__device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, float& s1) {
+  if constexpr (sizeof(ST) == 2) {
+    const __half2 h = *reinterpret_cast<const __half2*>(p);
+    s0 = __low2float(h);
+    s1 = __high2float(h);
+  } else {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    s0 = f.x;
+    s1 = f.y;
+  }
+}
+
+// Epilogue of one finished 16-row tile for batch row t (lane t of each row
+// group g): v0 = row g, v1 = row g + 8, already / 15. Paired epilogues (rows
+// 2i, 2i+1) take the odd row from the neighbouring row group's lane.
+template <int NB, int EPI>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0, float v1, int lane,
+                                            const int* kv_blk, const int* kv_off, const int* kv_pos) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool live = t < NB && t < a.nb;
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
+    if (!live) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = row0 + g + 8 * h;
+      if (row < a.rows) {
+        float v = h ? v1 : v0;
+        if constexpr (EPI == EPI_RESID) v = a.resid[(size_t)t * a.ldr + row] + v;
+        a.y[(size_t)t * a.ldy + row] = v;
+      }
+    }
+  } else {
+    // row 2i lives in row group g = 2i (mod 8), row 2i+1 in g + 1: even-g
+    // lanes take the odd row's value from lane + 4
+    const float n0 = __shfl_down_sync(0xffffffffu, v0, 4), n1 = __shfl_down_sync(0xffffffffu, v1, 4);
+    if (!live || (g & 1)) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = row0 + g + 8 * h;  // even
+      if (row + 1 >= a.rows) continue;
+      const float x1 = h ? v1 : v0, x2 = h ? n1 : n0;
+      if constexpr (EPI == EPI_SWIGLU) {
+        // rows 2i = gate_i, 2i+1 = up_i (chat.py:300-302, the +-40 clip)
+        const float e = expf(-fminf(fmaxf(x1, -40.f), 40.f));
+        a.y[(size_t)t * a.ldy + (row >> 1)] = x1 / (1.0f + e) * x2;
+      } else {
+        // fused q/k/v rows: [q heads (RoPE pairs adjacent)][k heads (pairs adjacent)][v]
+        const RopeKV& k = a.rk;
+        const int qrows = k.nh * k.hd, krows = k.nkv * k.hd, half = k.hd / 2;
+        const size_t blk = kv_blk[t], off = kv_off[t];
+        if (row < qrows + krows) {
+          const bool isq = row < qrows;
+          const int rr = isq ? row : row - qrows;
+          const int hh = rr / k.hd, p = (rr % k.hd) >> 1;
+          const int pos = kv_pos[t];
+          const float c = k.cos_t[(size_t)pos * half + p], s = k.sin_t[(size_t)pos * half + p];
+          // rotate-half RoPE, fp32 products rounded separately (chat.py:99-100)
+          const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+          const float o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+          if (isq) {
+            float* q = k.q_out + (size_t)t * qrows + (size_t)hh * k.hd;
+            q[p] = o1;
+            q[p + half] = o2;
+          } else {
+            const size_t base = ((blk * k.nkv + hh) * k.bs + off) * k.hd;
+            if (k.kv_fp16) {
+              __half* kc = static_cast<__half*>(k.kcache) + base;
+              kc[p] = __float2half_rn(o1);
+              kc[p + half] = __float2half_rn(o2);
+            } else {
+              float* kc = static_cast<float*>(k.kcache) + base;
+              kc[p] = o1;
+              kc[p + half] = o2;
+            }
+          }
+        } else {
+          const float vv[2] = {x1, x2};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int rr = row + e - qrows - krows;
+            const size_t idx = ((blk * k.nkv + rr / k.hd) * k.bs + off) * k.hd + rr % k.hd;
+            if (k.kv_fp16) static_cast<__half*>(k.vcache)[idx] = __float2half_rn(vv[e]);
+            else static_cast<float*>(k.vcache)[idx] = vv[e];
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int NB, typename ST, int EPI, bool NORM, int KS>
+__global__ void __launch_bounds__(TW * 32, 1)
+gemv_tc_kernel(TcArgs a) {
+  constexpr int ES = sizeof(ST);
+  constexpr int NC = 2 * NB;   // B columns: (high, low) bytes per batch row
+  constexpr int SG = 16 * ES;  // scale bytes of one group of a tile: 8 x (row g, row g+8)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int P = a.P;
+
+  // this CTA's tiles and units, this warp's run
+  const int G = gridDim.x;
+  const int ctile0 = (blockIdx.x * a.T16) / G, ctile1 = ((blockIdx.x + 1) * a.T16) / G;
+  const int cu0 = ctile0 * a.UT, cu1 = ctile1 * a.UT;
+  const int nU = cu1 - cu0;
+  const int wu0 = cu0 + ((warp * nU) >> TW_SHIFT), wu1 = cu0 + (((warp + 1) * nU) >> TW_SHIFT);
+  const int n_mine = wu1 - wu0;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  // [B fragments: P x NC x 4 lanes x 16 B][(sx, -15*sum q): P x NB x 8 B]
+  // [rinv: NB floats, 16 B][tile counters: MT ints][partials: TW x 2 x 16 x NB floats]
+  // [rings: TW x TS x stage_bytes][mbarriers: TW x TS]
+  uint4* xb = reinterpret_cast<uint4*>(smem);
+  int2* fq = reinterpret_cast<int2*>(xb + (size_t)P * NC * 4);
+  float* rinv_s = reinterpret_cast<float*>(fq + (size_t)P * NB);
+  int* cnt_s = reinterpret_cast<int*>(rinv_s + 4);
+  float* part_s = reinterpret_cast<float*>(cnt_s + a.MT);
+  uint8_t* ring = smem + a.x_bytes + (size_t)warp * TS * a.stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.x_bytes + (size_t)TW * TS * a.stage_bytes) + warp * TS;
+  __shared__ float red[TW];
+  __shared__ int ep_blk[NB], ep_off[NB], ep_pos[NB];
+
+  auto unit_span = [&](int u, int& tile, int& p0, int& np) {
+    tile = u / a.UT;
+    p0 = (u - tile * a.UT) * KS;
+    np = min(P - p0, KS);
+  };
+  // lane 0: unit j of this warp's run into stage j % TS (two bulk copies
+  // completing on the stage's mbarrier)
+  auto issue = [&](int j) {
+    int tile, p0, np;
+    unit_span(wu0 + j, tile, p0, np);
+    const int G0 = p0 >> a.gsh, G1 = ((p0 + np - 1) >> a.gsh) + 1;
+    uint8_t* st = ring + (size_t)(j % TS) * a.stage_bytes;
+    const uint32_t cb = (uint32_t)np * 512u, sb = (uint32_t)(G1 - G0) * SG;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(&bars[j % TS], cb + sb);
+    bulk_g2s(st, a.codes + ((size_t)tile * P + p0) * 512, cb, &bars[j % TS]);
+    bulk_g2s(st + KS * 512, a.scales + ((size_t)tile * a.ng + G0) * SG, sb, &bars[j % TS]);
+  };
+
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < TS; ++i) mbar_init(&bars[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  // 1) weights never depend on the previous kernel: the first stages go out
+  //    before the dependency wait
+  if (lane == 0)
+    for (int j = 0; j < min(TS, n_mine); ++j) issue(j);
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // 2) activation rows -> B fragments in shared memory
+  for (int i = threadIdx.x; i < a.MT; i += blockDim.x) cnt_s[i] = 0;
+  if constexpr (EPI == EPI_ROPE_KV) {
+    if (threadIdx.x < NB && threadIdx.x < a.nb) {
+      const int tt = *a.rk.t_prev + a.rk.row_base + threadIdx.x;
+      ep_blk[threadIdx.x] = a.rk.block_table[tt / a.rk.bs];
+      ep_off[threadIdx.x] = tt % a.rk.bs;
+      ep_pos[threadIdx.x] = a.rk.row_pos[threadIdx.x];
+    }
+  }
+  if constexpr (NORM) {
+    // chat.py:63-66: x / sqrt(mean(x^2) + eps) * w (fp32), one factor per row
+    for (int b = 0; b < NB; ++b) {
+      float ss = 0.f;
+      if (b < a.nb)
+        for (int k = threadIdx.x; k < a.cols; k += blockDim.x) {
+          const float v = a.x[(size_t)b * a.ldx + k];
+          ss = fmaf(v, v, ss);
+        }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int i = 0; i < TW; ++i) tot += red[i];
+        rinv_s[b] = 1.0f / sqrtf(tot / (float)a.cols + a.eps);
+      }
+      __syncthreads();
+    }
+  }
+  const bool vec_ok = ((a.ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+  // four threads per (batch row, pair), 16 columns each; every lane runs
+  // every pass (the shuffles below take the full warp)
+  for (int i0 = 0; i0 < NB * P * 4; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    const bool item = i < NB * P * 4;
+    const int b = item ? i / (P * 4) : 0, p = item ? (i >> 2) % P : 0, qd = i & 3;
+    const bool live = item && b < a.nb;
+    const float* xr = a.x + (size_t)b * a.ldx;
+    const int k0 = p * 64 + 16 * qd;
+    float v[16];
+    const bool full = live && vec_ok && k0 + 16 <= a.cols;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 f = *reinterpret_cast<const float4*>(xr + k0 + 4 * q);
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (live && k0 + j < a.cols) ? xr[k0 + j] : 0.f;
+    }
+    if constexpr (NORM) {
+      const float r = rinv_s[b];
+      if (full) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 u = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0 + 4 * q));
+          v[4 * q] = (v[4 * q] * r) * u.x;
+          v[4 * q + 1] = (v[4 * q + 1] * r) * u.y;
+          v[4 * q + 2] = (v[4 * q + 2] * r) * u.z;
+          v[4 * q + 3] = (v[4 * q + 3] * r) * u.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = (live && k0 + j < a.cols) ? (v[j] * r) * __ldg(a.norm_w + k0 + j) : 0.f;
+      }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+    int qs = 0;
+    float sxv = 0.f;
+    if (amax > 0.f) {
+      const float f = __fdiv_rn((float)TC_QMAX, amax);
+      sxv = __fdiv_rn(amax, (float)TC_QMAX);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        int q = __float2int_rn(__fmul_rn(v[j], f));
+        q = max(-TC_QMAX, min(TC_QMAX, q));
+        qs += q;
+        const int qh = (q + 128) >> 8, ql = q - 256 * qh;
+        hw[j >> 2] |= ((uint32_t)qh & 0xFFu) << (8 * (j & 3));
+        lw[j >> 2] |= ((uint32_t)ql & 0xFFu) << (8 * (j & 3));
+      }
+    }
+    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+    if (!item) continue;
+    // columns 4tt..4tt+3 of this quarter feed lane tt: block qd >> 1, b0 / b1 = qd & 1
+    uint32_t* xw = reinterpret_cast<uint32_t*>(xb + (size_t)(p * NC + 2 * b) * 4);
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+      xw[tt * 4 + qd] = hw[tt];
+      xw[16 + tt * 4 + qd] = lw[tt];
+    }
+    if (qd == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -15 * qs);
+  }
+  __syncthreads();
+
+  // 3) this warp's units
+  const uint4* xbl = xb + (g & (NC - 1)) * 4 + t;  // column g, or any valid one
+  const int2* fql = fq + (t & (NB - 1));           // batch row t, or any valid one
+  float acc0 = 0.f, acc1 = 0.f;  // rows g, g+8 of batch row t
+  bool ok = true;
+  for (int j = 0; j < n_mine; ++j) {
+    int tile, p0, np;
+    unit_span(wu0 + j, tile, p0, np);
+    const bool landed = mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1));
+    if (!__all_sync(0xffffffffu, landed)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* st = ring + (size_t)(j % TS) * a.stage_bytes;
+    const uint4* cw = reinterpret_cast<const uint4*>(st) + lane;
+    const uint8_t* sl = st + KS * 512 + g * 2 * ES;
+    const uint4* bp = xbl + (size_t)p0 * (NC * 4);
+    const int2* fp = fql + (size_t)p0 * NB;
+#pragma unroll
+    for (int i = 0; i < KS; ++i) {
+      if (i < np) {
+        const uint4 wq = cw[i * 32];
+        const uint4 bq = bp[i * NC * 4];
+        const int2 fv = fp[i * NB];
+        float s0, s1;
+        load_scale_pair<ST>(sl + (i >> a.gsh) * SG, s0, s1);
+        int c[4];
+        mma_first(c, wq.x & 0x0F0F0F0Fu, wq.x & 0xF0F0F0F0u, wq.y & 0x0F0F0F0Fu, wq.y & 0xF0F0F0F0u, bq.x, bq.y);
+        mma_acc(c, wq.z & 0x0F0F0F0Fu, wq.z & 0xF0F0F0F0u, wq.w & 0x0F0F0F0Fu, wq.w & 0xF0F0F0F0u, bq.z, bq.w);
+        const float fx = __int_as_float(fv.x);
+        const int T0 = c[0] * 512 + c[1] * 2 + fv.y;
+        const int T1 = c[2] * 512 + c[3] * 2 + fv.y * 16;  // rows g+8 carry codes * 16
+        acc0 = fmaf((float)T0, fx * s0, acc0);
+        acc1 = fmaf((float)T1, fx * (s1 * 0.0625f), acc1);
+      }
+    }
+    __syncwarp();  // every lane is done with stage j % TS
+    if (lane == 0 && j + TS < n_mine) issue(j + TS);
+
+    // end of this warp's run over `tile`?
+    const int u = wu0 + j;
+    if (j + 1 < n_mine && u + 1 < (tile + 1) * a.UT) continue;
+    const int tu0 = tile * a.UT, tu1 = tu0 + a.UT;  // the tile lies inside this CTA's range
+    float v0 = acc0, v1 = acc1;
+    bool have = true;  // this warp holds the tile's sum
+    if (wu0 > tu0 || wu1 < tu1) {
+      // several warps: partial -> shared slot (0: the tile this warp's run
+      // starts in, 1: the one it ends in); arrivals count units, so the warp
+      // that completes the tile's units sums the slots
+      float* ps = part_s + ((size_t)(warp * 2 + (wu0 >= tu0 ? 0 : 1)) * 16 + g) * NB + (t & (NB - 1));
+      if (t < NB) {
+        ps[0] = acc0;
+        ps[8 * NB] = acc1;
+      }
+      __threadfence_block();
+      __syncwarp();
+      const int mine = min(wu1, tu1) - max(wu0, tu0);
+      int old = 0;
+      if (lane == 0) old = atomicAdd(&cnt_s[tile - ctile0], mine);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      have = old + mine == a.UT;
+      if (have) {
+        __threadfence_block();
+        v0 = v1 = 0.f;
+        // the CTA's warps in order = the tile's units in order
+        for (int w = 0; w < TW; ++w) {
+          const int s0w = cu0 + ((w * nU) >> TW_SHIFT), s1w = cu0 + (((w + 1) * nU) >> TW_SHIFT);
+          if (max(s0w, tu0) >= min(s1w, tu1)) continue;
+          if (w == warp) {
+            v0 += acc0;
+            v1 += acc1;
+          } else {
+            const float* qs = part_s + ((size_t)(w * 2 + (s0w >= tu0 ? 0 : 1)) * 16 + g) * NB + (t & (NB - 1));
+            v0 += qs[0];
+            v1 += qs[8 * NB];
+          }
+        }
+      }
+    }
+    if (have) tc_epilogue<NB, EPI>(a, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_pos);
+    acc0 = acc1 = 0.f;
+  }
+  if (!ok) {
+    // a stage never landed: record it and let this warp's copies in flight
+    // finish (bounded) before the CTA's shared memory is released
+    if (lane == 0) {
+      atomicOr(a.fault, 2);
+      for (int i = 0; i < TS; ++i) mbar_wait_bounded(&bars[i], 0);
+    }
+    __syncwarp();
+  }
+}
+
+template <int NB, typename ST, int EPI, bool NORM, int KS>
+int launch_tc(const TcArgs& a, size_t smem, int grid, cudaStream_t s) {
+  auto kern = gemv_tc_kernel<NB, ST, EPI, NORM, KS>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      set_error("gemv_tc attribute (%zu bytes): %s", smem, cudaGetErrorString(e));
+      return LUMINA_E_CUDA;
+    }
+    configured = smem;
+  }
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(TW * 32), smem, s, a);
+  if (e != cudaSuccess) {
+    set_error("gemv_tc launch: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+template <int NB, typename ST, int KS>
+int tc_epi(const TcArgs& a, size_t smem, int grid, int epi, bool norm, cudaStream_t s) {
+  switch (epi) {
+    case EPI_STORE:
+      return norm ? launch_tc<NB, ST, EPI_STORE, true, KS>(a, smem, grid, s)
+                  : launch_tc<NB, ST, EPI_STORE, false, KS>(a, smem, grid, s);
+    case EPI_RESID: return norm ? LUMINA_E_UNSUPPORTED : launch_tc<NB, ST, EPI_RESID, false, KS>(a, smem, grid, s);
+    case EPI_SWIGLU: return norm ? launch_tc<NB, ST, EPI_SWIGLU, true, KS>(a, smem, grid, s) : LUMINA_E_UNSUPPORTED;
+    default: return norm ? launch_tc<NB, ST, EPI_ROPE_KV, true, KS>(a, smem, grid, s) : LUMINA_E_UNSUPPORTED;
+  }
+}
+
+template <int KS>
+int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bool norm, cudaStream_t s) {
+  if (fp16) {
+    switch (nb) {
+      case 1: return tc_epi<1, __half, KS>(a, smem, grid, epi, norm, s);
+      case 2: return tc_epi<2, __half, KS>(a, smem, grid, epi, norm, s);
+      default: return tc_epi<4, __half, KS>(a, smem, grid, epi, norm, s);
+    }
+  }
+  switch (nb) {
+    case 1: return tc_epi<1, float, KS>(a, smem, grid, epi, norm, s);
+    case 2: return tc_epi<2, float, KS>(a, smem, grid, epi, norm, s);
+    default: return tc_epi<4, float, KS>(a, smem, grid, epi, norm, s);
+  }
+}
+
+}  // namespace
+
+int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk) {
+  if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
+  const int gp = w->group / 64;
+  if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
+  if ((epi == EPI_SWIGLU || epi == EPI_ROPE_KV) && (w->rows & 1)) {
+    set_error("gemv: paired epilogue needs an even row count");
+    return LUMINA_E_ARG;
+  }
+  int* fault = fault_flag_ptr();
+  if (!fault) {
+    set_error("gemv_tc: fault flag unavailable");
+    return LUMINA_E_CUDA;
+  }
+  const int NB = batch == 1 ? 1 : batch == 2 ? 2 : 4;
+  TcArgs a{};
+  a.codes = w->codes;
+  a.scales = w->scales;
+  a.rows = w->rows;
+  a.cols = w->cols;
+  a.P = w->n_chunks / 2;
+  a.ng = w->n_groups;
+  a.gsh = gp == 1 ? 0 : gp == 2 ? 1 : 2;
+  a.T16 = w->rows_pad / 16;
+  a.x = x;
+  a.ldx = ldx;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  a.y = y;
+  a.ldy = ldy;
+  a.resid = resid;
+  a.ldr = ldr;
+  if (rk) a.rk = *rk;
+  a.nb = batch;
+  a.fault = fault;
+  const int es = w->fp16_scales ? 2 : 4;
+  // whole tiles per CTA: the smallest grid with the smallest per-CTA share
+  const int per = (a.T16 + sm_count() - 1) / sm_count();
+  const int grid = (a.T16 + per - 1) / per;
+  a.MT = per;
+  const size_t budget = 227 * 1024 - 1024;
+  const bool norm = norm_w != nullptr;
+  // units of 8 pairs when the TS-stage rings fit next to the activation
+  // tables, else of 6 or 4 (a unit holds whole scale groups: 2^gsh | KS)
+  for (int ks : {8, 6, 4}) {
+    if (ks % gp) continue;
+    a.UT = (a.P + ks - 1) / ks;
+    a.x_bytes = (a.P * 2 * NB * 64 + a.P * NB * 8 + 16 + a.MT * 4 + TW * 2 * 16 * NB * 4 + 127) / 128 * 128;
+    const int groups = std::max(1, ks >> a.gsh);
+    a.stage_bytes = (ks * 512 + groups * 16 * es + 127) / 128 * 128;
+    const size_t smem = (size_t)a.x_bytes + (size_t)TW * TS * a.stage_bytes + TW * TS * 8;
+    if (smem > budget) continue;
+    if (ks == 8) return tc_nb<8>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
+    if (ks == 6) return tc_nb<6>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
+    return tc_nb<4>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
+  }
+  return LUMINA_E_UNSUPPORTED;
+}
+
+}  // namespace lumina

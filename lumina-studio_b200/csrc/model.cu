@@ -55,6 +55,7 @@ struct lumina_model {
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   int max_splits = 32, split_rows = 64;
+  float *part1_o = nullptr, *part1_ml = nullptr;  // decode attention splits
   ActQ aq{};
   void* kv_tmp = nullptr;
   float* bias_dev = nullptr;
@@ -123,14 +124,20 @@ bool compatible(const lumina_weight* a, const lumina_weight* b) {
          a->mma == b->mma;
 }
 
-// A new tiled weight with the geometry of `a` and `rows` rows (zeroed).
-lumina_weight* alloc_like(const lumina_weight* a, int rows, int* rc) {
+// A new tiled weight with the geometry of `a` and `rows` rows (zeroed); with
+// `to_mma` (int4, group % 64 == 0) in the tensor-core fragment layout.
+lumina_weight* alloc_like(const lumina_weight* a, int rows, int* rc, bool to_mma = false) {
   lumina_weight* w = new lumina_weight(*a);
   w->rows = rows;
   w->rows_pad = (rows + ROW_PAD - 1) / ROW_PAD * ROW_PAD;
-  if (a->mma) w->rows_pad = (rows + 31) / 32 * 32;
-  const size_t cb = (size_t)w->rows_pad * a->row_bytes;
-  const size_t sb = a->mma ? (size_t)w->rows_pad * a->n_groups * (a->fp16_scales ? 2 : 4)
+  if (to_mma && !a->mma) {
+    w->mma = 1;
+    w->n_chunks = (a->nblk + 1) / 2 * 2;  // 32-column blocks, whole pairs
+    w->row_bytes = w->n_chunks * 16;
+  }
+  if (w->mma) w->rows_pad = (rows + 31) / 32 * 32;
+  const size_t cb = (size_t)w->rows_pad * w->row_bytes;
+  const size_t sb = w->mma ? (size_t)w->rows_pad * a->n_groups * (a->fp16_scales ? 2 : 4)
                            : (size_t)w->rows_pad * a->spr;
   w->codes = nullptr;
   w->scales = nullptr;
@@ -151,8 +158,8 @@ lumina_weight* alloc_like(const lumina_weight* a, int rows, int* rc) {
 
 // out row r <- row srow[r] of source sel[r] (up to three sources)
 lumina_weight* gather_rows(const std::vector<const lumina_weight*>& srcs, const std::vector<int>& sel,
-                           const std::vector<int>& srow, int* rc) {
-  lumina_weight* w = alloc_like(srcs[0], (int)sel.size(), rc);
+                           const std::vector<int>& srow, int* rc, bool to_mma = false) {
+  lumina_weight* w = alloc_like(srcs[0], (int)sel.size(), rc, to_mma);
   if (!w) return nullptr;
   int* d = nullptr;
   if (cudaMalloc(&d, sel.size() * 8) != cudaSuccess) {
@@ -182,7 +189,8 @@ lumina_weight* gather_rows(const std::vector<const lumina_weight*>& srcs, const 
 }
 
 // fused q/k/v with each head's rotation pairs (j, j + hd/2) as adjacent rows
-lumina_weight* build_qkv(const lumina_weight* q, const lumina_weight* k, const lumina_weight* v, int hd, int* rc) {
+lumina_weight* build_qkv(const lumina_weight* q, const lumina_weight* k, const lumina_weight* v, int hd, int* rc,
+                         bool to_mma) {
   std::vector<int> sel, srow;
   const lumina_weight* parts[2] = {q, k};
   for (int pi = 0; pi < 2; ++pi)
@@ -196,18 +204,33 @@ lumina_weight* build_qkv(const lumina_weight* q, const lumina_weight* k, const l
     sel.push_back(2);
     srow.push_back(r);
   }
-  return gather_rows({q, k, v}, sel, srow, rc);
+  return gather_rows({q, k, v}, sel, srow, rc, to_mma);
 }
 
 // gate/up interleaved: row 2i = gate_i, 2i+1 = up_i (SwiGLU epilogue)
-lumina_weight* build_gu(const lumina_weight* g, const lumina_weight* u, int* rc) {
+lumina_weight* build_gu(const lumina_weight* g, const lumina_weight* u, int* rc, bool to_mma) {
   std::vector<int> sel, srow;
   for (int i = 0; i < g->rows; ++i)
     for (int e = 0; e < 2; ++e) {
       sel.push_back(e);
       srow.push_back(i);
     }
-  return gather_rows({g, u}, sel, srow, rc);
+  return gather_rows({g, u}, sel, srow, rc, to_mma);
+}
+
+// the same rows in the tensor-core fragment layout
+lumina_weight* to_fragment_layout(const lumina_weight* a, int* rc) {
+  std::vector<int> sel(a->rows, 0), srow(a->rows);
+  for (int r = 0; r < a->rows; ++r) srow[r] = r;
+  return gather_rows({a}, sel, srow, rc, true);
+}
+
+// int4 with groups of 64k runs on the tensor-pipe decode GEMV unless
+// LUMINA_GEMV=dp2a keeps the CUDA-core layout
+bool wants_tc(const lumina_weight* w) {
+  const char* e = getenv("LUMINA_GEMV");
+  if (e && strcmp(e, "dp2a") == 0) return false;
+  return w->bits == 4 && w->group % 64 == 0;
 }
 
 // rope tables: cos/sin(float32(p) * freq_i) with freq_i =
@@ -312,6 +335,10 @@ int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
              int ldy, int epi, const float* resid, int ldr, const RopeKV* rk) {
   if (w->mma) {
+    if (n <= 4) {
+      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    }
     const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
     if (rc != LUMINA_E_UNSUPPORTED) return rc;
   }
@@ -358,9 +385,15 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   }
   // 2) attention (chat.py:264-281)
   const int splits = n > m->split_rows ? 1 : m->max_splits;
-  TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev, m->c.block_size,
-                       m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml, m->attn_counters, n, splits,
-                       s));
+  if (n == 1 && !bias) {
+    TRY(launch_attention_decode(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
+                                m->c.block_size, m->P_dev, m->attn, m->part1_o, m->part1_ml, m->attn_counters,
+                                m->c.max_seq, s));
+  } else {
+    TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
+                         m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml,
+                         m->attn_counters, n, splits, s));
+  }
   // 3) o_proj + residual (chat.py:282-283)
   if (tp) {
     TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->part, d, EPI_STORE, nullptr, 0, nullptr));
@@ -771,7 +804,7 @@ int lumina_model_finalize(lumina_model* m) {
     }
     int rc = LUMINA_OK;
     if (compatible(Ly.q, Ly.k) && compatible(Ly.q, Ly.v)) {
-      Ly.qkv = build_qkv(Ly.q, Ly.k, Ly.v, m->hd, &rc);
+      Ly.qkv = build_qkv(Ly.q, Ly.k, Ly.v, m->hd, &rc, wants_tc(Ly.q));
       if (rc) return rc;
       lumina_weight_free(Ly.q);
       lumina_weight_free(Ly.k);
@@ -779,11 +812,18 @@ int lumina_model_finalize(lumina_model* m) {
       Ly.q = Ly.k = Ly.v = Ly.qkv;  // keep non-null for the shape checks; freed once
     }
     if (compatible(Ly.gate, Ly.up)) {
-      Ly.gu = build_gu(Ly.gate, Ly.up, &rc);
+      Ly.gu = build_gu(Ly.gate, Ly.up, &rc, wants_tc(Ly.gate));
       if (rc) return rc;
       lumina_weight_free(Ly.gate);
       lumina_weight_free(Ly.up);
       Ly.gate = Ly.up = Ly.gu;
+    }
+    for (lumina_weight** pw : {&Ly.o, &Ly.down}) {
+      if ((*pw)->mma || !wants_tc(*pw)) continue;
+      lumina_weight* t = to_fragment_layout(*pw, &rc);
+      if (rc) return rc;
+      lumina_weight_free(*pw);
+      *pw = t;
     }
   }
   // rope tables
@@ -831,6 +871,11 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
   TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
+  {
+    const size_t s1 = (size_t)(c.max_seq + ATTN1_KEYS - 1) / ATTN1_KEYS;
+    TRY(dalloc(m, (void**)&m->part1_o, s1 * qw * 4));
+    TRY(dalloc(m, (void**)&m->part1_ml, s1 * m->nh * 2 * 4));
+  }
   LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
   if (!fault_flag_ptr()) {
     set_error("model_finalize: fault flag unavailable");

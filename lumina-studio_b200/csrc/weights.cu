@@ -350,7 +350,8 @@ int lumina_weight_upload(int device, int kind, int group_size, int pack, const u
   L.spr = (n_groups * es + 15) / 16 * 16;
   std::vector<uint8_t> sdev;
   // int4 goes to the tensor-core fragment layout when LUMINA_INT4_LAYOUT=mma
-  // (gemv_mma.cu: ahead at batch >= 4, behind the CUDA-core path at batch 1)
+  // (gemv_tc.cu for batch <= 8, gemv_mma.cu beyond); a model converts its
+  // own int4 projections to that layout when it is finalized
   const char* lay = getenv("LUMINA_INT4_LAYOUT");
   const bool want_mma = lay && strcmp(lay, "mma") == 0;
   if (bits == 4 && group_size % 64 == 0 && want_mma) {
@@ -473,7 +474,13 @@ int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx, 
                    ldy, w->cols, w->rows);
   DeviceGuard g(w->device);
   cudaStream_t s = (cudaStream_t)stream;
-  if (w->mma) return gemv_mma_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);
+  if (w->mma) {
+    if (batch <= 4) {
+      const int rc = gemv_tc_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s, nullptr);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    }
+    return gemv_mma_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);
+  }
   if (batch <= 4) {
     const int rc = gemv_fused_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);
     if (rc != LUMINA_E_UNSUPPORTED) return rc;

@@ -9,33 +9,40 @@ that the 2e-3 reference tolerance would hide.
 import numpy as np
 
 
-def act_quant(x):
-    """Per-32-column int16 quantization: q = rint(x * fp32(32767/amax))."""
+# The CUDA-core GEMVs quantize per 32 columns to +-32767; the tensor-pipe
+# decode GEMV (gemv_tc.cu) per 64 columns to +-32639, so that each value
+# splits into two signed bytes (q = 256 * qh + ql).
+CUDA_CORE = dict(block=32, qmax=32767)
+TENSOR_PIPE = dict(block=64, qmax=32639)
+
+
+def act_quant(x, block=32, qmax=32767):
+    """Per-block int16 quantization: q = rint(x * fp32(qmax/amax))."""
     x = np.asarray(x, dtype=np.float32)
     B, K = x.shape
-    nblk = (K + 31) // 32
-    xp = np.zeros((B, nblk * 32), np.float32)
+    nblk = (K + block - 1) // block
+    xp = np.zeros((B, nblk * block), np.float32)
     xp[:, :K] = x
-    blk = xp.reshape(B, nblk, 32)
+    blk = xp.reshape(B, nblk, block)
     amax = np.abs(blk).max(axis=2)
     with np.errstate(divide="ignore", invalid="ignore"):
-        f = np.where(amax > 0, np.float32(32767.0) / amax, np.float32(0)).astype(np.float32)
-        sx = np.where(amax > 0, amax / np.float32(32767.0), np.float32(0)).astype(np.float32)
-    q = np.rint((blk * f[:, :, None]).astype(np.float32)).clip(-32767, 32767).astype(np.int64)
+        f = np.where(amax > 0, np.float32(qmax) / amax, np.float32(0)).astype(np.float32)
+        sx = np.where(amax > 0, amax / np.float32(qmax), np.float32(0)).astype(np.float32)
+    q = np.rint((blk * f[:, :, None]).astype(np.float32)).clip(-qmax, qmax).astype(np.int64)
     return q, sx
 
 
-def gemv(codes, scales, group, bits, x):
+def gemv(codes, scales, group, bits, x, block=32, qmax=32767):
     """y (B, N) float64 for unpacked codes (N, K) and fp32 scales (N, ng)."""
     codes = np.asarray(codes, dtype=np.int64)
     N, K = codes.shape
     L = (1 << bits) - 1
-    q, sx = act_quant(x)
+    q, sx = act_quant(x, block, qmax)
     B, nblk, _ = q.shape
-    cp = np.zeros((N, nblk * 32), np.int64)
+    cp = np.zeros((N, nblk * block), np.int64)
     cp[:, :K] = codes
-    cb = cp.reshape(N, nblk, 32)
+    cb = cp.reshape(N, nblk, block)
     d = np.einsum("bkj,nkj->bnk", q, cb)                    # exact integer dots
     t = 2 * d - L * q.sum(axis=2)[:, None, :]
-    s = np.asarray(scales, dtype=np.float64)[:, (np.arange(nblk) * 32) // group]  # (N, nblk)
+    s = np.asarray(scales, dtype=np.float64)[:, (np.arange(nblk) * block) // group]  # (N, nblk)
     return (t * sx[:, None, :].astype(np.float64) * s[None]).sum(axis=2) / L

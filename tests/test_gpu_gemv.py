@@ -139,6 +139,34 @@ def test_gemv_7b_shapes(torch_cuda, kind, group, N, K, batch):
     np.testing.assert_allclose(y[:, rows], km, rtol=TIGHT, atol=TIGHT * np.abs(km).max())
 
 
+@pytest.mark.parametrize("group,N,K", [(64, 4096, 4096), (64, 12288, 4096), (128, 4096, 11008), (64, 300, 640),
+                                         (64, 4096, 11008)])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 8])
+def test_gemv_fragment_layout(torch_cuda, monkeypatch, group, N, K, batch):
+    """int4 in the tensor-core fragment layout: the tensor-pipe decode GEMV
+    (batch <= 4: units split over CTAs and warps, shared-tile combine; 64-
+    column activation blocks) and the batched fragment-layout GEMV (batch 8)
+    give their exact-model results, and the same bits on a repeated call."""
+    monkeypatch.setenv("LUMINA_INT4_LAYOUT", "mma")
+    rng = np.random.default_rng(N + K + batch)
+    codes = rng.integers(0, 16, (N, K)).astype(np.uint8)
+    ng = (K + group - 1) // group
+    scales = (np.abs(rng.standard_normal((N, ng))) * 0.02 + 1e-3).astype(np.float16).astype(np.float32)
+    w = upload("int4", group, codes, scales, N, K)
+    rows32, nbp = -(-N // 32) * 32, (-(-K // 32) + 1) // 2 * 2
+    assert w.info()["device_bytes"] == rows32 * nbp * 16 + rows32 * ng * 2  # the fragment layout
+    x = rng.standard_normal((batch, K)).astype(np.float32)
+    y = device_gemv(torch_cuda, w, x)
+    y2 = device_gemv(torch_cuda, w, x)
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
+    W = np.repeat(scales, group, axis=1)[:, :K] * lf.levels(4).astype(np.float32)[codes]
+    assert rel_l2(y, ref_gemv(x, W)) < REL_L2
+    rows = np.r_[0:128, N - 128:N]
+    arith = kernel_model.TENSOR_PIPE if batch <= 4 else kernel_model.CUDA_CORE
+    km = kernel_model.gemv(codes[rows], scales[rows], group, 4, x, **arith)
+    np.testing.assert_allclose(y[:, rows], km, rtol=TIGHT, atol=TIGHT * np.abs(km).max())
+
+
 def test_fp32_scales_path(torch_cuda):
     rng = np.random.default_rng(3)
     N, K = 300, 640
