@@ -80,7 +80,22 @@ struct TcArgs {
   RopeKV rk;
   int nb;       // live batch rows (<= NB)
   int* fault;
+  // the next packed weight of the decode step (its codes and scales), or
+  // null: the CTAs prefetch it into L2 once their own reads are issued
+  const uint8_t* next[2];
+  unsigned long long next_bytes[2];
 };
+
+// L2 prefetch of [p, p + bytes) (16-byte aligned, bytes % 16 == 0)
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned long long bytes) {
+  const uint8_t* c = static_cast<const uint8_t*>(p);
+  while (bytes > 0) {
+    const unsigned int n = bytes > (1u << 16) ? (1u << 16) : (unsigned int)bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+    c += n;
+    bytes -= n;
+  }
+}
 
 template <typename ST>
 __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, float& s1) {
@@ -211,10 +226,19 @@ gemv_tc_kernel(TcArgs a) {
     np = min(P - p0, KS);
   };
   // lane 0: unit j of this warp's run into stage j % TS (two bulk copies
-  // completing on the stage's mbarrier)
+  // completing on the stage's mbarrier); units are issued in order, so the
+  // (tile, unit-in-tile) of the next one is tracked, not divided out
+  int i_tile = 0, i_ku = 0;
+  if (n_mine > 0) {
+    i_tile = wu0 / a.UT;
+    i_ku = wu0 - i_tile * a.UT;
+  }
   auto issue = [&](int j) {
-    int tile, p0, np;
-    unit_span(wu0 + j, tile, p0, np);
+    const int tile = i_tile, p0 = i_ku * KS, np = min(P - p0, KS);
+    if (++i_ku == a.UT) {
+      i_ku = 0;
+      ++i_tile;
+    }
     const int G0 = p0 >> a.gsh, G1 = ((p0 + np - 1) >> a.gsh) + 1;
     uint8_t* st = ring + (size_t)(j % TS) * a.stage_bytes;
     const uint32_t cb = (uint32_t)np * 512u, sb = (uint32_t)(G1 - G0) * SG;
@@ -232,8 +256,31 @@ gemv_tc_kernel(TcArgs a) {
   __syncwarp();
   // 1) weights never depend on the previous kernel: the first stages go out
   //    before the dependency wait
-  if (lane == 0)
+  if (lane == 0) {
     for (int j = 0; j < min(TS, n_mine); ++j) issue(j);
+    // the rest of this warp's units into L2, so later stages fill at L2
+    // latency (codes of consecutive units of a tile are contiguous)
+    if (n_mine > TS) {
+      // (tile, pair) and (tile, group) orders are the memory orders, so the
+      // units' codes and scales are two contiguous spans
+      int t0, p0a, npa, t1, p0b, npb;
+      unit_span(wu0 + TS, t0, p0a, npa);
+      unit_span(wu1 - 1, t1, p0b, npb);
+      const size_t c0 = (size_t)t0 * P + p0a, c1 = (size_t)t1 * P + p0b + npb;
+      prefetch_l2(a.codes + c0 * 512, (unsigned long long)(c1 - c0) * 512);
+      const size_t g0 = (size_t)t0 * a.ng + (p0a >> a.gsh), g1 = (size_t)t1 * a.ng + ((p0b + npb - 1) >> a.gsh) + 1;
+      prefetch_l2(a.scales + g0 * SG, (unsigned long long)(g1 - g0) * SG);
+    }
+    // then this warp's slice of the next weight of the step
+    const int gw = blockIdx.x * TW + warp, nw = gridDim.x * TW;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (!a.next[r]) continue;
+      const unsigned long long chunks = a.next_bytes[r] / 16;
+      const unsigned long long c0 = chunks * gw / nw, c1 = chunks * (gw + 1) / nw;
+      if (c1 > c0) prefetch_l2(a.next[r] + c0 * 16, (c1 - c0) * 16);
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
 
@@ -268,56 +315,52 @@ gemv_tc_kernel(TcArgs a) {
     }
   }
   const bool vec_ok = ((a.ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
-  // four threads per (batch row, pair), 16 columns each; every lane runs
+  // eight threads per (batch row, pair), eight columns each; every lane runs
   // every pass (the shuffles below take the full warp)
-  for (int i0 = 0; i0 < NB * P * 4; i0 += blockDim.x) {
+  for (int i0 = 0; i0 < NB * P * 8; i0 += blockDim.x) {
     const int i = i0 + threadIdx.x;
-    const bool item = i < NB * P * 4;
-    const int b = item ? i / (P * 4) : 0, p = item ? (i >> 2) % P : 0, qd = i & 3;
+    const bool item = i < NB * P * 8;
+    const int b = item ? i / (P * 8) : 0, p = item ? (i >> 3) % P : 0, oc = i & 7;
     const bool live = item && b < a.nb;
     const float* xr = a.x + (size_t)b * a.ldx;
-    const int k0 = p * 64 + 16 * qd;
-    float v[16];
-    const bool full = live && vec_ok && k0 + 16 <= a.cols;
+    const int k0 = p * 64 + 8 * oc;
+    float v[8];
+    const bool full = live && vec_ok && k0 + 8 <= a.cols;
     if (full) {
+      const float4 f0 = *reinterpret_cast<const float4*>(xr + k0);
+      const float4 f1 = *reinterpret_cast<const float4*>(xr + k0 + 4);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+      if constexpr (NORM) {
+        const float r = rinv_s[b];
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0));
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0 + 4));
+        const float w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 f = *reinterpret_cast<const float4*>(xr + k0 + 4 * q);
-        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+        for (int j = 0; j < 8; ++j) v[j] = (v[j] * r) * w8[j];
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = (live && k0 + j < a.cols) ? xr[k0 + j] : 0.f;
-    }
-    if constexpr (NORM) {
-      const float r = rinv_s[b];
-      if (full) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 u = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0 + 4 * q));
-          v[4 * q] = (v[4 * q] * r) * u.x;
-          v[4 * q + 1] = (v[4 * q + 1] * r) * u.y;
-          v[4 * q + 2] = (v[4 * q + 2] * r) * u.z;
-          v[4 * q + 3] = (v[4 * q + 3] * r) * u.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = (live && k0 + j < a.cols) ? (v[j] * r) * __ldg(a.norm_w + k0 + j) : 0.f;
+      for (int j = 0; j < 8; ++j) {
+        const bool in = live && k0 + j < a.cols;
+        v[j] = in ? xr[k0 + j] : 0.f;
+        if constexpr (NORM) v[j] = in ? (v[j] * rinv_s[b]) * __ldg(a.norm_w + k0 + j) : 0.f;
       }
     }
     float amax = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
     int qs = 0;
     float sxv = 0.f;
     if (amax > 0.f) {
       const float f = __fdiv_rn((float)TC_QMAX, amax);
       sxv = __fdiv_rn(amax, (float)TC_QMAX);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 8; ++j) {
         int q = __float2int_rn(__fmul_rn(v[j], f));
         q = max(-TC_QMAX, min(TC_QMAX, q));
         qs += q;
@@ -328,15 +371,18 @@ gemv_tc_kernel(TcArgs a) {
     }
     qs += __shfl_xor_sync(0xffffffffu, qs, 1);
     qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 4);
     if (!item) continue;
-    // columns 4tt..4tt+3 of this quarter feed lane tt: block qd >> 1, b0 / b1 = qd & 1
+    // columns 8*oc .. 8*oc+7 of the pair: block oc >> 2, b0 / b1 = (oc >> 1) & 1,
+    // lanes tt = 2 * (oc & 1) and the next one, 4 columns each
+    const int comp = ((oc >> 2) << 1) | ((oc >> 1) & 1), tt0 = 2 * (oc & 1);
     uint32_t* xw = reinterpret_cast<uint32_t*>(xb + (size_t)(p * NC + 2 * b) * 4);
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt) {
-      xw[tt * 4 + qd] = hw[tt];
-      xw[16 + tt * 4 + qd] = lw[tt];
+    for (int e = 0; e < 2; ++e) {
+      xw[(tt0 + e) * 4 + comp] = hw[e];
+      xw[16 + (tt0 + e) * 4 + comp] = lw[e];
     }
-    if (qd == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -15 * qs);
+    if (oc == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -15 * qs);
   }
   __syncthreads();
 
@@ -345,9 +391,13 @@ gemv_tc_kernel(TcArgs a) {
   const int2* fql = fq + (t & (NB - 1));           // batch row t, or any valid one
   float acc0 = 0.f, acc1 = 0.f;  // rows g, g+8 of batch row t
   bool ok = true;
+  int tile = 0, ku = 0;
+  if (n_mine > 0) {
+    tile = wu0 / a.UT;
+    ku = wu0 - tile * a.UT;
+  }
   for (int j = 0; j < n_mine; ++j) {
-    int tile, p0, np;
-    unit_span(wu0 + j, tile, p0, np);
+    const int p0 = ku * KS, np = min(P - p0, KS);
     const bool landed = mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1));
     if (!__all_sync(0xffffffffu, landed)) {
       ok = false;
@@ -358,30 +408,34 @@ gemv_tc_kernel(TcArgs a) {
     const uint8_t* sl = st + KS * 512 + g * 2 * ES;
     const uint4* bp = xbl + (size_t)p0 * (NC * 4);
     const int2* fp = fql + (size_t)p0 * NB;
+    auto pair = [&](int i) {
+      const uint4 wq = cw[i * 32];
+      const uint4 bq = bp[i * NC * 4];
+      const int2 fv = fp[i * NB];
+      float s0, s1;
+      load_scale_pair<ST>(sl + (i >> a.gsh) * SG, s0, s1);
+      int c[4];
+      mma_first(c, wq.x & 0x0F0F0F0Fu, wq.x & 0xF0F0F0F0u, wq.y & 0x0F0F0F0Fu, wq.y & 0xF0F0F0F0u, bq.x, bq.y);
+      mma_acc(c, wq.z & 0x0F0F0F0Fu, wq.z & 0xF0F0F0F0u, wq.w & 0x0F0F0F0Fu, wq.w & 0xF0F0F0F0u, bq.z, bq.w);
+      const float fx = __int_as_float(fv.x);
+      const int T0 = c[0] * 512 + c[1] * 2 + fv.y;
+      const int T1 = c[2] * 512 + c[3] * 2 + fv.y * 16;  // rows g+8 carry codes * 16
+      acc0 = fmaf((float)T0, fx * s0, acc0);
+      acc1 = fmaf((float)T1, fx * (s1 * 0.0625f), acc1);
+    };
+    if (np == KS) {
 #pragma unroll
-    for (int i = 0; i < KS; ++i) {
-      if (i < np) {
-        const uint4 wq = cw[i * 32];
-        const uint4 bq = bp[i * NC * 4];
-        const int2 fv = fp[i * NB];
-        float s0, s1;
-        load_scale_pair<ST>(sl + (i >> a.gsh) * SG, s0, s1);
-        int c[4];
-        mma_first(c, wq.x & 0x0F0F0F0Fu, wq.x & 0xF0F0F0F0u, wq.y & 0x0F0F0F0Fu, wq.y & 0xF0F0F0F0u, bq.x, bq.y);
-        mma_acc(c, wq.z & 0x0F0F0F0Fu, wq.z & 0xF0F0F0F0u, wq.w & 0x0F0F0F0Fu, wq.w & 0xF0F0F0F0u, bq.z, bq.w);
-        const float fx = __int_as_float(fv.x);
-        const int T0 = c[0] * 512 + c[1] * 2 + fv.y;
-        const int T1 = c[2] * 512 + c[3] * 2 + fv.y * 16;  // rows g+8 carry codes * 16
-        acc0 = fmaf((float)T0, fx * s0, acc0);
-        acc1 = fmaf((float)T1, fx * (s1 * 0.0625f), acc1);
-      }
+      for (int i = 0; i < KS; ++i) pair(i);
+    } else {
+      for (int i = 0; i < np; ++i) pair(i);  // the short last unit of a row
     }
     __syncwarp();  // every lane is done with stage j % TS
     if (lane == 0 && j + TS < n_mine) issue(j + TS);
 
     // end of this warp's run over `tile`?
-    const int u = wu0 + j;
-    if (j + 1 < n_mine && u + 1 < (tile + 1) * a.UT) continue;
+    const bool tile_end = j + 1 == n_mine || ku + 1 == a.UT;
+    if (++ku == a.UT) ku = 0;
+    if (!tile_end) continue;
     const int tu0 = tile * a.UT, tu1 = tu0 + a.UT;  // the tile lies inside this CTA's range
     float v0 = acc0, v1 = acc1;
     bool have = true;  // this warp holds the tile's sum
@@ -404,9 +458,13 @@ gemv_tc_kernel(TcArgs a) {
       if (have) {
         __threadfence_block();
         v0 = v1 = 0.f;
-        // the CTA's warps in order = the tile's units in order
-        for (int w = 0; w < TW; ++w) {
-          const int s0w = cu0 + ((w * nU) >> TW_SHIFT), s1w = cu0 + (((w + 1) * nU) >> TW_SHIFT);
+        // the contributing warps are contiguous: from the first whose run
+        // holds tu0, in order (= the tile's units in order)
+        auto start = [&](int w) { return cu0 + ((w * nU) >> TW_SHIFT); };
+        int w = warp;
+        while (w > 0 && start(w) > tu0) --w;
+        for (; w < TW && start(w) < tu1; ++w) {
+          const int s0w = start(w), s1w = start(w + 1);
           if (max(s0w, tu0) >= min(s1w, tu1)) continue;
           if (w == warp) {
             v0 += acc0;
@@ -421,6 +479,7 @@ gemv_tc_kernel(TcArgs a) {
     }
     if (have) tc_epilogue<NB, EPI>(a, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_pos);
     acc0 = acc1 = 0.f;
+    ++tile;
   }
   if (!ok) {
     // a stage never landed: record it and let this warp's copies in flight
@@ -484,7 +543,8 @@ int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bo
 }  // namespace
 
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
-                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk) {
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
+                   const lumina_weight* next) {
   if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
@@ -518,6 +578,14 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   if (rk) a.rk = *rk;
   a.nb = batch;
   a.fault = fault;
+  if (next) {
+    const int es_n = next->fp16_scales ? 2 : 4;
+    a.next[0] = next->codes;
+    a.next_bytes[0] = (unsigned long long)next->rows_pad * next->row_bytes / 16 * 16;
+    a.next[1] = next->scales;
+    a.next_bytes[1] = (next->mma ? (unsigned long long)next->rows_pad * next->n_groups * es_n
+                                 : (unsigned long long)next->rows_pad * next->spr) / 16 * 16;
+  }
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
   const int per = (a.T16 + sm_count() - 1) / sm_count();

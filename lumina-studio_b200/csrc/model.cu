@@ -55,7 +55,6 @@ struct lumina_model {
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   int max_splits = 32, split_rows = 64;
-  float *part1_o = nullptr, *part1_ml = nullptr;  // decode attention splits
   ActQ aq{};
   void* kv_tmp = nullptr;
   float* bias_dev = nullptr;
@@ -333,10 +332,10 @@ int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
 // y = W x (+ epilogue): the fused decode GEMV for 1, 2 or 4 rows, else (or
 // when the shape does not fit it) act_quant + the global-activation GEMV.
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
-             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk) {
+             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const lumina_weight* next = nullptr) {
   if (w->mma) {
     if (n <= 4) {
-      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
+      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, next);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
@@ -374,7 +373,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     rk.kv_fp16 = m->c.kv_fp16;
     rk.q_out = m->q_buf;
     rk.row_base = 0;
-    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk));
+    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, Ly.o));
   } else {
     lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
     const int off[3] = {0, qw, qw + kw};
@@ -386,9 +385,8 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   // 2) attention (chat.py:264-281)
   const int splits = n > m->split_rows ? 1 : m->max_splits;
   if (n == 1 && !bias) {
-    TRY(launch_attention_decode(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
-                                m->c.block_size, m->P_dev, m->attn, m->part1_o, m->part1_ml, m->attn_counters,
-                                m->c.max_seq, s));
+    TRY(launch_attention_cluster(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
+                                 m->c.block_size, m->P_dev, m->attn, s));
   } else {
     TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
                          m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml,
@@ -400,11 +398,11 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(allreduce(m, m->part, (size_t)n * d));
     TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
   } else {
-    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, Ly.gu));
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
-    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr));
+    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr, Ly.down));
   } else {
     TRY(gemv_any(m, Ly.gate, m->x, d, n, Ly.post_norm, m->g_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(gemv_any(m, Ly.up, m->x, d, n, Ly.post_norm, m->u_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
@@ -415,7 +413,8 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(allreduce(m, m->part, (size_t)n * d));
     TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
   } else {
-    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr,
+                 l + 1 < m->c.n_layer ? m->L[l + 1].qkv : nullptr));
   }
   return LUMINA_OK;
 }
@@ -871,11 +870,6 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
   TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
-  {
-    const size_t s1 = (size_t)(c.max_seq + ATTN1_KEYS - 1) / ATTN1_KEYS;
-    TRY(dalloc(m, (void**)&m->part1_o, s1 * qw * 4));
-    TRY(dalloc(m, (void**)&m->part1_ml, s1 * m->nh * 2 * 4));
-  }
   LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
   if (!fault_flag_ptr()) {
     set_error("model_finalize: fault flag unavailable");
@@ -1156,8 +1150,12 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
       const int epis[4] = {EPI_STORE, EPI_STORE, Ly.gu ? EPI_SWIGLU : EPI_STORE, EPI_STORE};
       const int lds[4] = {width, d, m->ffn, d};
       const int ldx[4] = {d, qw, d, m->ffn};
+      const lumina_weight* nxt =
+          l + 1 < m->c.n_layer ? (m->L[l + 1].qkv ? m->L[l + 1].qkv : m->L[l + 1].q) : nullptr;
       for (int i = 0; i < 4; ++i) {
-        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr));
+        // each launch prefetches the next one's weights, as in the decode step
+        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr,
+                     i < 3 ? ws[i + 1] : nxt));
         if (count) {
           ++launches;
           const int out_rows = epis[i] == EPI_SWIGLU ? ws[i]->rows / 2 : ws[i]->rows;

@@ -62,13 +62,12 @@ int launch_rope_append(bool fp16, const float* qkv, int nh, int nkv, int hd, con
 int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
                      const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
                      float* part_o, float* part_ml, int* counters, int max_n, int max_splits, cudaStream_t s);
-// single-query decode attention (one new row, no bias) in splits of
-// ATTN1_KEYS keys; part_o / part_ml hold ceil(max_seq / ATTN1_KEYS) x nh
-// splits, counters nh ints (zero between launches)
-constexpr int ATTN1_KEYS = 64;
-int launch_attention_decode(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                            const int* bt, int bs, const DevParams* P, float* out, float* part_o, float* part_ml,
-                            int* counters, int max_seq, cudaStream_t s);
+// single-query decode attention (one new row, no bias): one cluster of
+// ATTNC_CLUSTER CTAs per head, keys streamed in chunks of ATTNC_CHUNK
+constexpr int ATTNC_CLUSTER = 8;
+constexpr int ATTNC_CHUNK = 64;
+int launch_attention_cluster(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
+                             const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s);
 int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, int batch, float* y, int ldy,
                       const float* resid, int ldr, cudaStream_t s, unsigned long long* amax = nullptr);
 int launch_gather_rows(const lumina_weight& out, const lumina_weight& s0, const lumina_weight& s1,

@@ -232,179 +232,6 @@ attn_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// Single-query decode attention (one new row, no bias): every key up to the
-// new row is visible (chat.py:264-281 with sq = 1). One CTA per (head,
-// split of 64 keys); the grid covers the longest context and CTAs past the
-// current length return at once. The split's K and V rows are copied into
-// shared memory in one burst (cp.async, 16 bytes per thread per copy; K rows
-// padded by 16 bytes so that lanes reading consecutive keys hit distinct
-// banks), then: scores with lanes along keys and two warps per half of the
-// head dimension, the split's softmax in one warp, P.V with threads along
-// dimension pairs, and the split's (max, sum, unnormalized output) merged by
-// the last CTA of the head in split order (deterministic), as attn_kernel.
-// ---------------------------------------------------------------------------
-template <int HD, typename KT>
-__global__ void __launch_bounds__(128)
-attn1_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
-             const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
-             const DevParams* __restrict__ P, float* __restrict__ out, float* __restrict__ part_o,
-             float* __restrict__ part_ml, float sdiv, int* __restrict__ counters) {
-  constexpr int kmax = ATTN1_KEYS;
-  constexpr int ES = sizeof(KT);
-  constexpr int KROW = HD * ES + 16;  // padded K row (bytes)
-  constexpr int VROW = HD * ES;
-  constexpr int CH = HD * ES / 16;    // 16-byte chunks per row
-  const int h = blockIdx.x, sp = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int T = P->t_tot, ns = (T + kmax - 1) / kmax;
-  if (sp >= ns) return;
-  const int k0 = sp * kmax, k1 = min(T, k0 + kmax), nk = k1 - k0;
-  const int kvh = h / (nh / nkv);
-  const size_t bstride = (size_t)nkv * bs * HD;
-
-  extern __shared__ __align__(16) uint8_t sm[];
-  uint8_t* ks = sm;                                   // [kmax][KROW]
-  uint8_t* vs = ks + (size_t)kmax * KROW;             // [kmax][VROW]
-  float* qs = reinterpret_cast<float*>(vs + (size_t)kmax * VROW);  // [HD]
-  float* sc = qs + HD;                                 // [2][kmax] half-dots, then p
-  __shared__ float red_m, red_l;
-  __shared__ float po[128 / (HD / 2)][HD];
-
-  // 1) the split's K and V rows, all copies in flight at once
-  for (int i = tid; i < nk * CH; i += 128) {
-    const int j = i / CH, c = i - j * CH;
-    const int key = k0 + j;
-    const int blk = block_table[key / bs], off = key % bs;
-    const size_t base = (size_t)blk * bstride + ((size_t)kvh * bs + off) * HD;
-    const uint8_t* kp = reinterpret_cast<const uint8_t*>(kcache + base) + c * 16;
-    const uint8_t* vp = reinterpret_cast<const uint8_t*>(vcache + base) + c * 16;
-    const uint32_t kd = (uint32_t)__cvta_generic_to_shared(ks + (size_t)j * KROW + c * 16);
-    const uint32_t vd = (uint32_t)__cvta_generic_to_shared(vs + (size_t)j * VROW + c * 16);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kd), "l"(kp) : "memory");
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(vd), "l"(vp) : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int d = tid; d < HD; d += 128) qs[d] = q[(size_t)h * HD + d];
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-
-  // 2) half-dots: warp w takes dims (w & 1) * HD/2 .. and keys (w >> 1) * 32 + lane
-  {
-    const int hf = warp & 1;
-    float qv[HD / 2];
-#pragma unroll
-    for (int e = 0; e < HD / 2; ++e) qv[e] = qs[hf * (HD / 2) + e];
-    for (int j = (warp >> 1) * 32 + lane; j < nk; j += 64) {
-      // this key's half row from shared memory, 16 bytes per load
-      const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)j * KROW + hf * (HD / 2) * ES);
-      float d = 0.f;
-#pragma unroll
-      for (int c = 0; c < (HD / 2) * ES / 16; ++c) {
-        const uint4 w = kr[c];
-        if constexpr (ES == 2) {
-          const __half2* hh = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(hh[e]);
-            d = fmaf(qv[c * 8 + 2 * e], f.x, d);
-            d = fmaf(qv[c * 8 + 2 * e + 1], f.y, d);
-          }
-        } else {
-          d = fmaf(qv[c * 4], __uint_as_float(w.x), d);
-          d = fmaf(qv[c * 4 + 1], __uint_as_float(w.y), d);
-          d = fmaf(qv[c * 4 + 2], __uint_as_float(w.z), d);
-          d = fmaf(qv[c * 4 + 3], __uint_as_float(w.w), d);
-        }
-      }
-      sc[hf * kmax + j] = d;
-    }
-  }
-  __syncthreads();
-
-  // 3) the split's softmax (warp 0)
-  if (warp == 0) {
-    float m = -INFINITY;
-    for (int j = lane; j < nk; j += 32) {
-      const float s = __fdiv_rn(sc[j] + sc[kmax + j], sdiv);
-      sc[j] = s;
-      m = fmaxf(m, s);
-    }
-    m = warp_max(m);
-    float l = 0.f;
-    for (int j = lane; j < nk; j += 32) {
-      const float p = expf(sc[j] - m);
-      sc[j] = p;
-      l += p;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      red_m = m;
-      red_l = l;
-    }
-  }
-  __syncthreads();
-
-  // 4) P.V: thread (phase kp, dim pair dp), keys kp, kp + NPH, ...
-  constexpr int DP = HD / 2, NPH = 128 / DP;
-  const int dp = tid % DP, kp = tid / DP;
-  float o0 = 0.f, o1 = 0.f;
-  for (int j = kp; j < nk; j += NPH) {
-    const float p = sc[j];
-    float2 v;
-    if constexpr (ES == 2) {
-      v = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)j * VROW + dp * 4));
-    } else {
-      v = *reinterpret_cast<const float2*>(vs + (size_t)j * VROW + dp * 8);
-    }
-    o0 = fmaf(p, v.x, o0);
-    o1 = fmaf(p, v.y, o1);
-  }
-  po[kp][2 * dp] = o0;
-  po[kp][2 * dp + 1] = o1;
-  __syncthreads();
-  const float M = red_m, L = red_l;
-  for (int d = tid; d < HD; d += 128) {
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < NPH; ++i) acc += po[i][d];
-    if (ns == 1) out[(size_t)h * HD + d] = acc / L;
-    else part_o[((size_t)sp * nh + h) * HD + d] = acc;
-  }
-  if (ns == 1) return;
-  if (tid == 0) {
-    part_ml[((size_t)sp * nh + h) * 2 + 0] = M;
-    part_ml[((size_t)sp * nh + h) * 2 + 1] = L;
-  }
-  // the last split CTA of this head merges every split in split order
-  // (deterministic), then re-arms the counter for the next forward
-  __shared__ int is_last;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&counters[h], 1) == ns - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  float Mx = -INFINITY;
-  for (int s2 = 0; s2 < ns; ++s2) Mx = fmaxf(Mx, __ldcg(&part_ml[((size_t)s2 * nh + h) * 2]));
-  float Lx = 0.f;
-  for (int s2 = 0; s2 < ns; ++s2) {
-    const float ms = __ldcg(&part_ml[((size_t)s2 * nh + h) * 2]);
-    if (ms != -INFINITY) Lx += expf(ms - Mx) * __ldcg(&part_ml[((size_t)s2 * nh + h) * 2 + 1]);
-  }
-  for (int d = tid; d < HD; d += 128) {
-    float acc = 0.f;
-    for (int s2 = 0; s2 < ns; ++s2) {
-      const float ms = __ldcg(&part_ml[((size_t)s2 * nh + h) * 2]);
-      if (ms != -INFINITY) acc = fmaf(expf(ms - Mx), __ldcg(&part_o[((size_t)s2 * nh + h) * HD + d]), acc);
-    }
-    out[(size_t)h * HD + d] = acc / Lx;
-  }
-  if (tid == 0) counters[h] = 0;
-}
-
-// ---------------------------------------------------------------------------
 // fp16-weight GEMV, fp32 x / accumulate: the LM head (chat.py:388, fp16 head
 // from chat.py:140) and projections a file keeps raw. Warp per 2 rows, lanes
 // along K with 16-byte loads.
@@ -708,39 +535,6 @@ int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const v
     return LUMINA_E_UNSUPPORTED;
   }
 #undef ATT
-  return LUMINA_OK;
-}
-
-static int attn1_smem_bytes(bool fp16, int hd) {
-  const int es = fp16 ? 2 : 4, kmax = ATTN1_KEYS;
-  return kmax * (hd * es + 16) + kmax * hd * es + hd * 4 + 2 * kmax * 4;
-}
-
-int launch_attention_decode(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                            const int* bt, int bs, const DevParams* P, float* out, float* part_o, float* part_ml,
-                            int* counters, int max_seq, cudaStream_t s) {
-  const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
-  const int smem = attn1_smem_bytes(fp16, hd);
-  dim3 grid(nh, (max_seq + ATTN1_KEYS - 1) / ATTN1_KEYS);
-#define ATT1(HD_, KT_)                                                                                           \
-  do {                                                                                                          \
-    static int configured = 0;                                                                                  \
-    if (smem > configured) {                                                                                    \
-      RET_LAUNCH(cudaFuncSetAttribute(attn1_kernel<HD_, KT_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
-      configured = smem;                                                                                        \
-    }                                                                                                           \
-    RET_LAUNCH(launch_pdl(attn1_kernel<HD_, KT_>, grid, dim3(128), (size_t)smem, s, q, nh, nkv, (const KT_*)kc,  \
-                          (const KT_*)vc, bt, bs, P, out, part_o, part_ml, sdiv, counters));                   \
-  } while (0)
-  if (hd == 128) {
-    if (fp16) ATT1(128, __half); else ATT1(128, float);
-  } else if (hd == 64) {
-    if (fp16) ATT1(64, __half); else ATT1(64, float);
-  } else {
-    set_error("attention: head_dim %d not built (64, 128)", hd);
-    return LUMINA_E_UNSUPPORTED;
-  }
-#undef ATT1
   return LUMINA_OK;
 }
 
