@@ -31,6 +31,7 @@
 // the partials in unit order (so the result does not depend on which warp
 // finishes last) and applies the epilogue.
 #include "gemv_impl.cuh"
+#include "tc_act.cuh"
 
 namespace lumina {
 
@@ -39,7 +40,6 @@ namespace {
 constexpr int TW = 16;          // warps per CTA
 constexpr int TW_SHIFT = 4;     // log2(TW)
 constexpr int TS = 3;           // ring stages per warp
-constexpr int TC_QMAX = 32639;  // 256 * 127 + 127
 
 __device__ __forceinline__ void mma_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -208,16 +208,15 @@ gemv_tc_kernel(TcArgs a) {
 
   extern __shared__ __align__(128) uint8_t smem[];
   // [B fragments: P x NC x 4 lanes x 16 B][(sx, -15*sum q): P x NB x 8 B]
-  // [rinv: NB floats, 16 B][tile counters: MT ints][partials: TW x 2 x 16 x NB floats]
+  // [tile counters: MT ints][partials: TW x 2 x 16 x NB floats]
   // [rings: TW x TS x stage_bytes][mbarriers: TW x TS]
   uint4* xb = reinterpret_cast<uint4*>(smem);
   int2* fq = reinterpret_cast<int2*>(xb + (size_t)P * NC * 4);
-  float* rinv_s = reinterpret_cast<float*>(fq + (size_t)P * NB);
-  int* cnt_s = reinterpret_cast<int*>(rinv_s + 4);
+  int* cnt_s = reinterpret_cast<int*>(fq + (size_t)P * NB);
   float* part_s = reinterpret_cast<float*>(cnt_s + a.MT);
   uint8_t* ring = smem + a.x_bytes + (size_t)warp * TS * a.stage_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.x_bytes + (size_t)TW * TS * a.stage_bytes) + warp * TS;
-  __shared__ float red[TW];
+  __shared__ float red[NB * TW];
   __shared__ int ep_blk[NB], ep_off[NB], ep_pos[NB];
 
   auto unit_span = [&](int u, int& tile, int& p0, int& np) {
@@ -281,6 +280,9 @@ gemv_tc_kernel(TcArgs a) {
       if (c1 > c0) prefetch_l2(a.next[r] + c0 * 16, (c1 - c0) * 16);
     }
   }
+  // norm weights never depend on the previous kernel either
+  float wpre[TQ_CH][8];
+  if constexpr (NORM) tq_preload<NB>(wpre, a.norm_w, a.cols, P);
   pdl_launch_dependents();
   pdl_wait();
 
@@ -294,96 +296,7 @@ gemv_tc_kernel(TcArgs a) {
       ep_pos[threadIdx.x] = a.rk.row_pos[threadIdx.x];
     }
   }
-  if constexpr (NORM) {
-    // chat.py:63-66: x / sqrt(mean(x^2) + eps) * w (fp32), one factor per row
-    for (int b = 0; b < NB; ++b) {
-      float ss = 0.f;
-      if (b < a.nb)
-        for (int k = threadIdx.x; k < a.cols; k += blockDim.x) {
-          const float v = a.x[(size_t)b * a.ldx + k];
-          ss = fmaf(v, v, ss);
-        }
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float tot = 0.f;
-        for (int i = 0; i < TW; ++i) tot += red[i];
-        rinv_s[b] = 1.0f / sqrtf(tot / (float)a.cols + a.eps);
-      }
-      __syncthreads();
-    }
-  }
-  const bool vec_ok = ((a.ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
-  // eight threads per (batch row, pair), eight columns each; every lane runs
-  // every pass (the shuffles below take the full warp)
-  for (int i0 = 0; i0 < NB * P * 8; i0 += blockDim.x) {
-    const int i = i0 + threadIdx.x;
-    const bool item = i < NB * P * 8;
-    const int b = item ? i / (P * 8) : 0, p = item ? (i >> 3) % P : 0, oc = i & 7;
-    const bool live = item && b < a.nb;
-    const float* xr = a.x + (size_t)b * a.ldx;
-    const int k0 = p * 64 + 8 * oc;
-    float v[8];
-    const bool full = live && vec_ok && k0 + 8 <= a.cols;
-    if (full) {
-      const float4 f0 = *reinterpret_cast<const float4*>(xr + k0);
-      const float4 f1 = *reinterpret_cast<const float4*>(xr + k0 + 4);
-      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-      if constexpr (NORM) {
-        const float r = rinv_s[b];
-        const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0));
-        const float4 u1 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k0 + 4));
-        const float w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (v[j] * r) * w8[j];
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const bool in = live && k0 + j < a.cols;
-        v[j] = in ? xr[k0 + j] : 0.f;
-        if constexpr (NORM) v[j] = in ? (v[j] * rinv_s[b]) * __ldg(a.norm_w + k0 + j) : 0.f;
-      }
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
-    int qs = 0;
-    float sxv = 0.f;
-    if (amax > 0.f) {
-      const float f = __fdiv_rn((float)TC_QMAX, amax);
-      sxv = __fdiv_rn(amax, (float)TC_QMAX);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        int q = __float2int_rn(__fmul_rn(v[j], f));
-        q = max(-TC_QMAX, min(TC_QMAX, q));
-        qs += q;
-        const int qh = (q + 128) >> 8, ql = q - 256 * qh;
-        hw[j >> 2] |= ((uint32_t)qh & 0xFFu) << (8 * (j & 3));
-        lw[j >> 2] |= ((uint32_t)ql & 0xFFu) << (8 * (j & 3));
-      }
-    }
-    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
-    qs += __shfl_xor_sync(0xffffffffu, qs, 4);
-    if (!item) continue;
-    // columns 8*oc .. 8*oc+7 of the pair: block oc >> 2, b0 / b1 = (oc >> 1) & 1,
-    // lanes tt = 2 * (oc & 1) and the next one, 4 columns each
-    const int comp = ((oc >> 2) << 1) | ((oc >> 1) & 1), tt0 = 2 * (oc & 1);
-    uint32_t* xw = reinterpret_cast<uint32_t*>(xb + (size_t)(p * NC + 2 * b) * 4);
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      xw[(tt0 + e) * 4 + comp] = hw[e];
-      xw[16 + (tt0 + e) * 4 + comp] = lw[e];
-    }
-    if (oc == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -15 * qs);
-  }
+  tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red);
   __syncthreads();
 
   // 3) this warp's units
@@ -598,7 +511,7 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   for (int ks : {8, 6, 4}) {
     if (ks % gp) continue;
     a.UT = (a.P + ks - 1) / ks;
-    a.x_bytes = (a.P * 2 * NB * 64 + a.P * NB * 8 + 16 + a.MT * 4 + TW * 2 * 16 * NB * 4 + 127) / 128 * 128;
+    a.x_bytes = (a.P * 2 * NB * 64 + a.P * NB * 8 + a.MT * 4 + TW * 2 * 16 * NB * 4 + 127) / 128 * 128;
     const int groups = std::max(1, ks >> a.gsh);
     a.stage_bytes = (ks * 512 + groups * 16 * es + 127) / 128 * 128;
     const size_t smem = (size_t)a.x_bytes + (size_t)TW * TS * a.stage_bytes + TW * TS * 8;
