@@ -74,6 +74,9 @@ struct lumina_model {
   int* chain_tokens = nullptr;            // [max_seq] generated tokens
   int* chain_count = nullptr;
   int chain_kernels = 0;                  // kernel nodes in chain_graph
+  void* mk_plan = nullptr;                // persistent decode-step kernel (decode_mk.cu), or null
+  unsigned int* mk_sync = nullptr;
+  float* mk_part = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int graph_splits = 0;
   bool finalized = false;
@@ -530,6 +533,41 @@ int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int*
   return LUMINA_OK;
 }
 
+// the persistent decode step (one new row, embed .. head), greedy: commit
+// the argmax as the next token on the device
+int launch_mk(lumina_model* m, bool greedy) {
+  MkRun r{};
+  r.x = m->x;
+  r.q_buf = m->q_buf;
+  r.attn = m->attn;
+  r.ffn_buf = m->ffn_buf;
+  r.kpool = m->kpool;
+  r.vpool = m->vpool;
+  r.layer_elems = m->layer_elems;
+  r.kv_fp16 = m->c.kv_fp16;
+  r.bt = m->bt_dev;
+  r.bs = m->c.block_size;
+  r.cos_t = m->rope_cos;
+  r.sin_t = m->rope_sin;
+  r.P = m->P_dev;
+  r.rowpos = m->rowpos_dev;
+  r.tokens = m->tokens_dev;
+  r.embed = m->embed;
+  r.embed_rows = m->embed_rows;
+  r.head = m->head;
+  r.vocab = m->head_rows;
+  r.logits = m->logits;
+  r.amax_key = m->amax_key_dev;
+  r.greedy = greedy ? 1 : 0;
+  r.chain_tokens = m->chain_tokens;
+  r.chain_count = m->chain_count;
+  r.max_splits = m->max_splits;
+  r.max_seq = m->c.max_seq;
+  r.part = m->mk_part;
+  r.sync = m->mk_sync;
+  return decode_mk_launch(m->mk_plan, r, m->stream);
+}
+
 int capture_step(lumina_model* m) {
   cudaStream_t s = m->stream;
   cudaGraph_t g = nullptr;
@@ -545,13 +583,17 @@ int capture_step(lumina_model* m) {
       break;
     }
     const bool fused_argmax = m->comm == nullptr;
-    if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
-                           fused_argmax ? m->amax_key_dev : nullptr, s)))
-      break;
-    for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
-    if (rc) break;
-    if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
-    if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
+    if (m->mk_plan) {
+      if ((rc = launch_mk(m, false))) break;
+    } else {
+      if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
+                             fused_argmax ? m->amax_key_dev : nullptr, s)))
+        break;
+      for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
+      if (rc) break;
+      if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
+      if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
+    }
     if (cudaMemcpyAsync(m->logits_host, m->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaMemcpyAsync(m->argmax_host, m->argmax_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaMemcpyAsync(m->amax_key_host, m->amax_key_dev, 8, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
@@ -605,6 +647,10 @@ int capture_chain(lumina_model* m) {
   const int V = m->head_rows * std::max(1, m->c.tp_size);
   const bool fused_argmax = m->comm == nullptr;
   do {
+    if (m->mk_plan) {
+      rc = launch_mk(m, true);
+      break;
+    }
     if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
                            fused_argmax ? m->amax_key_dev : nullptr, s)))
       break;
@@ -870,6 +916,36 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
   TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
+  {
+    // the persistent decode step when LUMINA_MEGAKERNEL=1 and the model fits it
+    const char* e = getenv("LUMINA_MEGAKERNEL");
+    if (e && strcmp(e, "1") == 0 && !m->comm && c.tp_size <= 1) {
+      MkSetup ms;
+      ms.n_layer = c.n_layer;
+      ms.d = m->d;
+      ms.nh = m->nh;
+      ms.nkv = m->nkv;
+      ms.hd = m->hd;
+      ms.ffn = m->ffn;
+      ms.eps = c.eps;
+      ms.kv_fp16 = c.kv_fp16;
+      ms.block_size = c.block_size;
+      for (const Layer& Ly : m->L) {
+        ms.w.push_back({Ly.qkv, Ly.o, Ly.gu, Ly.down});
+        ms.in_norm.push_back(Ly.in_norm);
+        ms.post_norm.push_back(Ly.post_norm);
+      }
+      void* plan = nullptr;
+      const int rc = decode_mk_prepare(&plan, ms);
+      if (rc == LUMINA_OK) {
+        m->mk_plan = plan;
+        TRY(dalloc(m, (void**)&m->mk_sync, decode_mk_sync_words(plan) * 4));
+        TRY(dalloc(m, (void**)&m->mk_part, decode_mk_part_floats(m->nh, m->hd, c.max_seq) * 4));
+      } else if (rc != LUMINA_E_UNSUPPORTED) {
+        return rc;
+      }
+    }
+  }
   LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
   if (!fault_flag_ptr()) {
     set_error("model_finalize: fault flag unavailable");
@@ -899,6 +975,7 @@ int lumina_model_free(lumina_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
   if (m->chain_graph) cudaGraphExecDestroy(m->chain_graph);
+  if (m->mk_plan) decode_mk_free(m->mk_plan);
   if (m->ev0) cudaEventDestroy(m->ev0);
   if (m->ev1) cudaEventDestroy(m->ev1);
   if (m->comm) ncclCommDestroy(m->comm);
