@@ -80,22 +80,7 @@ struct TcArgs {
   RopeKV rk;
   int nb;       // live batch rows (<= NB)
   int* fault;
-  // the next packed weight of the decode step (its codes and scales), or
-  // null: the CTAs prefetch it into L2 once their own reads are issued
-  const uint8_t* next[2];
-  unsigned long long next_bytes[2];
 };
-
-// L2 prefetch of [p, p + bytes) (16-byte aligned, bytes % 16 == 0)
-__device__ __forceinline__ void prefetch_l2(const void* p, unsigned long long bytes) {
-  const uint8_t* c = static_cast<const uint8_t*>(p);
-  while (bytes > 0) {
-    const unsigned int n = bytes > (1u << 16) ? (1u << 16) : (unsigned int)bytes;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
-    c += n;
-    bytes -= n;
-  }
-}
 
 template <typename ST>
 __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, float& s1) {
@@ -219,11 +204,6 @@ gemv_tc_kernel(TcArgs a) {
   __shared__ float red[NB * TW];
   __shared__ int ep_blk[NB], ep_off[NB], ep_pos[NB];
 
-  auto unit_span = [&](int u, int& tile, int& p0, int& np) {
-    tile = u / a.UT;
-    p0 = (u - tile * a.UT) * KS;
-    np = min(P - p0, KS);
-  };
   // lane 0: unit j of this warp's run into stage j % TS (two bulk copies
   // completing on the stage's mbarrier); units are issued in order, so the
   // (tile, unit-in-tile) of the next one is tracked, not divided out
@@ -257,28 +237,6 @@ gemv_tc_kernel(TcArgs a) {
   //    before the dependency wait
   if (lane == 0) {
     for (int j = 0; j < min(TS, n_mine); ++j) issue(j);
-    // the rest of this warp's units into L2, so later stages fill at L2
-    // latency (codes of consecutive units of a tile are contiguous)
-    if (n_mine > TS) {
-      // (tile, pair) and (tile, group) orders are the memory orders, so the
-      // units' codes and scales are two contiguous spans
-      int t0, p0a, npa, t1, p0b, npb;
-      unit_span(wu0 + TS, t0, p0a, npa);
-      unit_span(wu1 - 1, t1, p0b, npb);
-      const size_t c0 = (size_t)t0 * P + p0a, c1 = (size_t)t1 * P + p0b + npb;
-      prefetch_l2(a.codes + c0 * 512, (unsigned long long)(c1 - c0) * 512);
-      const size_t g0 = (size_t)t0 * a.ng + (p0a >> a.gsh), g1 = (size_t)t1 * a.ng + ((p0b + npb - 1) >> a.gsh) + 1;
-      prefetch_l2(a.scales + g0 * SG, (unsigned long long)(g1 - g0) * SG);
-    }
-    // then this warp's slice of the next weight of the step
-    const int gw = blockIdx.x * TW + warp, nw = gridDim.x * TW;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      if (!a.next[r]) continue;
-      const unsigned long long chunks = a.next_bytes[r] / 16;
-      const unsigned long long c0 = chunks * gw / nw, c1 = chunks * (gw + 1) / nw;
-      if (c1 > c0) prefetch_l2(a.next[r] + c0 * 16, (c1 - c0) * 16);
-    }
   }
   // norm weights never depend on the previous kernel either
   float wpre[TQ_CH][8];
@@ -456,8 +414,7 @@ int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bo
 }  // namespace
 
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
-                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
-                   const lumina_weight* next) {
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk) {
   if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
@@ -491,14 +448,6 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   if (rk) a.rk = *rk;
   a.nb = batch;
   a.fault = fault;
-  if (next) {
-    const int es_n = next->fp16_scales ? 2 : 4;
-    a.next[0] = next->codes;
-    a.next_bytes[0] = (unsigned long long)next->rows_pad * next->row_bytes / 16 * 16;
-    a.next[1] = next->scales;
-    a.next_bytes[1] = (next->mma ? (unsigned long long)next->rows_pad * next->n_groups * es_n
-                                 : (unsigned long long)next->rows_pad * next->spr) / 16 * 16;
-  }
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
   const int per = (a.T16 + sm_count() - 1) / sm_count();

@@ -335,10 +335,10 @@ int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
 // y = W x (+ epilogue): the fused decode GEMV for 1, 2 or 4 rows, else (or
 // when the shape does not fit it) act_quant + the global-activation GEMV.
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
-             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const lumina_weight* next = nullptr) {
+             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk) {
   if (w->mma) {
     if (n <= 4) {
-      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, next);
+      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
@@ -376,7 +376,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     rk.kv_fp16 = m->c.kv_fp16;
     rk.q_out = m->q_buf;
     rk.row_base = 0;
-    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, Ly.o));
+    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk));
   } else {
     lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
     const int off[3] = {0, qw, qw + kw};
@@ -401,11 +401,11 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(allreduce(m, m->part, (size_t)n * d));
     TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
   } else {
-    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, Ly.gu));
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
-    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr, Ly.down));
+    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr));
   } else {
     TRY(gemv_any(m, Ly.gate, m->x, d, n, Ly.post_norm, m->g_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(gemv_any(m, Ly.up, m->x, d, n, Ly.post_norm, m->u_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
@@ -416,8 +416,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(allreduce(m, m->part, (size_t)n * d));
     TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
   } else {
-    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr,
-                 l + 1 < m->c.n_layer ? m->L[l + 1].qkv : nullptr));
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
   }
   return LUMINA_OK;
 }
@@ -1227,12 +1226,8 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
       const int epis[4] = {EPI_STORE, EPI_STORE, Ly.gu ? EPI_SWIGLU : EPI_STORE, EPI_STORE};
       const int lds[4] = {width, d, m->ffn, d};
       const int ldx[4] = {d, qw, d, m->ffn};
-      const lumina_weight* nxt =
-          l + 1 < m->c.n_layer ? (m->L[l + 1].qkv ? m->L[l + 1].qkv : m->L[l + 1].q) : nullptr;
       for (int i = 0; i < 4; ++i) {
-        // each launch prefetches the next one's weights, as in the decode step
-        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr,
-                     i < 3 ? ws[i + 1] : nxt));
+        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr));
         if (count) {
           ++launches;
           const int out_rows = epis[i] == EPI_SWIGLU ? ws[i]->rows / 2 : ws[i]->rows;

@@ -154,12 +154,9 @@ int gemv_mma_launch(const lumina_weight* w, const float* x, int ldx, int batch, 
 
 // int4 decode GEMV on the tensor pipe (gemv_tc.cu), batch 1, 2 or 4 (3 runs
 // as 4), weights in the fragment layout with group = 64 * 2^k.
-// `next` (may be null): the packed weight the caller runs next; its bytes
-// are prefetched into L2 while this GEMV streams its own.
 // LUMINA_E_UNSUPPORTED when the shape does not fit.
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
-                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
-                   const lumina_weight* next = nullptr);
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk);
 
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);
