@@ -5,7 +5,11 @@
 // cluster takes keys [r*T/CS, (r+1)*T/CS) and streams them through a
 // double-buffered shared-memory ring of ATTNC_CHUNK keys (cp.async, 16
 // bytes per copy; K rows padded by 16 bytes so that lanes reading
-// consecutive keys hit distinct banks), keeping an online softmax: scores
+// consecutive keys hit distinct banks). Only the new row (and q) come from
+// the preceding q/k/v kernel; the key count and block table are fixed for
+// the whole step, so both ring chunks are requested before the dependency
+// wait without the new row, which is read after it. The CTA keeps an online
+// softmax: scores
 // with lanes along keys and two warps per half of the head dimension, the
 // chunk's max / exponentials in one warp, P.V with threads along dimension
 // pairs. The CTAs' (max, sum, unnormalized output) meet in distributed
@@ -46,8 +50,8 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
   const int h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
-  pdl_wait();
-  const int T = P->t_tot;
+  // set before the step (host copy or the previous step's commit kernel)
+  const int T = P->t_tot, knew = P->t_prev;
   const int k0 = (r * T) / CS, k1 = ((r + 1) * T) / CS, nk = k1 - k0;
   const int kvh = h / (nh / nkv);
   const size_t bstride = (size_t)nkv * bs * HD;
@@ -60,13 +64,16 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
   float* oc = po + C::NPH * HD;                                        // [HD] this CTA's output
   float* ml = oc + HD;                                                 // m, l, alpha
   // chunk c's K rows at buf + (c & 1) * BUF, V rows after the K rows
-  auto issue = [&](int c) {
+  // one commit group per call (possibly empty); before the dependency wait
+  // (pre) the new row is left out
+  auto issue = [&](int c, bool pre) {
     uint8_t* ks = buf + (size_t)(c & 1) * C::BUF;
     uint8_t* vs = ks + (size_t)CK * C::KROW;
     const int j0 = k0 + c * CK, n = min(CK, k1 - j0);
     for (int i = tid; i < n * C::CH; i += 128) {
       const int j = i / C::CH, ch = i - j * C::CH;
       const int key = j0 + j;
+      if (pre && key == knew) continue;
       const int blk = block_table[key / bs], off = key % bs;
       const size_t base = (size_t)blk * bstride + ((size_t)kvh * bs + off) * HD;
       const uint8_t* kp = reinterpret_cast<const uint8_t*>(kcache + base) + ch * 16;
@@ -80,7 +87,23 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
   };
 
   const int nchunks = (nk + CK - 1) / CK;
-  if (nchunks > 0) issue(0);
+  issue(0, true);
+  issue(1, true);
+  pdl_wait();
+  // the new row, when it sits in a chunk requested before the wait
+  if (knew >= k0 && knew < k1 && (knew - k0) / CK < 2) {
+    const int j = knew - k0, c = j / CK, jj = j - c * CK;
+    uint8_t* ks = buf + (size_t)(c & 1) * C::BUF;
+    uint8_t* vs = ks + (size_t)CK * C::KROW;
+    const int blk = block_table[knew / bs], off = knew % bs;
+    const size_t base = (size_t)blk * bstride + ((size_t)kvh * bs + off) * HD;
+    for (int ch = tid; ch < C::CH; ch += 128) {
+      *reinterpret_cast<uint4*>(ks + (size_t)jj * C::KROW + ch * 16) =
+          __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(kcache + base) + ch * 16));
+      *reinterpret_cast<uint4*>(vs + (size_t)jj * C::VROW + ch * 16) =
+          __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(vcache + base) + ch * 16));
+    }
+  }
   for (int d = tid; d < HD; d += 128) qs[d] = q[(size_t)h * HD + d];
   if (tid == 0) {
     ml[0] = -INFINITY;
@@ -89,12 +112,7 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
   const int dp = tid % C::DP, kp = tid / C::DP;
   float o0 = 0.f, o1 = 0.f;  // dims 2dp, 2dp+1 over keys of phase kp
   for (int c = 0; c < nchunks; ++c) {
-    if (c + 1 < nchunks) {
-      issue(c + 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // chunk c landed (c + 1 may be in flight)
     __syncthreads();
     const uint8_t* ks = buf + (size_t)(c & 1) * C::BUF;
     const uint8_t* vs = ks + (size_t)CK * C::KROW;
@@ -172,7 +190,10 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
       }
     }
     __syncthreads();  // the buffer of chunk c is free for chunk c + 2
+    if (c + 2 < nchunks) issue(c + 2, false);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   po[kp * HD + 2 * dp] = o0;
   po[kp * HD + 2 * dp + 1] = o1;
   __syncthreads();
