@@ -238,9 +238,9 @@ def peaks():
 
 
 def traffic_ratio():
-    """DRAM bytes / algorithmic bytes of the packed GEMV from the committed
-    ncu summary (profiles/gemv_fused_7b_int4_traffic.json), or None."""
-    p = os.path.join(REPO, "profiles", "gemv_fused_7b_int4_traffic.json")
+    """DRAM bytes / algorithmic bytes of the decode GEMV from the committed
+    ncu summary (profiles/gemv_tc_7b_int4_traffic.json), or None."""
+    p = os.path.join(REPO, "profiles", "gemv_tc_7b_int4_traffic.json")
     try:
         d = json.load(open(p))
         return float(d["dram_bytes"]) / float(d["algorithmic_bytes"]), d.get("source", p)
@@ -248,8 +248,80 @@ def traffic_ratio():
         return None, None
 
 
+# GEMV sweep over the per-layer 7B shapes (out rows N, in cols K) and bit widths
+SWEEP_SHAPES = ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096))
+SWEEP_KINDS = (("int4", 4, 64), ("int3", 3, 64), ("int2", 2, 128), ("binary", 1, 128))
+SWEEP_BATCHES = (1, 4, 16)
+
+
+def sweep_bytes(N, K, bits, group, batch):
+    """Algorithmic bytes of one GEMV call: packed codes + fp16 scales +
+    fp32 activations in + fp32 outputs."""
+    return N * ((K * bits + 7) // 8) + N * (-(-K // group)) * 2 + batch * K * 4 + batch * N * 4
+
+
+def run_sweep(args):
+    """Decode-only GEMV sweep: each bit width x shape x batch through the
+    public lumina_gemv entry point. A set of weight copies larger than 3x the
+    L2 is cycled so every call streams its weights from HBM; the calls are
+    captured in one CUDA graph and timed with CUDA events on its stream.
+    Prints one JSON line per case."""
+    import torch
+    from lumina_b200.cuda import Weight
+    from lumina_b200.packing import to_file_layout
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    os.environ["LUMINA_INT4_LAYOUT"] = "mma"  # int4 in the decode model's tensor-pipe layout
+    rng = np.random.default_rng(0)
+    for kind, bits, group in SWEEP_KINDS:
+        for N, K in SWEEP_SHAPES:
+            ng = -(-K // group)
+            if kind == "binary":
+                blob, pack = rng.integers(0, 256, (N, K // 8), dtype=np.uint8), "none"
+            else:
+                blob, pack, _ = to_file_layout(kind, rng.integers(0, 1 << bits, (N, K), dtype=np.uint8))
+            scales = (np.abs(rng.standard_normal((N, ng))) * 0.02 + 1e-3).astype(np.float16).astype(np.float32)
+            wb = sweep_bytes(N, K, bits, group, 0)
+            copies = max(2, -(-3 * L2_BYTES // wb))
+            ws = [Weight.upload(kind, group, pack, blob, scales, N, K) for _ in range(copies)]
+            reps = max(1, -(-64 // copies))
+            for batch in SWEEP_BATCHES:
+                x = torch.randn(batch, K, device="cuda")
+                y = torch.empty(batch, N, device="cuda")
+                s = torch.cuda.Stream()
+                with torch.cuda.stream(s):
+                    for w in ws:  # first-use setup (attributes, scratch) outside the capture
+                        w.gemv(x.data_ptr(), batch, K, y.data_ptr(), N, s.cuda_stream)
+                    s.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                        for _ in range(reps):
+                            for w in ws:
+                                w.gemv(x.data_ptr(), batch, K, y.data_ptr(), N, s.cuda_stream)
+                    g.replay()
+                    times = []
+                    for _ in range(5):
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(s)
+                        g.replay()
+                        e1.record(s)
+                        e1.synchronize()
+                        times.append(e0.elapsed_time(e1) / (reps * copies))
+                    del g
+                ms = float(np.median(times))
+                b = sweep_bytes(N, K, bits, group, batch)
+                print(json.dumps({"sweep": "gemv", "kind": kind, "group": group, "N": N, "K": K, "batch": batch,
+                                  "us_per_call": ms * 1e3, "bytes_per_call": b, "gbs": b / (ms * 1e-3) / 1e9,
+                                  "frac": b / (ms * 1e-3) / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
+                                  "weight_copies": copies}), flush=True)
+            del ws
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
+    ap.add_argument("--sweep", action="store_true",
+                    help="GEMV sweep over bit widths x 7B shapes x batch 1/4/16 (JSON line per case)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
@@ -265,6 +337,8 @@ def main(argv=None):
         cfg["num_hidden_layers"] = args.layers
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.sweep:
+        return run_sweep(args)
 
     import torch
     import torch.distributed as dist
@@ -355,7 +429,8 @@ def main(argv=None):
                              "frac": achieved / peak, "peak_kind": peak_kind,
                              "traffic": (ratio * per_launch) if ratio else None,
                              "traffic_source": tsrc,
-                             "kernel": "gemv_fused (packed int4 dequant GEMV, 128 launches per token)",
+                             "kernel": "gemv_tc_kernel (tensor-pipe int4 dequant GEMV: one token's 128 "
+                                       "projections, RMSNorm prologues, store / SwiGLU epilogues)",
                              "algorithmic_bytes_per_launch": per_launch, "ms_per_launch": ms_launch},
                 "cpu_baseline": cb,
                 "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
