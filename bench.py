@@ -35,6 +35,10 @@ Besides the device-chained loop the line carries
   * clocks: nvidia-smi samples taken during the timed region.
 
 ``--impl reference`` runs only that CPU path (rank 0; other ranks exit 0).
+``--moe`` measures the same decode on the virtual-MoE variant of the 7B
+shape (every SwiGLU split into 8 routed experts of 1376, top-2; one GPU).
+``--sweep`` prints one line per case of the decode-only GEMV sweep (int4 /
+int3 / int2 / binary x the four 7B projection shapes x batch 1, 4, 16).
 """
 from __future__ import annotations
 
@@ -60,8 +64,13 @@ L2_BYTES = 126 * 2 ** 20
 KV_BYTES_PER_ROW = 32 * 2 * 4096 * 2
 
 
-def workload(cfg, tp):
-    return {"workload": "llama2-7b-shape decoder, Lumina int4 g64 fp16 scales, batch 1, "
+MOE_EXPERTS, MOE_TOP_K = 8, 2
+
+
+def workload(cfg, tp, moe=False):
+    mlp = (f"every SwiGLU split into {MOE_EXPERTS} virtual-MoE experts of "
+           f"{cfg['intermediate_size'] // MOE_EXPERTS}, sigmoid router, top-{MOE_TOP_K}, ") if moe else ""
+    return {"workload": "llama2-7b-shape decoder, " + mlp + "Lumina int4 g64 fp16 scales, batch 1, "
                         "512-token random prompt prefill then greedy decode, fp16 KV paged in 16-token blocks",
             "layers": cfg["num_hidden_layers"], "d_model": cfg["hidden_size"],
             "heads": cfg["num_attention_heads"], "head_dim": cfg["hidden_size"] // cfg["num_attention_heads"],
@@ -328,7 +337,11 @@ def main(argv=None):
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (development only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--moe", action="store_true",
+                    help="the virtual-MoE 7B shape (8 experts x 1376, top-2) instead of the dense model")
     args = ap.parse_args(argv)
+    if args.moe and args.gpus > 1:
+        ap.error("--moe runs on one GPU (virtual-MoE layers are not tensor-parallel)")
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     from lumina_b200 import synthetic
@@ -365,10 +378,11 @@ def main(argv=None):
 
     from lumina_b200.engine import CudaChatModel, make_pick
     max_seq = max(4608, PROMPT + max(args.warmup, args.steps) + 16)
-    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=local)
+    moe = (MOE_EXPERTS, MOE_TOP_K) if args.moe else None
+    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=local, moe=moe)
     t0 = time.perf_counter()
     model = CudaChatModel._from_records(recs, synthetic.hf_cfg(cfg), None, 32, 32, 1e-6, 1e4, local, True,
-                                        max_seq, 512, 16, rank, world)
+                                        max_seq, 512, 16, rank, world, moe_map=recs.moe_map)
     build_s = time.perf_counter() - t0
     model.init_tp()
     try:
@@ -416,21 +430,26 @@ def main(argv=None):
         ratio, tsrc = traffic_ratio()
         kv_mean = PROMPT + args.steps / 2
         tok_bytes = alg_bytes + model.vocab // world * 4096 * 2 + KV_BYTES_PER_ROW // world * kv_mean
+        if args.moe:
+            # the touched experts' gate/up/down codes + fp16 scales, and the fp32 router
+            ie, d = cfg["intermediate_size"] // MOE_EXPERTS, cfg["hidden_size"]
+            tok_bytes += cfg["num_hidden_layers"] * (MOE_TOP_K * 3 * ie * (d // 2 + d // 64 * 2)
+                                                     + MOE_EXPERTS * d * 4)
         cb = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not args.moe:
             model.close()
             cb = cpu_baseline(cfg)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights x int16 activations, int32 dot, f32",
                 "data": "synthetic (seeded N(0,0.02) weights quantized to Lumina int4 g64; random prompt)",
-                "config": workload(cfg, world),
+                "config": workload(cfg, world, args.moe),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_kind": peak_kind,
                              "traffic": (ratio * per_launch) if ratio else None,
                              "traffic_source": tsrc,
-                             "kernel": "gemv_tc_kernel (tensor-pipe int4 dequant GEMV: one token's 128 "
-                                       "projections, RMSNorm prologues, store / SwiGLU epilogues)",
+                             "kernel": f"gemv_tc_kernel (tensor-pipe int4 dequant GEMV: one token's {launches} "
+                                       "packed projections, RMSNorm prologues, store / SwiGLU epilogues)",
                              "algorithmic_bytes_per_launch": per_launch, "ms_per_launch": ms_launch},
                 "cpu_baseline": cb,
                 "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,

@@ -152,6 +152,17 @@ int lumina_model_create(int device, const lumina_model_config* cfg, lumina_model
 int lumina_model_set_weight(lumina_model* m, const char* name, lumina_weight* w);
 int lumina_model_set_tensor(lumina_model* m, const char* name, const float* host,
                             int rows, int cols);
+/* Mark `layer` as a virtual-MoE layer (replaces the per-layer entry of the
+ * .lumina header's "virtual_moe" map that ChatModel reads, chat.py:157-183,
+ * and its routed branch, chat.py:285-299 -> qwen_next.py:31-78 with unit
+ * weights). The layer then takes, instead of gate/up/down_proj:
+ *   "model.layers.L.mlp.experts.gate_up_proj"  packed int4 (experts*2*ie, d)
+ *   "model.layers.L.mlp.experts.down_proj"     packed int4 (experts*ie, d)
+ *   "model.layers.L.mlp.gate.weight"           raw router (experts, d)
+ *   "model.layers.L.mlp.gate_bias"             raw router bias (experts), optional
+ * int4 with groups of 64k, d % 64 == 0, experts <= 64, top_k <= 8; not
+ * under tensor parallelism (LUMINA_E_UNSUPPORTED at finalize). */
+int lumina_model_set_moe(lumina_model* m, int layer, int experts, int ie, int top_k);
 /* Check every tensor is present, allocate KV pages and buffers, build the
  * fused projection layouts. */
 int lumina_model_finalize(lumina_model* m);

@@ -22,6 +22,11 @@ struct Layer {
   lumina_weight *gate = nullptr, *up = nullptr, *down = nullptr;
   lumina_weight *qkv = nullptr, *gu = nullptr;  // fused layouts built at finalize
   float *in_norm = nullptr, *post_norm = nullptr;
+  // virtual-MoE MLP (moe_e > 0): flat experts + router (chat.py:285-299)
+  lumina_weight *moe_gu = nullptr, *moe_down = nullptr;
+  float *router_w = nullptr, *router_b = nullptr;
+  int moe_e = 0, moe_ie = 0, moe_k = 0;
+  int router_rows = 0, router_blen = 0;  // as set, checked against moe_e at finalize
 };
 
 size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -77,6 +82,7 @@ struct lumina_model {
   void* mk_plan = nullptr;                // persistent decode-step kernel (decode_mk.cu), or null
   unsigned int* mk_sync = nullptr;
   float* mk_part = nullptr;
+  MoeScratch moe{};                       // virtual-MoE scratch (null without MoE layers)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int graph_splits = 0;
   bool finalized = false;
@@ -402,6 +408,12 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
   } else {
     TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+  }
+  // 4) rmsnorm -> virtual-MoE MLP (chat.py:284-299), residual in place
+  if (Ly.moe_e) {
+    MoeLayerArgs ma{Ly.moe_gu, Ly.moe_down, Ly.router_w, Ly.router_b, Ly.post_norm, m->c.eps,
+                    Ly.moe_e, Ly.moe_ie, Ly.moe_k, d};
+    return launch_moe(ma, n, m->moe, m->x, s);
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
@@ -756,12 +768,30 @@ int lumina_model_set_weight(lumina_model* m, const char* name, lumina_weight* w)
   else if (what == "mlp.gate_proj.weight") slot = &Ly.gate;
   else if (what == "mlp.up_proj.weight") slot = &Ly.up;
   else if (what == "mlp.down_proj.weight") slot = &Ly.down;
+  else if (what == "mlp.experts.gate_up_proj") slot = &Ly.moe_gu;
+  else if (what == "mlp.experts.down_proj") slot = &Ly.moe_down;
   if (!slot) {
-    set_error("model_set_weight: unknown projection %s (virtual-MoE layers are not built)", name);
+    set_error("model_set_weight: unknown projection %s", name);
     return LUMINA_E_UNSUPPORTED;
   }
   if (*slot) lumina_weight_free(*slot);
   *slot = w;
+  return LUMINA_OK;
+}
+
+int lumina_model_set_moe(lumina_model* m, int layer, int experts, int ie, int top_k) {
+  LUMINA_CHECK_ARG(m, "model_set_moe: null model");
+  LUMINA_CHECK_ARG(!m->finalized, "model_set_moe: model already finalized");
+  LUMINA_CHECK_ARG(layer >= 0 && layer < m->c.n_layer, "model_set_moe: layer %d outside 0..%d", layer,
+                   m->c.n_layer - 1);
+  LUMINA_CHECK_ARG(experts >= 1 && experts <= MOE_MAX_E && ie >= 1 && top_k >= 1 && top_k <= experts &&
+                       top_k <= MOE_MAX_K,
+                   "model_set_moe: experts %d / ie %d / top_k %d outside 1..%d / >= 1 / 1..min(experts, %d)",
+                   experts, ie, top_k, MOE_MAX_E, MOE_MAX_K);
+  Layer& Ly = m->L[layer];
+  Ly.moe_e = experts;
+  Ly.moe_ie = ie;
+  Ly.moe_k = top_k;
   return LUMINA_OK;
 }
 
@@ -807,6 +837,27 @@ int lumina_model_set_tensor(lumina_model* m, const char* name, const float* host
     (what[0] == 'i' ? m->L[l].in_norm : m->L[l].post_norm) = (float*)p;
     return LUMINA_OK;
   }
+  if (parse_layer_name(name, &l, &what) && l >= 0 && l < m->c.n_layer &&
+      (what == "mlp.gate.weight" || what == "mlp.gate_bias")) {
+    // virtual-MoE router (E, d) and its bias (E), kept raw by the converter
+    // and rounded to fp16 with every other tensor (chat.py:140)
+    const bool is_w = what == "mlp.gate.weight";
+    LUMINA_CHECK_ARG(is_w ? cols == m->d : cnt <= (size_t)MOE_MAX_E, "%s: shape (%d, %d) does not fit d_model %d",
+                     name, rows, cols, m->d);
+    std::vector<float> f(cnt);
+    for (size_t i = 0; i < cnt; ++i) f[i] = __half2float(__float2half_rn(host[i]));
+    void* p = nullptr;
+    TRY(dalloc(m, &p, cnt * 4));
+    LUMINA_CUDA_TRY(cudaMemcpy(p, f.data(), cnt * 4, cudaMemcpyHostToDevice));
+    if (is_w) {
+      m->L[l].router_w = (float*)p;
+      m->L[l].router_rows = rows;
+    } else {
+      m->L[l].router_b = (float*)p;
+      m->L[l].router_blen = (int)cnt;
+    }
+    return LUMINA_OK;
+  }
   set_error("model_set_tensor: %s is not a raw tensor this model uses (raw projections are not built)", name);
   return LUMINA_E_UNSUPPORTED;
 }
@@ -829,22 +880,46 @@ int lumina_model_finalize(lumina_model* m) {
     m->head_rows = m->embed_rows;
   }
   const int qw = m->nh * m->hd, kw = m->nkv * m->hd;
+  bool any_moe = false;
+  int moe_k = 1, moe_ie = 1;
   for (int l = 0; l < c.n_layer; ++l) {
     Layer& Ly = m->L[l];
-    if (!Ly.q || !Ly.k || !Ly.v || !Ly.o || !Ly.gate || !Ly.up || !Ly.down || !Ly.in_norm || !Ly.post_norm) {
+    const bool moe = Ly.moe_e > 0;
+    if (!Ly.q || !Ly.k || !Ly.v || !Ly.o || !Ly.in_norm || !Ly.post_norm ||
+        (!moe && (!Ly.gate || !Ly.up || !Ly.down))) {
       set_error("model_finalize: layer %d is missing a tensor", l);
       return LUMINA_E_STATE;
     }
     if (Ly.q->rows != qw || Ly.k->rows != kw || Ly.v->rows != kw || Ly.q->cols != m->d || Ly.o->rows != m->d ||
-        Ly.o->cols != qw || Ly.gate->cols != m->d || Ly.up->rows != Ly.gate->rows || Ly.down->rows != m->d ||
-        Ly.down->cols != Ly.gate->rows) {
+        Ly.o->cols != qw ||
+        (!moe && (Ly.gate->cols != m->d || Ly.up->rows != Ly.gate->rows || Ly.down->rows != m->d ||
+                  Ly.down->cols != Ly.gate->rows))) {
       set_error("model_finalize: layer %d shapes do not match the config", l);
       return LUMINA_E_ARG;
     }
-    if (l == 0) m->ffn = Ly.gate->rows;
-    if (Ly.gate->rows != m->ffn) {
-      set_error("model_finalize: layer %d ffn %d != %d", l, Ly.gate->rows, m->ffn);
-      return LUMINA_E_ARG;
+    if (moe) {
+      // virtual-MoE MLP: one GPU holds every expert (no expert parallelism)
+      if (c.tp_size > 1) {
+        set_error("model_finalize: virtual-MoE layer %d under tensor parallelism is not built", l);
+        return LUMINA_E_UNSUPPORTED;
+      }
+      if (Ly.router_rows != Ly.moe_e || (Ly.router_b && Ly.router_blen != Ly.moe_e)) {
+        set_error("model_finalize: layer %d router has %d rows / %d biases for %d experts", l, Ly.router_rows,
+                  Ly.router_blen, Ly.moe_e);
+        return LUMINA_E_ARG;
+      }
+      MoeLayerArgs ma{Ly.moe_gu, Ly.moe_down, Ly.router_w, Ly.router_b, Ly.post_norm, c.eps,
+                      Ly.moe_e, Ly.moe_ie, Ly.moe_k, m->d};
+      TRY(moe_check(ma));
+      any_moe = true;
+      moe_k = std::max(moe_k, Ly.moe_k);
+      moe_ie = std::max(moe_ie, Ly.moe_ie);
+    } else {
+      if (m->ffn == 0) m->ffn = Ly.gate->rows;
+      if (Ly.gate->rows != m->ffn) {
+        set_error("model_finalize: layer %d ffn %d != %d", l, Ly.gate->rows, m->ffn);
+        return LUMINA_E_ARG;
+      }
     }
     int rc = LUMINA_OK;
     if (compatible(Ly.q, Ly.k) && compatible(Ly.q, Ly.v)) {
@@ -854,6 +929,15 @@ int lumina_model_finalize(lumina_model* m) {
       lumina_weight_free(Ly.k);
       lumina_weight_free(Ly.v);
       Ly.q = Ly.k = Ly.v = Ly.qkv;  // keep non-null for the shape checks; freed once
+    }
+    if (moe) {
+      if (!Ly.o->mma && wants_tc(Ly.o)) {
+        lumina_weight* t = to_fragment_layout(Ly.o, &rc);
+        if (rc) return rc;
+        lumina_weight_free(Ly.o);
+        Ly.o = t;
+      }
+      continue;
     }
     if (compatible(Ly.gate, Ly.up)) {
       Ly.gu = build_gu(Ly.gate, Ly.up, &rc, wants_tc(Ly.gate));
@@ -915,6 +999,15 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
   TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
+  if (any_moe) {
+    TRY(moe_prepare(m->d));
+    TRY(dalloc(m, (void**)&m->moe.h, (size_t)R * m->d * 4));
+    TRY(dalloc(m, (void**)&m->moe.sel, (size_t)R * moe_k * 4));
+    TRY(dalloc(m, (void**)&m->moe.act, (size_t)R * moe_k * moe_ie * 4));
+    TRY(dalloc(m, (void**)&m->moe.part, (size_t)MOE_SPLITS * R * m->d * 4));
+    TRY(dalloc(m, (void**)&m->moe.counters, (size_t)(m->d / 64) * 4));
+    LUMINA_CUDA_TRY(cudaMemset(m->moe.counters, 0, (size_t)(m->d / 64) * 4));
+  }
   {
     // the persistent decode step when LUMINA_MEGAKERNEL=1 and the model fits it
     const char* e = getenv("LUMINA_MEGAKERNEL");
@@ -994,6 +1087,8 @@ int lumina_model_free(lumina_model* m) {
     }
     lumina_weight_free(Ly.o);
     lumina_weight_free(Ly.down);
+    lumina_weight_free(Ly.moe_gu);
+    lumina_weight_free(Ly.moe_down);
   }
   for (void* p : m->allocs) cudaFree(p);
   if (m->P_host) cudaFreeHost(m->P_host);
@@ -1226,7 +1321,8 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
       const int epis[4] = {EPI_STORE, EPI_STORE, Ly.gu ? EPI_SWIGLU : EPI_STORE, EPI_STORE};
       const int lds[4] = {width, d, m->ffn, d};
       const int ldx[4] = {d, qw, d, m->ffn};
-      for (int i = 0; i < 4; ++i) {
+      const int nproj = Ly.moe_e ? 2 : 4;  // a virtual-MoE MLP is not a packed GEMV
+      for (int i = 0; i < nproj; ++i) {
         TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr));
         if (count) {
           ++launches;

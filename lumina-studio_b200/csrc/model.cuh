@@ -110,6 +110,33 @@ size_t decode_mk_part_floats(int nh, int hd, int max_seq);
 int decode_mk_launch(void* plan, const MkRun& r, cudaStream_t s);
 void decode_mk_free(void* plan);
 
+// Virtual-MoE MLP (moe.cu): router + top-k, gate/up + SwiGLU of the picked
+// experts, transposed down projection + residual, in place on x.
+constexpr int MOE_MAX_E = 64;   // experts per layer
+constexpr int MOE_MAX_K = 8;    // top-k
+constexpr int MOE_ROWS = 4;     // batch rows per pass of the expert kernels
+constexpr int MOE_PPC = 32;     // (gate, up) neuron pairs per CTA
+constexpr int MOE_SPLITS = 4;   // neuron ranges of the down projection
+struct MoeLayerArgs {
+  const lumina_weight* gate_up;  // (E*2Ie, d) int4, row-major chunk layout
+  const lumina_weight* down;     // (E*Ie, d)
+  const float* router_w;         // (E, d) fp32 (fp16-rounded values)
+  const float* router_b;         // (E) or null
+  const float* norm_w;           // post-attention RMSNorm weight
+  float eps;
+  int E, Ie, K, d;
+};
+struct MoeScratch {
+  float* h;                 // (rows, d) normalized rows
+  int* sel;                 // (rows, K) picked experts
+  float* act;               // (rows, K, Ie) silu(g) * u
+  float* part;              // (MOE_SPLITS, rows, d) down partials
+  unsigned int* counters;   // d / 64, zero between launches
+};
+int moe_check(const MoeLayerArgs& a);
+int moe_prepare(int d);
+int launch_moe(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s);
+
 int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, int batch, float* y, int ldy,
                       const float* resid, int ldr, cudaStream_t s, unsigned long long* amax = nullptr);
 int launch_gather_rows(const lumina_weight& out, const lumina_weight& s0, const lumina_weight& s1,

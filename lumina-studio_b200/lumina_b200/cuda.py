@@ -84,6 +84,7 @@ SIGNATURES = {
     "lumina_model_create": [_I, ctypes.POINTER(ModelConfig), ctypes.POINTER(_VP)],
     "lumina_model_set_weight": [_VP, ctypes.c_char_p, _VP],
     "lumina_model_set_tensor": [_VP, ctypes.c_char_p, _FP, _I, _I],
+    "lumina_model_set_moe": [_VP, _I, _I, _I, _I],
     "lumina_model_finalize": [_VP],
     "lumina_model_free": [_VP],
     "lumina_nccl_unique_id": [_U8P],

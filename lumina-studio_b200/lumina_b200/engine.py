@@ -21,6 +21,7 @@ There is no CPU path: without the CUDA library these raise ``LuminaError``.
 from __future__ import annotations
 
 import ctypes
+import re
 import time
 
 import numpy as np
@@ -120,6 +121,32 @@ class DeviceKV:
         return self.model.kv_read(lyr, start, n)
 
 
+def moe_map_from_header(header: dict) -> dict:
+    """{layer: entry} from a .lumina header's "virtual_moe" map, whose keys
+    are tensor-name prefixes (serve.py:1357-1366)."""
+    out = {}
+    for pfx, mm in (header.get("virtual_moe") or {}).items():
+        mt = re.search(r"layers\.(\d+)\.", str(pfx))
+        if mt:
+            out[int(mt.group(1))] = mm
+    return out
+
+
+def moe_layers(recs: dict, n_layer: int, moe_map: dict | None) -> dict:
+    """Layers holding virtual-MoE experts -> (experts, ie, top_k), with the
+    reference's rule (chat.py:157-183): an experts tensor without a map
+    entry for its layer is an error."""
+    out = {}
+    for l in range(n_layer):
+        if f"model.layers.{l}.mlp.experts.gate_up_proj" not in recs:
+            continue
+        mm = (moe_map or {}).get(l, (moe_map or {}).get(str(l)))
+        if mm is None:
+            raise KeyError(f"layer {l} has virtual-MoE experts but no virtual_moe header entry (experts/ie/top_k)")
+        out[l] = {"experts": int(mm["experts"]), "ie": int(mm["ie"]), "top_k": int(mm["top_k"])}
+    return out
+
+
 class CudaChatModel:
     """The reference ChatModel (chat.py:106-304) with its decode path on a B200."""
 
@@ -181,11 +208,16 @@ class CudaChatModel:
     def from_lumina(cls, path: str, cfg: dict, tok=None, n_heads: int = 14, n_kv: int = 2,
                     eps: float = 1e-6, theta: float = 1000000.0, device: int = 0,
                     kv_fp16: bool = False, max_seq: int = 4096, max_rows: int = 128,
-                    block_size: int = 16, tp_rank: int = 0, tp_size: int = 1):
+                    block_size: int = 16, tp_rank: int = 0, tp_size: int = 1, moe_map: dict | None = None):
+        """``moe_map`` {layer: {"experts", "ie", "top_k"}} defaults to the
+        file header's "virtual_moe" entries, keyed by layer as
+        serve._api_load_lumina builds it (serve.py:1357-1366)."""
         with LuminaFile(path) as f:
             recs = {n: f.record(n) for n in f.names()}
+            if moe_map is None:
+                moe_map = moe_map_from_header(f.header)
             return cls._from_records(recs, cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16,
-                                     max_seq, max_rows, block_size, tp_rank, tp_size)
+                                     max_seq, max_rows, block_size, tp_rank, tp_size, moe_map=moe_map)
 
     @classmethod
     def from_payloads(cls, payloads: dict, cfg: dict, tok=None, group_size: int = 64, **kw):
@@ -208,22 +240,26 @@ class CudaChatModel:
                                  kw.pop("eps", 1e-6), kw.pop("theta", 1000000.0), kw.pop("device", 0),
                                  kw.pop("kv_fp16", False), kw.pop("max_seq", 4096),
                                  kw.pop("max_rows", 128), kw.pop("block_size", 16),
-                                 kw.pop("tp_rank", 0), kw.pop("tp_size", 1))
+                                 kw.pop("tp_rank", 0), kw.pop("tp_size", 1), moe_map=kw.pop("moe_map", None))
 
     @classmethod
     def _from_records(cls, recs, cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16, max_seq,
-                      max_rows, block_size, tp_rank, tp_size):
+                      max_rows, block_size, tp_rank, tp_size, moe_map=None):
         from . import sharding
         emb = recs["model.embed_tokens.weight"]
         if emb.kind != "raw":
             raise LuminaError(3, "quantized embeddings are not on this path (lumina_convert keeps them raw)")
         d_model = emb.shape[1]
         nl = int(cfg.get("num_hidden_layers", 24))
-        gate0 = recs["model.layers.0.mlp.gate_proj.weight"]
+        moe = moe_layers(recs, nl, moe_map)
+        dense = [l for l in range(nl) if l not in moe]
+        ffn = (recs[f"model.layers.{dense[0]}.mlp.gate_proj.weight"].shape[0] if dense
+               else max(m["ie"] for m in moe.values()))
         head = recs.get("lm_head.weight")
         vocab = (head or emb).shape[0]
         obj = cls._shell(cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16, max_seq, max_rows,
-                         block_size, tp_rank, tp_size, d_model, gate0.shape[0], vocab)
+                         block_size, tp_rank, tp_size, d_model, ffn, vocab)
+        obj.moe = moe
         try:
             obj._set_tensor("model.embed_tokens.weight", emb.data)
             if head is not None:
@@ -234,9 +270,23 @@ class CudaChatModel:
                 p = f"model.layers.{l}."
                 for nm in ("input_layernorm.weight", "post_attention_layernorm.weight"):
                     obj._set_tensor(p + nm, recs[p + nm].data)
+                mlp = ("mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")
+                if l in moe:
+                    if tp_size > 1:
+                        raise LuminaError(4, f"layer {l}: virtual-MoE layers under tensor parallelism are not built")
+                    mc = moe[l]
+                    check(obj.lib.lumina_model_set_moe(obj.h, l, mc["experts"], mc["ie"], mc["top_k"]), obj.lib)
+                    obj._set_tensor(p + "mlp.gate.weight", recs[p + "mlp.gate.weight"].data)
+                    if p + "mlp.gate_bias" in recs:
+                        obj._set_tensor(p + "mlp.gate_bias", recs[p + "mlp.gate_bias"].data)
+                    for nm in ("mlp.experts.gate_up_proj", "mlp.experts.down_proj"):
+                        rec = recs[p + nm]
+                        if rec.kind == "raw":
+                            raise LuminaError(3, f"{p + nm} is stored raw; only packed experts are built")
+                        obj._set_weight(p + nm, upload_record(rec, device))
+                    mlp = ()
                 for nm in ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
-                           "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
-                           "mlp.down_proj.weight"):
+                           "self_attn.o_proj.weight") + mlp:
                     rec = recs[p + nm]
                     if rec.kind == "raw":
                         raise LuminaError(3, f"{p + nm} is stored raw; only packed projections are built")

@@ -58,6 +58,39 @@ def host_weights(cfg: dict, seed: int = 0) -> dict[str, np.ndarray]:
     return w
 
 
+def virtual_moe_weights(cfg: dict, experts: int = 8, top_k: int = 2, seed: int = 0,
+                        router_std: float = 0.02) -> tuple[dict[str, np.ndarray], dict]:
+    """``host_weights`` with every layer's SwiGLU MLP split into ``experts``
+    routed experts, stored flat as the reference's virtual-MoE converter
+    writes them (virtual_moe.py:140-147, 228-235): expert e owns the
+    contiguous neurons [e*Ie, (e+1)*Ie), Ie = ffn / experts;
+    ``experts.gate_up_proj`` (E*2Ie, D) holds its gate rows then its up rows,
+    ``experts.down_proj`` (E*Ie, D) the transposed down columns. The router
+    ``gate.weight`` (E, D) and ``gate_bias`` (E) are N(0, router_std), drawn
+    after the dense weights from seed + 1000. Returns (arrays, virtual_moe
+    header map keyed by tensor prefix, as write_lumina stores it)."""
+    f, d = cfg["intermediate_size"], cfg["hidden_size"]
+    if f % experts:
+        raise ValueError(f"ffn {f} does not split into {experts} equal experts")
+    ie = f // experts
+    w = host_weights(cfg, seed)
+    rng = np.random.default_rng(seed + 1000)
+    meta = {}
+    for l in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{l}.mlp."
+        g = w.pop(p + "gate_proj.weight")
+        u = w.pop(p + "up_proj.weight")
+        dn = w.pop(p + "down_proj.weight")
+        w[p + "experts.gate_up_proj"] = np.concatenate(
+            [np.concatenate([g[e * ie:(e + 1) * ie], u[e * ie:(e + 1) * ie]]) for e in range(experts)])
+        w[p + "experts.down_proj"] = np.ascontiguousarray(
+            np.concatenate([dn[:, e * ie:(e + 1) * ie].T for e in range(experts)]))
+        w[p + "gate.weight"] = (rng.standard_normal((experts, d)) * router_std).astype(np.float32)
+        w[p + "gate_bias"] = (rng.standard_normal(experts) * router_std).astype(np.float32)
+        meta[p] = {"experts": experts, "ie": ie, "top_k": top_k, "router_feat": "raw", "layer": str(l)}
+    return w, meta
+
+
 def prompt_ids(cfg: dict, n: int, seed: int = 0) -> list[int]:
     """Uniform random prompt ids from a seeded generator."""
     rng = np.random.default_rng(seed + 1)
@@ -127,9 +160,34 @@ class QuantizedRecords:
     from its own seed (seed, index in ``tensor_order``) when first asked for
     and is not kept, so a 7B model never sits on the host as a whole."""
 
-    def __init__(self, cfg: dict, bits: int = 4, group: int = 64, seed: int = 0, device: int = 0):
+    def __init__(self, cfg: dict, bits: int = 4, group: int = 64, seed: int = 0, device: int = 0,
+                 moe: tuple[int, int] | None = None):
+        """``moe = (experts, top_k)`` makes every layer a virtual-MoE layer:
+        the MLP's gate/up/down become ``experts.gate_up_proj`` (E*2Ie, D)
+        and ``experts.down_proj`` (E*Ie, D), quantized like the other
+        projections, plus a raw router ``gate.weight`` (E, D) and
+        ``gate_bias`` (E), all N(0, 0.02); ``moe_map`` then holds the
+        per-layer (experts, ie, top_k)."""
         self.cfg, self.bits, self.group, self.seed, self.device = cfg, bits, group, seed, device
-        self.order = {n: (i, s) for i, (n, s) in enumerate(tensor_order(cfg))}
+        order = tensor_order(cfg)
+        self.moe_map = {}
+        if moe:
+            e, k = moe
+            f, d = cfg["intermediate_size"], cfg["hidden_size"]
+            if f % e:
+                raise ValueError(f"ffn {f} does not split into {e} equal experts")
+            ie = f // e
+            out = []
+            for name, shape in order:
+                if ".mlp.gate_proj." in name:
+                    p = name[: -len("gate_proj.weight")]
+                    out += [(p + "experts.gate_up_proj", (e * 2 * ie, d)), (p + "experts.down_proj", (e * ie, d)),
+                            (p + "gate.weight", (e, d)), (p + "gate_bias", (e,))]
+                    self.moe_map[int(name.split(".")[2])] = {"experts": e, "ie": ie, "top_k": k}
+                elif ".mlp.up_proj." not in name and ".mlp.down_proj." not in name:
+                    out.append((name, shape))
+            order = out
+        self.order = {n: (i, s) for i, (n, s) in enumerate(order)}
 
     def __contains__(self, name):
         return name in self.order
@@ -141,12 +199,12 @@ class QuantizedRecords:
         import torch
         from .loader import Record
         idx, shape = self.order[name]
-        if len(shape) == 1:
+        if len(shape) == 1 and not name.endswith("gate_bias"):
             return Record(name, "raw", shape, data=np.ones(shape, np.float32))
         g = torch.Generator(device=f"cuda:{self.device}")
         g.manual_seed(self.seed * 100003 + idx)
         w = torch.randn(shape, generator=g, device=f"cuda:{self.device}", dtype=torch.float32) * 0.02
-        if "embed" in name or "lm_head" in name:
+        if "embed" in name or "lm_head" in name or name.endswith((".gate.weight", "gate_bias")):
             return Record(name, "raw", shape, data=w.cpu().numpy())
         c, s = _quantize_gpu(w, self.bits, self.group)
         packed = _pack_gpu(c, self.bits).contiguous().cpu().numpy().reshape(-1)

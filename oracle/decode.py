@@ -61,7 +61,8 @@ def apply_rope(x, angles):
 
 
 def _sigmoid(x):
-    return 1.0 / (1.0 + np.exp(-x))
+    """qwen_next.py:23-24 (clip to +-40, float32 exponent)."""
+    return 1.0 / (1.0 + np.exp(-np.clip(x, -40, 40).astype(np.float32)))
 
 
 def moe_grouped_forward(h, gate_up, down, router_w, top_k, router_b=None,

@@ -36,3 +36,23 @@ def tiny_file(tmp_path_factory):
     path = str(tmp_path_factory.mktemp("tiny") / "tiny.lumina")
     write_lumina(path, payloads, name="tiny", rung="int4", group_size=64)
     return path
+
+
+MOE_GOLDEN = {"experts": 8, "top_k": 2, "router_std": 0.1}  # tests/golden/make_golden.py MOE
+
+
+@pytest.fixture(scope="session")
+def tiny_moe_file(tmp_path_factory):
+    """The tiny model with every MLP split into 8 routed experts (top-2),
+    quantized by the oracle and written by the oracle writer with the
+    virtual_moe header entry the reference's writer stores."""
+    from oracle.quant import convert_arrays
+    from oracle.lumina_format import write_lumina
+    from lumina_b200 import synthetic
+    w, meta = synthetic.virtual_moe_weights(synthetic.TINY, MOE_GOLDEN["experts"], MOE_GOLDEN["top_k"], seed=0,
+                                            router_std=MOE_GOLDEN["router_std"])
+    payloads = convert_arrays(w, "int4", group_size=64, fp16_scales=True)
+    path = str(tmp_path_factory.mktemp("tiny_moe") / "tiny_moe.lumina")
+    write_lumina(path, payloads, name="tiny_moe", rung="int4", group_size=64,
+                 extra_header={"virtual_moe": meta})
+    return path

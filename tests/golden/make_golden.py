@@ -282,19 +282,117 @@ def make_tops(ref):
     print("tops KAT written")
 
 
+MOE = {"experts": 8, "top_k": 2, "router_std": 0.1}  # tiny shape, every layer routed
+
+
+def make_moe(ref, tmp):
+    """Virtual-MoE decode (chat.py:285-299 -> qwen_next.moe_grouped_forward):
+    the tiny model with every SwiGLU split into 8 experts (top-2), quantized
+    by the reference's converter, written with its virtual_moe header entry,
+    read back by the reference loader and decoded by ChatModel with the
+    moe_map serve._api_load_lumina builds. Records the prefill and
+    teacher-forced logits, 16 greedy tokens, the quantized-tensor hashes and
+    the smallest top-k score gap over every routing decision (so the device
+    test knows its routing margin)."""
+    import json
+    import re
+    import struct
+    from lumina_convert import convert_arrays, write_lumina
+    from lumina_framework import qwen_next
+    from lumina_framework.adapters import load_model
+    from lumina_framework.chat import ChatModel, generate
+
+    cfg = synthetic.TINY
+    w, meta = synthetic.virtual_moe_weights(cfg, MOE["experts"], MOE["top_k"], seed=0,
+                                            router_std=MOE["router_std"])
+    payloads, stats = convert_arrays(w, {}, "int4", group_size=64)
+    fixed, hashes = {}, {}
+    for name, (kind, payload) in payloads.items():
+        if kind == "raw":
+            fixed[name] = (kind, payload)
+            continue
+        codes, scales = payload
+        scales = np.asarray(scales, dtype=np.float32).astype(np.float16).astype(np.float32)
+        fixed[name] = (kind, (codes, scales))
+        hashes[name] = sha(np.asarray(codes).astype(np.uint8), scales)
+    path = os.path.join(tmp, "tiny_moe.lumina")
+    write_lumina(path, fixed, stats, "tiny_moe", "int4", group_size=64, moe_meta=meta)
+    raw = open(path, "rb").read()
+    hlen = struct.unpack("<IIQ", raw[:16])[2]
+    hdr = json.loads(raw[16:16 + hlen])
+    moe_map = {}
+    for pfx, mm in (hdr.get("virtual_moe") or {}).items():  # serve.py:1357-1366
+        mt = re.search(r"layers\.(\d+)\.", str(pfx))
+        if mt:
+            moe_map[int(mt.group(1))] = mm
+    lm = load_model(path)
+    model = ChatModel.from_tensors(lm.tensors.tensors, synthetic.hf_cfg(cfg), StubTok(),
+                                   theta=cfg["rope_theta"], moe_map=moe_map)
+    assert sorted(model.moe) == list(range(cfg["num_hidden_layers"]))
+
+    gaps = []
+    orig = qwen_next.moe_grouped_forward
+
+    def probe(h, gate_up, down, router_w, top_k, **kw):
+        lg = h @ router_w.T
+        if kw.get("router_b") is not None:
+            lg = lg + np.asarray(kw["router_b"], dtype=np.float32)
+        sc = np.sort(qwen_next._sigmoid(lg), axis=1)[:, ::-1]
+        gaps.append(float((sc[:, top_k - 1] - sc[:, top_k]).min()))
+        return orig(h, gate_up, down, router_w, top_k, **kw)
+
+    qwen_next.moe_grouped_forward = probe
+    try:
+        prompt = synthetic.prompt_ids(cfg, 24, seed=0)
+        emb = model.t["model.embed_tokens.weight"].astype(np.float32)
+        head_t = model.head.T.astype(np.float32)
+        cache = {}
+        h = emb[np.array(prompt)]
+        for lyr in range(model.n_layer):
+            h = model._layer(h, lyr, cache, 0)
+        out = {"prompt": np.array(prompt), "logits_prefill_last": (h[-1:] @ head_t)[0].astype(np.float32)}
+        pos = len(prompt)
+        forced = [int(t) for t in np.random.default_rng(9).integers(0, cfg["vocab_size"], 8)]
+        for s, tk in enumerate(forced):
+            hh = emb[[tk]]
+            for lyr in range(model.n_layer):
+                hh = model._layer(hh, lyr, cache, pos)
+            pos += 1
+            if s in (0, 7):
+                out[f"logits_step{s}"] = (hh @ head_t)[0].astype(np.float32)
+        r = generate(model, prompt, max_tokens=16, rng=np.random.default_rng(0))
+    finally:
+        qwen_next.moe_grouped_forward = orig
+    out.update({"forced": np.array(forced), "tokens": np.array(r["tokens"]),
+                "min_route_gap": np.array(min(gaps)),
+                "moe": np.array([MOE["experts"], MOE["top_k"]]), "router_std": np.array(MOE["router_std"]),
+                "quant_sha_names": np.array(sorted(hashes)),
+                "quant_sha": np.array([hashes[k] for k in sorted(hashes)])})
+    np.savez_compressed(os.path.join(HERE, "tiny_moe.npz"), **out)
+    print("moe tokens[:8]", r["tokens"][:8], "min route gap %.3g" % min(gaps))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=("format", "tiny", "tops", "moe"), default=None,
+                    help="regenerate one fixture family (tiny includes the EAGLE fixture)")
     args = ap.parse_args()
     ref = args.reference
     os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba_"))
     sys.path.insert(0, os.path.join(ref, "src"))
     sys.path.insert(0, os.path.join(ref, "scripts"))
+    want = (lambda k: args.only in (None, k))  # noqa: E731
     with tempfile.TemporaryDirectory() as tmp:
-        make_format(ref, tmp)
-        model, prompt = make_tiny(ref, tmp)
-        make_eagle(ref, model, prompt)
-        make_tops(ref)
+        if want("format"):
+            make_format(ref, tmp)
+        if want("tiny"):
+            model, prompt = make_tiny(ref, tmp)
+            make_eagle(ref, model, prompt)
+        if want("tops"):
+            make_tops(ref)
+        if want("moe"):
+            make_moe(ref, tmp)
 
 
 if __name__ == "__main__":

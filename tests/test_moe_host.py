@@ -1,0 +1,44 @@
+"""Host-side logic of the virtual-MoE path (CPU): the header map, the
+layer detection rule, and the synthetic expert layout, which with every
+expert picked reproduces the dense SwiGLU it was split from
+(virtual_moe.py:140-147; qwen_next.py:31-78 with unit weights)."""
+import numpy as np
+import pytest
+
+from lumina_b200 import synthetic
+from lumina_b200.engine import moe_layers, moe_map_from_header
+from oracle.decode import moe_grouped_forward
+
+
+def test_header_map_is_keyed_by_layer():
+    hdr = {"virtual_moe": {"model.layers.2.mlp.": {"experts": 8, "ie": 86, "top_k": 2},
+                           "no_layer_here": {"experts": 1, "ie": 1, "top_k": 1}}}
+    assert moe_map_from_header(hdr) == {2: {"experts": 8, "ie": 86, "top_k": 2}}
+    assert moe_map_from_header({}) == {}
+
+
+def test_experts_without_a_map_entry_are_an_error():
+    recs = {"model.layers.1.mlp.experts.gate_up_proj": object()}
+    with pytest.raises(KeyError, match="layer 1"):
+        moe_layers(recs, 2, {})
+    got = moe_layers(recs, 2, {"1": {"experts": 4, "ie": 10, "top_k": 2, "router_feat": "abs"}})
+    assert got == {1: {"experts": 4, "ie": 10, "top_k": 2}}  # router_feat is dropped, as chat.py:181-183
+
+
+def test_all_experts_reproduce_the_dense_mlp():
+    cfg = dict(synthetic.TINY, num_hidden_layers=1)
+    dense = synthetic.host_weights(cfg, seed=3)
+    w, meta = synthetic.virtual_moe_weights(cfg, experts=8, top_k=8, seed=3)
+    p = "model.layers.0.mlp."
+    assert meta[p] == {"experts": 8, "ie": 86, "top_k": 8, "router_feat": "raw", "layer": "0"}
+    assert w[p + "experts.gate_up_proj"].shape == (8 * 2 * 86, 256)
+    assert w[p + "experts.down_proj"].shape == (8 * 86, 256)
+    h = np.random.default_rng(0).standard_normal((3, 256)).astype(np.float32)
+    g = h @ dense[p + "gate_proj.weight"].T
+    u = h @ dense[p + "up_proj.weight"].T
+    ref = ((g / (1.0 + np.exp(-np.clip(g, -40, 40)))) * u) @ dense[p + "down_proj.weight"].T
+    out, info = moe_grouped_forward(h, w[p + "experts.gate_up_proj"].reshape(8, 172, 256),
+                                    w[p + "experts.down_proj"].reshape(8, 86, 256), w[p + "gate.weight"], 8,
+                                    router_b=w[p + "gate_bias"])
+    assert sorted(info["experts"][0].tolist()) == list(range(8))
+    np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-6)

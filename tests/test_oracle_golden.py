@@ -202,3 +202,53 @@ def test_tops_known_answers(golden):
     assert np.array_equal(xq, k["repack_xq"]) and np.array_equal(xs, k["repack_xs"])
     S, s, x = k["bin_S"], k["bin_s"], k["bin_x"]
     np.testing.assert_allclose(x @ (S.astype(np.float32) * s[:, None]).T, k["bin_y"], rtol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# virtual MoE (chat.py:285-299 -> qwen_next.py:31-78), tests/golden/tiny_moe.npz
+# ---------------------------------------------------------------------------
+def test_moe_quantization_matches_reference(golden):
+    from conftest import MOE_GOLDEN
+    g = golden("tiny_moe.npz")
+    assert [int(v) for v in g["moe"]] == [MOE_GOLDEN["experts"], MOE_GOLDEN["top_k"]]
+    assert float(g["router_std"]) == MOE_GOLDEN["router_std"]
+    w, _ = synthetic.virtual_moe_weights(synthetic.TINY, MOE_GOLDEN["experts"], MOE_GOLDEN["top_k"], seed=0,
+                                         router_std=MOE_GOLDEN["router_std"])
+    payloads = quant.convert_arrays(w, "int4", group_size=64, fp16_scales=True)
+    names = [str(n) for n in g["quant_sha_names"]]
+    assert names == sorted(n for n, (k, _) in payloads.items() if k != "raw")
+    assert "model.layers.0.mlp.experts.gate_up_proj" in names and "model.layers.0.mlp.gate.weight" not in names
+    for n, h in zip(names, g["quant_sha"]):
+        codes, scales = payloads[n][1]
+        assert _sha(codes.astype(np.uint8), scales) == str(h), n
+
+
+@pytest.fixture(scope="module")
+def tiny_moe_model(tiny_moe_file):
+    from lumina_b200.engine import moe_map_from_header
+    hdr, _ = lf.read_header(tiny_moe_file)
+    return OracleModel(lf.load_dequant(tiny_moe_file), synthetic.hf_cfg(synthetic.TINY),
+                       theta=synthetic.TINY["rope_theta"], moe_map=moe_map_from_header(hdr))
+
+
+def test_moe_oracle_matches_reference(golden, tiny_moe_model):
+    g = golden("tiny_moe.npz")
+    m = tiny_moe_model
+    assert sorted(m.moe) == list(range(synthetic.TINY["num_hidden_layers"]))
+    prompt = [int(t) for t in g["prompt"]]
+    toks, logits, _ = generate(m, prompt, 16, return_logits=True)
+    assert toks == [int(t) for t in g["tokens"]]
+    np.testing.assert_allclose(logits[0], g["logits_prefill_last"], rtol=1e-5, atol=1e-7)
+    emb, head = m.embed(), m.head_t()
+    cache = {}
+    h = emb[np.array(prompt)]
+    for lyr in range(m.n_layer):
+        h = m.layer(h, lyr, cache, 0)
+    pos = h.shape[0]
+    for s, tk in enumerate(int(t) for t in g["forced"]):
+        hh = emb[[tk]]
+        for lyr in range(m.n_layer):
+            hh = m.layer(hh, lyr, cache, pos)
+        pos += 1
+        if f"logits_step{s}" in g:
+            np.testing.assert_allclose((hh @ head)[0], g[f"logits_step{s}"], rtol=1e-5, atol=1e-7)
