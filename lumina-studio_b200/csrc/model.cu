@@ -1002,9 +1002,9 @@ int lumina_model_finalize(lumina_model* m) {
   if (any_moe) {
     TRY(moe_prepare(m->d));
     TRY(dalloc(m, (void**)&m->moe.h, (size_t)R * m->d * 4));
-    TRY(dalloc(m, (void**)&m->moe.sel, (size_t)R * moe_k * 4));
+    TRY(dalloc(m, (void**)&m->moe.score, (size_t)R * MOE_MAX_E * 4));
     TRY(dalloc(m, (void**)&m->moe.act, (size_t)R * moe_k * moe_ie * 4));
-    TRY(dalloc(m, (void**)&m->moe.part, (size_t)MOE_SPLITS * R * m->d * 4));
+    TRY(dalloc(m, (void**)&m->moe.part, moe_part_rows(R) * m->d * 4));
     TRY(dalloc(m, (void**)&m->moe.counters, (size_t)(m->d / 64) * 4));
     LUMINA_CUDA_TRY(cudaMemset(m->moe.counters, 0, (size_t)(m->d / 64) * 4));
   }

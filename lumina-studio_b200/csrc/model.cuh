@@ -110,13 +110,20 @@ size_t decode_mk_part_floats(int nh, int hd, int max_seq);
 int decode_mk_launch(void* plan, const MkRun& r, cudaStream_t s);
 void decode_mk_free(void* plan);
 
-// Virtual-MoE MLP (moe.cu): router + top-k, gate/up + SwiGLU of the picked
+// Virtual-MoE MLP (moe.cu): router scores, gate/up + SwiGLU of the picked
 // experts, transposed down projection + residual, in place on x.
-constexpr int MOE_MAX_E = 64;   // experts per layer
-constexpr int MOE_MAX_K = 8;    // top-k
-constexpr int MOE_ROWS = 4;     // batch rows per pass of the expert kernels
-constexpr int MOE_PPC = 32;     // (gate, up) neuron pairs per CTA
-constexpr int MOE_SPLITS = 4;   // neuron ranges of the down projection
+constexpr int MOE_MAX_E = 64;      // experts per layer
+constexpr int MOE_MAX_K = 8;       // top-k
+constexpr int MOE_ROWS = 4;        // batch rows per pass of the expert kernels
+constexpr int MOE_PPC = 8;         // (gate, up) neuron pairs per CTA: one per warp
+constexpr int MOE_SPLITS_MAX = 16; // neuron ranges of the down projection
+inline int moe_splits(int n) { return n <= 32 ? MOE_SPLITS_MAX : 4; }
+// rows of down partials a forward of up to max_rows rows needs
+inline size_t moe_part_rows(int max_rows) {
+  const int a = max_rows < 32 ? max_rows : 32;
+  const size_t p1 = (size_t)moe_splits(a) * a, p2 = (size_t)moe_splits(max_rows) * max_rows;
+  return p1 > p2 ? p1 : p2;
+}
 struct MoeLayerArgs {
   const lumina_weight* gate_up;  // (E*2Ie, d) int4, row-major chunk layout
   const lumina_weight* down;     // (E*Ie, d)
@@ -128,9 +135,9 @@ struct MoeLayerArgs {
 };
 struct MoeScratch {
   float* h;                 // (rows, d) normalized rows
-  int* sel;                 // (rows, K) picked experts
+  float* score;             // (rows, MOE_MAX_E) router scores
   float* act;               // (rows, K, Ie) silu(g) * u
-  float* part;              // (MOE_SPLITS, rows, d) down partials
+  float* part;              // (moe_part_rows(max_rows), d) down partials
   unsigned int* counters;   // d / 64, zero between launches
 };
 int moe_check(const MoeLayerArgs& a);

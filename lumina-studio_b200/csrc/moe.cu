@@ -14,34 +14,37 @@
 // plus the router (E, D) and its bias (E), raw tensors rounded to fp16 as
 // ChatModel rounds every tensor (chat.py:140).
 //
-// Kernels (one launch each per layer, grids fixed by the shapes so that a
-// captured decode graph replays them):
-//  * moe_route_kernel, one CTA per row: RMSNorm (chat.py:284, the same fp32
-//    arithmetic as the GEMV prologues), router logits h . router[e] + b[e],
-//    sigmoid scores with the +-40 clip (qwen_next.py:23-24), top-k by
-//    descending score with ties to the lower expert index (numpy's argsort
-//    of -scores, qwen_next.py:63, is an insertion sort for E <= 16 and so
-//    keeps index order on ties).
-//  * moe_gu_kernel, grid (expert, tile of MOE_PPC neuron pairs): rows are
-//    taken in passes of MOE_ROWS; a CTA whose expert no row of the pass
-//    picked skips the pass without touching its weights, so only the
-//    touched experts stream from HBM. A warp owns one (gate, up) row pair
-//    at a time, each lane a 16-byte chunk (32 codes) per row; the codes are
-//    widened to fp32 once and dotted against every picking row held in
-//    shared memory:
+// Kernels (one launch each per layer, grids fixed by the row count so that
+// a captured decode graph replays them):
+//  * moe_route_kernel, grid (row, expert): the row's RMSNorm (chat.py:284,
+//    the same fp32 arithmetic as the GEMV prologues) and its router logit
+//    h . router[e] + b[e] as a sigmoid score with the +-40 clip
+//    (qwen_next.py:23-24). One CTA per (row, expert) keeps every load of the
+//    row and the router row in flight at once.
+//  * The expert kernels take rows in passes of up to MOE_ROWS and derive the
+//    picks of a pass from the scores themselves: top-k by descending score
+//    (qwen_next.py:63, np.argsort(-scores)[:, :k]) with exact ties to the
+//    lower expert index (numpy's sort is not stable, so the reference orders
+//    exact ties by its sort algorithm; both pick the same score values), and
+//    the distinct experts the pass touches.
+//  * moe_gu_kernel, grid (touched-expert slot, tile of MOE_PPC neuron pairs):
+//    CTA x works for the x-th expert the pass touches, so only touched
+//    experts stream from HBM and, at decode, every CTA has work. One warp
+//    per (gate, up) row pair, each lane a 16-byte chunk (32 codes) per row;
+//    the codes are widened to fp32 once and dotted against every picking row
+//    held in shared memory:
 //      sum_k h_k * level(c_k) = s/15 * (2 * sum h_k c_k - 15 * sum h_k)
 //    per 32-column chunk (one scale; level(c) = (2c - 15)/15,
 //    adapters/lumina.py:135-139), then silu(g) * u with the +-40 clip
 //    (qwen_next.py:71-72).
-//  * moe_down_kernel, grid (64-column slice, MOE_SPLITS neuron ranges): 8
-//    lanes decode 8 columns each of one down row, so a warp covers four rows
-//    of a slice per load; a lane accumulates its 8 columns for up to
-//    MOE_ROWS batch rows. Partial sums reduce in a fixed order -- shuffles
-//    over the four row lanes, the 8 warps in shared memory, then the splits
-//    in index order by the CTA that finishes a slice last (found with a
-//    per-slice counter it resets for the next launch) -- which also adds the
-//    residual (chat.py:299: x + d). Results therefore do not depend on CTA
-//    timing.
+//  * moe_down_kernel, grid (64-column slice, neuron range): 8 lanes decode 8
+//    columns each of one down row, so a warp covers four rows of a slice per
+//    load; a lane accumulates its 8 columns for every row of the pass.
+//    Partial sums reduce in a fixed order -- shuffles over the four row
+//    lanes, the 8 warps in shared memory, then the neuron ranges in index
+//    order by the CTA that finishes a slice last (found with a per-slice
+//    counter it resets for the next launch) -- which also adds the residual
+//    (chat.py:299: x + d). Results therefore do not depend on CTA timing.
 #include "model.cuh"
 
 namespace lumina {
@@ -55,20 +58,6 @@ constexpr int MOE_WARPS = MOE_THREADS / 32;
 // of 2^23 and the exponent bias is subtracted again (exact for 0..255).
 __device__ __forceinline__ float byte_to_float(uint32_t v, uint32_t j) {
   return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | j)) - 8388608.f;
-}
-
-// the 32 int4 codes of one 16-byte chunk as floats, column order
-__device__ __forceinline__ void decode_chunk(const uint4& v, float (&c)[32]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t lo = w[q] & 0x0F0F0F0Fu, hi = (w[q] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c[8 * q + 2 * j] = byte_to_float(lo, j);
-      c[8 * q + 2 * j + 1] = byte_to_float(hi, j);
-    }
-  }
 }
 
 template <typename ST>
@@ -86,162 +75,231 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // ---------------------------------------------------------------------------
 // router
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(MOE_THREADS)
+constexpr int ROUTE_THREADS = 128;
+
+__device__ __forceinline__ float block_sum_route(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();  // red is free again
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < ROUTE_THREADS / 32; ++i) t += red[i];
+  return t;
+}
+
+// CTA (row r, expert e): the row's RMSNorm and its router logit for e, as
+// a sigmoid score. Every CTA of a row computes the same norm factor (same
+// loads, same order), so h is one value everywhere; expert 0's CTA stores it.
+__global__ void __launch_bounds__(ROUTE_THREADS)
 moe_route_kernel(const float* __restrict__ x, int d, const float* __restrict__ norm_w, float eps,
-                 const float* __restrict__ rw, const float* __restrict__ rb, int E, int K, float* __restrict__ h,
-                 int* __restrict__ sel) {
-  extern __shared__ float hs[];  // d floats
-  __shared__ float red[MOE_WARPS];
-  __shared__ float score[MOE_MAX_E];
-  const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float* xr = x + (size_t)r * d;
+                 const float* __restrict__ rw, const float* __restrict__ rb, int E, float* __restrict__ h,
+                 float* __restrict__ score) {
+  __shared__ float red[ROUTE_THREADS / 32];
+  const int r = blockIdx.x, e = blockIdx.y;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * d);
+  const float4* nw = reinterpret_cast<const float4*>(norm_w);
+  const float4* wr = reinterpret_cast<const float4*>(rw + (size_t)e * d);
+  const int d4 = d >> 2;
   // chat.py:63-66: x / sqrt(mean(x^2) + eps) * w, fp32
   float ss = 0.f;
-  for (int k = threadIdx.x; k < d; k += MOE_THREADS) ss = fmaf(xr[k], xr[k], ss);
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < MOE_WARPS; ++i) tot += red[i];
-  const float inv = 1.0f / sqrtf(tot / (float)d + eps);
-  for (int k = threadIdx.x; k < d; k += MOE_THREADS) {
-    const float v = (xr[k] * inv) * norm_w[k];
-    hs[k] = v;
-    h[(size_t)r * d + k] = v;
+#pragma unroll 8
+  for (int k = threadIdx.x; k < d4; k += ROUTE_THREADS) {
+    const float4 v = xr[k];
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
   }
-  __syncthreads();
-  // logits = h @ router^T (+ bias), sigmoid scores (qwen_next.py:57-61)
-  for (int e = warp; e < E; e += MOE_WARPS) {
-    const float* w = rw + (size_t)e * d;
-    float acc = 0.f;
-    for (int k = lane; k < d; k += 32) acc = fmaf(hs[k], w[k], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      const float lg = acc + (rb ? rb[e] : 0.f);
-      score[e] = 1.0f / (1.0f + expf(-fminf(fmaxf(lg, -40.f), 40.f)));
+  const float inv = 1.0f / sqrtf(block_sum_route(ss, red) / (float)d + eps);
+  // logit = h . router[e] (+ bias), score = sigmoid with the +-40 clip (qwen_next.py:23-24, 57-61)
+  float acc = 0.f;
+#pragma unroll 8
+  for (int k = threadIdx.x; k < d4; k += ROUTE_THREADS) {
+    const float4 v = xr[k], w = nw[k], q = wr[k];
+    float4 hv;
+    hv.x = (v.x * inv) * w.x;
+    hv.y = (v.y * inv) * w.y;
+    hv.z = (v.z * inv) * w.z;
+    hv.w = (v.w * inv) * w.w;
+    acc = fmaf(hv.x, q.x, acc);
+    acc = fmaf(hv.y, q.y, acc);
+    acc = fmaf(hv.z, q.z, acc);
+    acc = fmaf(hv.w, q.w, acc);
+    if (e == 0) reinterpret_cast<float4*>(h + (size_t)r * d)[k] = hv;
+  }
+  const float lg = block_sum_route(acc, red) + (rb ? rb[e] : 0.f);
+  if (threadIdx.x == 0) score[(size_t)r * MOE_MAX_E + e] = 1.0f / (1.0f + expf(-fminf(fmaxf(lg, -40.f), 40.f)));
+}
+
+// ---------------------------------------------------------------------------
+// the picks of a pass of rows, shared by the expert kernels
+// ---------------------------------------------------------------------------
+// top-k of a row by descending score (np.argsort(-scores)[:, :k],
+// qwen_next.py:63), exact ties to the lower expert index
+__device__ __forceinline__ void topk_row(const float* sc, int E, int K, int* out) {
+  unsigned long long taken = 0ull;
+  for (int j = 0; j < K; ++j) {
+    int best = -1;
+    float bv = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const float v = sc[e];
+      if (!((taken >> e) & 1ull) && (best < 0 || v > bv)) {
+        best = e;
+        bv = v;
+      }
     }
+    taken |= 1ull << best;
+    out[j] = best;
   }
-  __syncthreads();
+}
+
+// Rows r0 .. r0+pr-1: their picks, and the distinct experts they touch in
+// ascending order (thread 0 fills the shared tables).
+struct PassPicks {
+  int pick[MOE_ROWS][MOE_MAX_K];
+  int touched[MOE_MAX_E];
+  int nt;
+};
+
+__device__ __forceinline__ void pass_picks(const float* __restrict__ score, int r0, int pr, int E, int K,
+                                           PassPicks& pp) {
   if (threadIdx.x == 0) {
-    unsigned long long taken = 0ull;
-    for (int j = 0; j < K; ++j) {
-      int best = -1;
-      for (int e = 0; e < E; ++e)
-        if (!((taken >> e) & 1ull) && (best < 0 || score[e] > score[best])) best = e;
-      taken |= 1ull << best;
-      sel[r * K + j] = best;
+    unsigned long long used = 0ull;
+    for (int q = 0; q < pr; ++q) {
+      topk_row(score + (size_t)(r0 + q) * MOE_MAX_E, E, K, pp.pick[q]);
+      for (int j = 0; j < K; ++j) used |= 1ull << pp.pick[q][j];
     }
+    int nt = 0;
+    for (int e = 0; e < E; ++e)
+      if ((used >> e) & 1ull) pp.touched[nt++] = e;
+    pp.nt = nt;
   }
+  __syncthreads();
+}
+
+// slot of expert e among row q's picks, or -1
+__device__ __forceinline__ int slot_of(const PassPicks& pp, int q, int K, int e) {
+  for (int j = 0; j < K; ++j)
+    if (pp.pick[q][j] == e) return j;
+  return -1;
 }
 
 // ---------------------------------------------------------------------------
 // gate/up of the picked experts + SwiGLU
 // ---------------------------------------------------------------------------
-// slot of expert e in row r's picks, or -1
-__device__ __forceinline__ int pick_slot(const int* sel, int r, int K, int e) {
-  for (int j = 0; j < K; ++j)
-    if (sel[r * K + j] == e) return j;
-  return -1;
-}
-
-template <typename ST>
-__global__ void __launch_bounds__(MOE_THREADS)
-moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, const int* __restrict__ sel, int K,
-              int Ie, float* __restrict__ act) {
+// grid (touched-expert slot x, pair tile): in each pass of PR rows, CTA x
+// works for the x-th distinct expert the pass touches (if any); one (gate,
+// up) row pair per warp. PR = 1 (decode) keeps registers low enough for
+// several CTAs per SM.
+template <typename ST, int PR>
+__global__ void __launch_bounds__(MOE_THREADS, PR == 1 ? 3 : 1)
+moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, const float* __restrict__ score,
+              int E, int K, int Ie, float* __restrict__ act) {
   extern __shared__ __align__(16) float sm[];
-  // hsw: MOE_ROWS rows of h, 4 pad floats after every 32 (conflict-free
-  // 16-byte reads when lanes take consecutive chunks); hsum: per row and chunk
+  // hsw: PR rows of h, 4 pad floats after every 32 (conflict-free 16-byte
+  // reads when lanes take consecutive chunks); hsum: per row and chunk
   const int nch = d >> 5, ldh = d + (d >> 3);
   float* hsw = sm;
-  float* hsum = sm + MOE_ROWS * ldh;
-  __shared__ int slot[MOE_ROWS];
-  const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int p0 = blockIdx.y * MOE_PPC;
-  for (int r0 = 0; r0 < n; r0 += MOE_ROWS) {
-    __syncthreads();  // the previous pass is done with slot / hsw
-    if (threadIdx.x < MOE_ROWS) {
-      const int r = r0 + threadIdx.x;
-      slot[threadIdx.x] = r < n ? pick_slot(sel, r, K, e) : -1;
-    }
-    __syncthreads();
-    int sl[MOE_ROWS];
-    bool any = false;
+  float* hsum = sm + PR * ldh;
+  __shared__ PassPicks pp;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int i = blockIdx.y * MOE_PPC + warp;  // this warp's neuron pair
+  for (int r0 = 0; r0 < n; r0 += PR) {
+    const int rows = min(PR, n - r0);
+    __syncthreads();  // the previous pass is done with pp / hsw
+    pass_picks(score, r0, rows, E, K, pp);
+    if ((int)blockIdx.x >= pp.nt) continue;
+    const int e = pp.touched[blockIdx.x];
+    int sl[PR];
 #pragma unroll
-    for (int q = 0; q < MOE_ROWS; ++q) {
-      sl[q] = slot[q];
-      any |= sl[q] >= 0;
-    }
-    if (!any) continue;
+    for (int q = 0; q < PR; ++q) sl[q] = q < rows ? slot_of(pp, q, K, e) : -1;
 #pragma unroll
-    for (int q = 0; q < MOE_ROWS; ++q) {
+    for (int q = 0; q < PR; ++q) {
       if (sl[q] < 0) continue;
-      const float* hr = h + (size_t)(r0 + q) * d;
-      for (int k = threadIdx.x; k < d; k += MOE_THREADS) hsw[q * ldh + k + 4 * (k >> 5)] = hr[k];
+      const float4* hr = reinterpret_cast<const float4*>(h + (size_t)(r0 + q) * d);
+#pragma unroll 4
+      for (int k4 = threadIdx.x; k4 < (d >> 2); k4 += MOE_THREADS) {
+        const int k = k4 << 2;  // 4 columns inside one 32-column chunk
+        *reinterpret_cast<float4*>(hsw + q * ldh + k + 4 * (k >> 5)) = hr[k4];
+      }
     }
     __syncthreads();
-    for (int t = warp; t < MOE_ROWS * nch; t += MOE_WARPS) {
+    for (int t = warp; t < rows * nch; t += MOE_WARPS) {
       const int q = t / nch, c = t - q * nch;
       if (sl[q] < 0) continue;
       const float v = warp_sum(hsw[q * ldh + c * 36 + lane]);
       if (lane == 0) hsum[q * nch + c] = v;
     }
     __syncthreads();
-    for (int pi = warp; pi < MOE_PPC; pi += MOE_WARPS) {
-      const int i = p0 + pi;
-      if (i >= Ie) break;
-      const int rg = e * 2 * Ie + i, ru = rg + Ie;
-      float ag[MOE_ROWS], au[MOE_ROWS];
+    if (i >= Ie) continue;
+    const int rg = e * 2 * Ie + i, ru = rg + Ie;
+    float ag[PR], au[PR];
 #pragma unroll
-      for (int q = 0; q < MOE_ROWS; ++q) ag[q] = au[q] = 0.f;
-      for (int cb = 0; cb < nch; cb += 128) {
-        uint4 wg[4], wu[4];
+    for (int q = 0; q < PR; ++q) ag[q] = au[q] = 0.f;
+    for (int cb = 0; cb < nch; cb += 128) {
+      uint4 wg[4], wu[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = cb + u * 32 + lane;
-          if (c < nch) {
-            wg[u] = ldg_stream(w.codes + code_offset(w, rg, c));
-            wu[u] = ldg_stream(w.codes + code_offset(w, ru, c));
-          }
+      for (int u = 0; u < 4; ++u) {
+        const int c = cb + u * 32 + lane;
+        if (c < nch) {
+          wg[u] = ldg_stream(w.codes + code_offset(w, rg, c));
+          wu[u] = ldg_stream(w.codes + code_offset(w, ru, c));
         }
+      }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = cb + u * 32 + lane;
-          if (c >= nch) continue;
-          const int grp = (c << 5) / w.group;
-          const float sg = moe_scale<ST>(w, rg, grp), su = moe_scale<ST>(w, ru, grp);
-          float cg[32], cu[32];
-          decode_chunk(wg[u], cg);
-          decode_chunk(wu[u], cu);
+      for (int u = 0; u < 4; ++u) {
+        const int c = cb + u * 32 + lane;
+        if (c >= nch) continue;
+        const int grp = (c << 5) / w.group;
+        const float sg = moe_scale<ST>(w, rg, grp), su = moe_scale<ST>(w, ru, grp);
+        const uint32_t gw[4] = {wg[u].x, wg[u].y, wg[u].z, wg[u].w};
+        const uint32_t uw[4] = {wu[u].x, wu[u].y, wu[u].z, wu[u].w};
+        float dg[PR], du[PR];
 #pragma unroll
-          for (int q = 0; q < MOE_ROWS; ++q) {
+        for (int q = 0; q < PR; ++q) dg[q] = du[q] = 0.f;
+#pragma unroll
+        for (int qw = 0; qw < 4; ++qw) {
+          // word qw = columns 8qw .. 8qw+7: low nibbles even, high nibbles odd
+          const uint32_t glo = gw[qw] & 0x0F0F0F0Fu, ghi = (gw[qw] >> 4) & 0x0F0F0F0Fu;
+          const uint32_t ulo = uw[qw] & 0x0F0F0F0Fu, uhi = (uw[qw] >> 4) & 0x0F0F0F0Fu;
+          float cg[8], cu[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            cg[2 * j] = byte_to_float(glo, j);
+            cg[2 * j + 1] = byte_to_float(ghi, j);
+            cu[2 * j] = byte_to_float(ulo, j);
+            cu[2 * j + 1] = byte_to_float(uhi, j);
+          }
+#pragma unroll
+          for (int q = 0; q < PR; ++q) {
             if (sl[q] < 0) continue;
-            const float* hv = hsw + q * ldh + c * 36;
-            float dg = 0.f, du = 0.f;
+            const float* hv = hsw + q * ldh + c * 36 + 8 * qw;
+            const float4 h0 = *reinterpret_cast<const float4*>(hv);
+            const float4 h1 = *reinterpret_cast<const float4*>(hv + 4);
+            const float hh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
-            for (int t4 = 0; t4 < 8; ++t4) {
-              const float4 hh = *reinterpret_cast<const float4*>(hv + 4 * t4);
-              dg = fmaf(hh.x, cg[4 * t4], dg);
-              dg = fmaf(hh.y, cg[4 * t4 + 1], dg);
-              dg = fmaf(hh.z, cg[4 * t4 + 2], dg);
-              dg = fmaf(hh.w, cg[4 * t4 + 3], dg);
-              du = fmaf(hh.x, cu[4 * t4], du);
-              du = fmaf(hh.y, cu[4 * t4 + 1], du);
-              du = fmaf(hh.z, cu[4 * t4 + 2], du);
-              du = fmaf(hh.w, cu[4 * t4 + 3], du);
+            for (int t = 0; t < 8; ++t) {
+              dg[q] = fmaf(hh[t], cg[t], dg[q]);
+              du[q] = fmaf(hh[t], cu[t], du[q]);
             }
-            const float m15 = -15.f * hsum[q * nch + c];
-            ag[q] = fmaf(sg, fmaf(2.f, dg, m15), ag[q]);
-            au[q] = fmaf(su, fmaf(2.f, du, m15), au[q]);
           }
         }
-      }
 #pragma unroll
-      for (int q = 0; q < MOE_ROWS; ++q) {
-        if (sl[q] < 0) continue;
-        const float g = warp_sum(ag[q]) / 15.f, u = warp_sum(au[q]) / 15.f;
-        if (lane == 0) act[((size_t)(r0 + q) * K + sl[q]) * Ie + i] = silu_mul(g, u);
+        for (int q = 0; q < PR; ++q) {
+          if (sl[q] < 0) continue;
+          const float m15 = -15.f * hsum[q * nch + c];
+          ag[q] = fmaf(sg, fmaf(2.f, dg[q], m15), ag[q]);
+          au[q] = fmaf(su, fmaf(2.f, du[q], m15), au[q]);
+        }
       }
+    }
+#pragma unroll
+    for (int q = 0; q < PR; ++q) {
+      if (sl[q] < 0) continue;
+      const float g = warp_sum(ag[q]) / 15.f, u = warp_sum(au[q]) / 15.f;
+      if (lane == 0) act[((size_t)(r0 + q) * K + sl[q]) * Ie + i] = silu_mul(g, u);
     }
   }
 }
@@ -249,13 +307,13 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
 // ---------------------------------------------------------------------------
 // transposed down projection of the picked experts + residual
 // ---------------------------------------------------------------------------
-template <typename ST>
-__global__ void __launch_bounds__(MOE_THREADS)
-moe_down_kernel(const lumina_weight w, int d, int n, const int* __restrict__ sel, int E, int K, int Ie,
+template <typename ST, int PR>
+__global__ void __launch_bounds__(MOE_THREADS, PR == 1 ? 4 : 1)
+moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ score, int E, int K, int Ie,
                 const float* __restrict__ act, float* __restrict__ part, unsigned int* __restrict__ counters,
                 float* __restrict__ x) {
-  __shared__ float red[MOE_WARPS][MOE_ROWS][64];
-  __shared__ int slot[MOE_ROWS];
+  __shared__ float red[MOE_WARPS][PR][64];
+  __shared__ PassPicks pp;
   __shared__ int last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c0 = blockIdx.x * 64, split = blockIdx.y, S = gridDim.y;
@@ -263,35 +321,33 @@ moe_down_kernel(const lumina_weight w, int d, int n, const int* __restrict__ sel
   const int rsub = lane >> 3, cl = lane & 7;
   const int grp = c0 / w.group;
   const size_t coff = (size_t)(c0 >> 1) + 4 * cl;  // this lane's 4 code bytes within a row
-  for (int r0 = 0; r0 < n; r0 += MOE_ROWS) {
-    float acc[MOE_ROWS][8];
+  for (int r0 = 0; r0 < n; r0 += PR) {
+    const int rows = min(PR, n - r0);
+    float acc[PR][8];
 #pragma unroll
-    for (int q = 0; q < MOE_ROWS; ++q)
+    for (int q = 0; q < PR; ++q)
 #pragma unroll
       for (int t = 0; t < 8; ++t) acc[q][t] = 0.f;
-    for (int e = 0; e < E; ++e) {
-      __syncthreads();
-      if (threadIdx.x < MOE_ROWS) {
-        const int r = r0 + threadIdx.x;
-        slot[threadIdx.x] = r < n ? pick_slot(sel, r, K, e) : -1;
-      }
-      __syncthreads();
-      int sl[MOE_ROWS];
-      bool any = false;
+    __syncthreads();  // the previous pass is done with pp / red
+    pass_picks(score, r0, rows, E, K, pp);
+    for (int xe = 0; xe < pp.nt; ++xe) {
+      const int e = pp.touched[xe];
+      const float* ap[PR];
+      bool on[PR];
 #pragma unroll
-      for (int q = 0; q < MOE_ROWS; ++q) {
-        sl[q] = slot[q];
-        any |= sl[q] >= 0;
+      for (int q = 0; q < PR; ++q) {
+        const int j = q < rows ? slot_of(pp, q, K, e) : -1;
+        on[q] = j >= 0;
+        ap[q] = act + ((size_t)(r0 + q) * K + (j < 0 ? 0 : j)) * Ie;
       }
-      if (!any) continue;
-      const float* ap[MOE_ROWS];
-#pragma unroll
-      for (int q = 0; q < MOE_ROWS; ++q) ap[q] = act + ((size_t)(r0 + q) * K + (sl[q] < 0 ? 0 : sl[q])) * Ie;
 #pragma unroll 4
       for (int i = ib + warp * 4 + rsub; i < ie; i += 4 * MOE_WARPS) {
         const int R = e * Ie + i;
         const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(w.codes + (size_t)R * w.row_bytes + coff));
         const float s = moe_scale<ST>(w, R, grp);
+        float coef[PR];
+#pragma unroll
+        for (int q = 0; q < PR; ++q) coef[q] = on[q] ? __ldg(ap[q] + i) * s : 0.f;
         const uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
         float lv[8];
 #pragma unroll
@@ -300,17 +356,16 @@ moe_down_kernel(const lumina_weight w, int d, int n, const int* __restrict__ sel
           lv[2 * j + 1] = fmaf(2.f, byte_to_float(hi, j), -15.f);
         }
 #pragma unroll
-        for (int q = 0; q < MOE_ROWS; ++q) {
-          if (sl[q] < 0) continue;
-          const float coef = __ldg(ap[q] + i) * s;
+        for (int q = 0; q < PR; ++q) {
+          if (!on[q]) continue;
 #pragma unroll
-          for (int t = 0; t < 8; ++t) acc[q][t] = fmaf(coef, lv[t], acc[q][t]);
+          for (int t = 0; t < 8; ++t) acc[q][t] = fmaf(coef[q], lv[t], acc[q][t]);
         }
       }
     }
     // lanes l, l+8, l+16, l+24 hold the same columns: fold them, then the warps
 #pragma unroll
-    for (int q = 0; q < MOE_ROWS; ++q)
+    for (int q = 0; q < PR; ++q)
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         float v = acc[q][t];
@@ -319,9 +374,8 @@ moe_down_kernel(const lumina_weight w, int d, int n, const int* __restrict__ sel
         if (rsub == 0) red[warp][q][cl * 8 + t] = v;
       }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < MOE_ROWS * 64; idx += MOE_THREADS) {
+    for (int idx = threadIdx.x; idx < rows * 64; idx += MOE_THREADS) {
       const int q = idx >> 6, col = idx & 63;
-      if (r0 + q >= n) continue;
       float v = 0.f;
 #pragma unroll
       for (int wi = 0; wi < MOE_WARPS; ++wi) v += red[wi][q][col];
@@ -344,7 +398,7 @@ moe_down_kernel(const lumina_weight w, int d, int n, const int* __restrict__ sel
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
 }
 
-size_t gu_smem_bytes(int d) { return (size_t)(MOE_ROWS * (d + d / 8) + MOE_ROWS * (d / 32)) * 4; }
+size_t gu_smem_bytes(int d, int pr) { return (size_t)(pr * (d + d / 8) + pr * (d / 32)) * 4; }
 
 }  // namespace
 
@@ -370,7 +424,7 @@ int moe_check(const MoeLayerArgs& a) {
     set_error("virtual-MoE experts are built for int4 with groups of 64k in the row-major layout, d %% 64 == 0");
     return LUMINA_E_UNSUPPORTED;
   }
-  if (gu_smem_bytes(a.d) > 200 * 1024) {
+  if (gu_smem_bytes(a.d, MOE_ROWS) > 200 * 1024 || a.d % 4) {
     set_error("virtual-MoE layer: d %d too wide for the shared-memory row stage", a.d);
     return LUMINA_E_UNSUPPORTED;
   }
@@ -378,33 +432,41 @@ int moe_check(const MoeLayerArgs& a) {
 }
 
 int moe_prepare(int d) {
-  const int smem = (int)gu_smem_bytes(d);
-  LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int s1 = (int)gu_smem_bytes(d, 1), s4 = (int)gu_smem_bytes(d, MOE_ROWS);
+  LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<__half, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+  LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<float, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+  LUMINA_CUDA_TRY(
+      cudaFuncSetAttribute(moe_gu_kernel<__half, MOE_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, s4));
+  LUMINA_CUDA_TRY(
+      cudaFuncSetAttribute(moe_gu_kernel<float, MOE_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, s4));
   return LUMINA_OK;
 }
 
-int launch_moe(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
-  const int d = a.d;
-  moe_route_kernel<<<n, MOE_THREADS, d * 4, s>>>(x, d, a.norm_w, a.eps, a.router_w, a.router_b, a.E, a.K, sc.h,
-                                                 sc.sel);
+namespace {
+
+template <typename ST, int PR>
+int launch_experts(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
+  // a pass of PR rows touches at most min(E, PR * K) experts
+  const dim3 ggu(std::min(a.E, PR * a.K), (a.Ie + MOE_PPC - 1) / MOE_PPC);
+  moe_gu_kernel<ST, PR><<<ggu, MOE_THREADS, gu_smem_bytes(a.d, PR), s>>>(*a.gate_up, sc.h, a.d, n, sc.score, a.E,
+                                                                          a.K, a.Ie, sc.act);
   LUMINA_LAUNCH_CHECK();
-  const dim3 ggu(a.E, (a.Ie + MOE_PPC - 1) / MOE_PPC);
-  const size_t smem = gu_smem_bytes(d);
-  if (a.gate_up->fp16_scales)
-    moe_gu_kernel<__half><<<ggu, MOE_THREADS, smem, s>>>(*a.gate_up, sc.h, d, n, sc.sel, a.K, a.Ie, sc.act);
-  else
-    moe_gu_kernel<float><<<ggu, MOE_THREADS, smem, s>>>(*a.gate_up, sc.h, d, n, sc.sel, a.K, a.Ie, sc.act);
-  LUMINA_LAUNCH_CHECK();
-  const dim3 gdn(d / 64, MOE_SPLITS);
-  if (a.down->fp16_scales)
-    moe_down_kernel<__half><<<gdn, MOE_THREADS, 0, s>>>(*a.down, d, n, sc.sel, a.E, a.K, a.Ie, sc.act, sc.part,
-                                                        sc.counters, x);
-  else
-    moe_down_kernel<float><<<gdn, MOE_THREADS, 0, s>>>(*a.down, d, n, sc.sel, a.E, a.K, a.Ie, sc.act, sc.part,
-                                                       sc.counters, x);
+  const dim3 gdn(a.d / 64, moe_splits(n));
+  moe_down_kernel<ST, PR><<<gdn, MOE_THREADS, 0, s>>>(*a.down, a.d, n, sc.score, a.E, a.K, a.Ie, sc.act, sc.part,
+                                                      sc.counters, x);
   LUMINA_LAUNCH_CHECK();
   return LUMINA_OK;
+}
+
+}  // namespace
+
+int launch_moe(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
+  moe_route_kernel<<<dim3(n, a.E), ROUTE_THREADS, 0, s>>>(x, a.d, a.norm_w, a.eps, a.router_w, a.router_b, a.E,
+                                                           sc.h, sc.score);
+  LUMINA_LAUNCH_CHECK();
+  const bool h16 = a.gate_up->fp16_scales;
+  if (n == 1) return h16 ? launch_experts<__half, 1>(a, n, sc, x, s) : launch_experts<float, 1>(a, n, sc, x, s);
+  return h16 ? launch_experts<__half, MOE_ROWS>(a, n, sc, x, s) : launch_experts<float, MOE_ROWS>(a, n, sc, x, s);
 }
 
 }  // namespace lumina

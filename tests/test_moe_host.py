@@ -42,3 +42,35 @@ def test_all_experts_reproduce_the_dense_mlp():
                                     router_b=w[p + "gate_bias"])
     assert sorted(info["experts"][0].tolist()) == list(range(8))
     np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-6)
+
+
+def _device_topk(sc, k):
+    """The device rule (moe.cu topk_row): descending score, ties to the
+    lower expert index."""
+    out, taken = [], set()
+    for _ in range(k):
+        best = None
+        for e, v in enumerate(sc):
+            if e not in taken and (best is None or v > sc[best]):
+                best = e
+        taken.add(best)
+        out.append(best)
+    return out
+
+
+@pytest.mark.parametrize("E", [2, 4, 8, 16, 64])
+def test_topk_rule_matches_numpy_argsort(E):
+    """qwen_next.py:63 picks np.argsort(-scores)[:, :k]. Without ties the
+    device rule gives the same experts in the same order. numpy's sort is not
+    stable, so on exact score ties the reference's order is its sort
+    algorithm's; the device takes the lower index, and both pick the same
+    score values."""
+    rng = np.random.default_rng(E)
+    for _ in range(200):
+        sc = rng.standard_normal(E).astype(np.float32)
+        k = int(rng.integers(1, E + 1))
+        assert _device_topk(sc.tolist(), k) == np.argsort(-sc[None], axis=1)[0, :k].tolist()
+        tied = rng.choice(np.float32([0.25, 0.5, 0.75, 1.0]), size=E).astype(np.float32)
+        dev = _device_topk(tied.tolist(), k)
+        ref = np.argsort(-tied[None], axis=1)[0, :k]
+        assert sorted(tied[dev].tolist()) == sorted(tied[ref].tolist())
