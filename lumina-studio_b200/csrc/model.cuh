@@ -116,7 +116,7 @@ constexpr int MOE_MAX_E = 64;      // experts per layer
 constexpr int MOE_MAX_K = 8;       // top-k
 constexpr int MOE_ROWS = 4;        // batch rows per pass of the expert kernels
 constexpr int MOE_PPC = 8;         // (gate, up) neuron pairs per CTA: one per warp
-constexpr int MOE_SPLITS_MAX = 16; // neuron ranges of the down projection
+constexpr int MOE_SPLITS_MAX = 8;  // neuron ranges of the down projection
 inline int moe_splits(int n) { return n <= 32 ? MOE_SPLITS_MAX : 4; }
 // rows of down partials a forward of up to max_rows rows needs
 inline size_t moe_part_rows(int max_rows) {

@@ -20,7 +20,10 @@
 //    the same fp32 arithmetic as the GEMV prologues) and its router logit
 //    h . router[e] + b[e] as a sigmoid score with the +-40 clip
 //    (qwen_next.py:23-24). One CTA per (row, expert) keeps every load of the
-//    row and the router row in flight at once.
+//    row and the router row in flight at once; the router row is fetched
+//    before the dependency wait. The three kernels chain with programmatic
+//    dependent launch, so each one's CTAs are resident before its
+//    predecessor ends.
 //  * The expert kernels take rows in passes of up to MOE_ROWS and derive the
 //    picks of a pass from the scores themselves: top-k by descending score
 //    (qwen_next.py:63, np.argsort(-scores)[:, :k]) with exact ties to the
@@ -92,16 +95,27 @@ __device__ __forceinline__ float block_sum_route(float v, float* red) {
 // CTA (row r, expert e): the row's RMSNorm and its router logit for e, as
 // a sigmoid score. Every CTA of a row computes the same norm factor (same
 // loads, same order), so h is one value everywhere; expert 0's CTA stores it.
+// The router and norm rows do not depend on the previous kernel: they are
+// staged in shared memory before the dependency wait.
 __global__ void __launch_bounds__(ROUTE_THREADS)
 moe_route_kernel(const float* __restrict__ x, int d, const float* __restrict__ norm_w, float eps,
                  const float* __restrict__ rw, const float* __restrict__ rb, int E, float* __restrict__ h,
                  float* __restrict__ score) {
+  extern __shared__ __align__(16) float4 rs[];  // [d/4] router row e, [d/4] norm weight
   __shared__ float red[ROUTE_THREADS / 32];
   const int r = blockIdx.x, e = blockIdx.y;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * d);
-  const float4* nw = reinterpret_cast<const float4*>(norm_w);
-  const float4* wr = reinterpret_cast<const float4*>(rw + (size_t)e * d);
   const int d4 = d >> 2;
+  const float4* wr = reinterpret_cast<const float4*>(rw + (size_t)e * d);
+  const float4* nw = reinterpret_cast<const float4*>(norm_w);
+#pragma unroll 8
+  for (int k = threadIdx.x; k < d4; k += ROUTE_THREADS) {
+    rs[k] = __ldg(wr + k);
+    rs[d4 + k] = __ldg(nw + k);
+  }
+  const float bias = rb ? __ldg(rb + e) : 0.f;
+  pdl_launch_dependents();
+  pdl_wait();
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * d);
   // chat.py:63-66: x / sqrt(mean(x^2) + eps) * w, fp32
   float ss = 0.f;
 #pragma unroll 8
@@ -117,7 +131,7 @@ moe_route_kernel(const float* __restrict__ x, int d, const float* __restrict__ n
   float acc = 0.f;
 #pragma unroll 8
   for (int k = threadIdx.x; k < d4; k += ROUTE_THREADS) {
-    const float4 v = xr[k], w = nw[k], q = wr[k];
+    const float4 v = xr[k], w = rs[d4 + k], q = rs[k];
     float4 hv;
     hv.x = (v.x * inv) * w.x;
     hv.y = (v.y * inv) * w.y;
@@ -129,7 +143,7 @@ moe_route_kernel(const float* __restrict__ x, int d, const float* __restrict__ n
     acc = fmaf(hv.w, q.w, acc);
     if (e == 0) reinterpret_cast<float4*>(h + (size_t)r * d)[k] = hv;
   }
-  const float lg = block_sum_route(acc, red) + (rb ? rb[e] : 0.f);
+  const float lg = block_sum_route(acc, red) + bias;
   if (threadIdx.x == 0) score[(size_t)r * MOE_MAX_E + e] = 1.0f / (1.0f + expf(-fminf(fmaxf(lg, -40.f), 40.f)));
 }
 
@@ -160,6 +174,7 @@ __device__ __forceinline__ void topk_row(const float* sc, int E, int K, int* out
 struct PassPicks {
   int pick[MOE_ROWS][MOE_MAX_K];
   int touched[MOE_MAX_E];
+  signed char slot[MOE_MAX_E][MOE_ROWS];  // slot of touched[x] among row q's picks, or -1
   int nt;
 };
 
@@ -173,17 +188,18 @@ __device__ __forceinline__ void pass_picks(const float* __restrict__ score, int 
     }
     int nt = 0;
     for (int e = 0; e < E; ++e)
-      if ((used >> e) & 1ull) pp.touched[nt++] = e;
+      if ((used >> e) & 1ull) {
+        for (int q = 0; q < MOE_ROWS; ++q) {
+          signed char j = -1;
+          for (int jj = 0; q < pr && jj < K; ++jj)
+            if (pp.pick[q][jj] == e) j = (signed char)jj;
+          pp.slot[nt][q] = j;
+        }
+        pp.touched[nt++] = e;
+      }
     pp.nt = nt;
   }
   __syncthreads();
-}
-
-// slot of expert e among row q's picks, or -1
-__device__ __forceinline__ int slot_of(const PassPicks& pp, int q, int K, int e) {
-  for (int j = 0; j < K; ++j)
-    if (pp.pick[q][j] == e) return j;
-  return -1;
 }
 
 // ---------------------------------------------------------------------------
@@ -206,6 +222,9 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
   __shared__ PassPicks pp;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int i = blockIdx.y * MOE_PPC + warp;  // this warp's neuron pair
+  // everything below reads the router's outputs (scores, h)
+  pdl_launch_dependents();
+  pdl_wait();
   for (int r0 = 0; r0 < n; r0 += PR) {
     const int rows = min(PR, n - r0);
     __syncthreads();  // the previous pass is done with pp / hsw
@@ -214,7 +233,7 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
     const int e = pp.touched[blockIdx.x];
     int sl[PR];
 #pragma unroll
-    for (int q = 0; q < PR; ++q) sl[q] = q < rows ? slot_of(pp, q, K, e) : -1;
+    for (int q = 0; q < PR; ++q) sl[q] = pp.slot[blockIdx.x][q];
 #pragma unroll
     for (int q = 0; q < PR; ++q) {
       if (sl[q] < 0) continue;
@@ -321,6 +340,10 @@ moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ s
   const int rsub = lane >> 3, cl = lane & 7;
   const int grp = c0 / w.group;
   const size_t coff = (size_t)(c0 >> 1) + 4 * cl;  // this lane's 4 code bytes within a row
+  const int range = ie - ib;
+  // everything below reads the earlier kernels' outputs (scores, act, x)
+  pdl_launch_dependents();
+  pdl_wait();
   for (int r0 = 0; r0 < n; r0 += PR) {
     const int rows = min(PR, n - r0);
     float acc[PR][8];
@@ -330,38 +353,32 @@ moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ s
       for (int t = 0; t < 8; ++t) acc[q][t] = 0.f;
     __syncthreads();  // the previous pass is done with pp / red
     pass_picks(score, r0, rows, E, K, pp);
-    for (int xe = 0; xe < pp.nt; ++xe) {
-      const int e = pp.touched[xe];
-      const float* ap[PR];
-      bool on[PR];
+    // (touched expert, neuron) pairs of this CTA's range, flattened so that
+    // the loads of every touched expert are in flight together
+    const int total = pp.nt * range;
+#pragma unroll 4
+    for (int t = warp * 4 + rsub; t < total; t += 4 * MOE_WARPS) {
+      const int xe = t / range, i = ib + (t - xe * range);
+      const int R = pp.touched[xe] * Ie + i;
+      const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(w.codes + (size_t)R * w.row_bytes + coff));
+      const float s = moe_scale<ST>(w, R, grp);
+      float coef[PR];
 #pragma unroll
       for (int q = 0; q < PR; ++q) {
-        const int j = q < rows ? slot_of(pp, q, K, e) : -1;
-        on[q] = j >= 0;
-        ap[q] = act + ((size_t)(r0 + q) * K + (j < 0 ? 0 : j)) * Ie;
+        const int j = pp.slot[xe][q];
+        coef[q] = j >= 0 ? __ldg(act + ((size_t)(r0 + q) * K + j) * Ie + i) * s : 0.f;
       }
-#pragma unroll 4
-      for (int i = ib + warp * 4 + rsub; i < ie; i += 4 * MOE_WARPS) {
-        const int R = e * Ie + i;
-        const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(w.codes + (size_t)R * w.row_bytes + coff));
-        const float s = moe_scale<ST>(w, R, grp);
-        float coef[PR];
+      const uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
+      float lv[8];
 #pragma unroll
-        for (int q = 0; q < PR; ++q) coef[q] = on[q] ? __ldg(ap[q] + i) * s : 0.f;
-        const uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
-        float lv[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          lv[2 * j] = fmaf(2.f, byte_to_float(lo, j), -15.f);
-          lv[2 * j + 1] = fmaf(2.f, byte_to_float(hi, j), -15.f);
-        }
-#pragma unroll
-        for (int q = 0; q < PR; ++q) {
-          if (!on[q]) continue;
-#pragma unroll
-          for (int t = 0; t < 8; ++t) acc[q][t] = fmaf(coef[q], lv[t], acc[q][t]);
-        }
+      for (int j = 0; j < 4; ++j) {
+        lv[2 * j] = fmaf(2.f, byte_to_float(lo, j), -15.f);
+        lv[2 * j + 1] = fmaf(2.f, byte_to_float(hi, j), -15.f);
       }
+#pragma unroll
+      for (int q = 0; q < PR; ++q)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[q][c] = fmaf(coef[q], lv[c], acc[q][c]);
     }
     // lanes l, l+8, l+16, l+24 hold the same columns: fold them, then the warps
 #pragma unroll
@@ -433,6 +450,7 @@ int moe_check(const MoeLayerArgs& a) {
 
 int moe_prepare(int d) {
   const int s1 = (int)gu_smem_bytes(d, 1), s4 = (int)gu_smem_bytes(d, MOE_ROWS);
+  LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d * 8));
   LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<__half, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
   LUMINA_CUDA_TRY(cudaFuncSetAttribute(moe_gu_kernel<float, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
   LUMINA_CUDA_TRY(
@@ -448,22 +466,19 @@ template <typename ST, int PR>
 int launch_experts(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
   // a pass of PR rows touches at most min(E, PR * K) experts
   const dim3 ggu(std::min(a.E, PR * a.K), (a.Ie + MOE_PPC - 1) / MOE_PPC);
-  moe_gu_kernel<ST, PR><<<ggu, MOE_THREADS, gu_smem_bytes(a.d, PR), s>>>(*a.gate_up, sc.h, a.d, n, sc.score, a.E,
-                                                                          a.K, a.Ie, sc.act);
-  LUMINA_LAUNCH_CHECK();
+  LUMINA_CUDA_TRY(launch_pdl(moe_gu_kernel<ST, PR>, ggu, dim3(MOE_THREADS), gu_smem_bytes(a.d, PR), s, *a.gate_up,
+                             (const float*)sc.h, a.d, n, (const float*)sc.score, a.E, a.K, a.Ie, sc.act));
   const dim3 gdn(a.d / 64, moe_splits(n));
-  moe_down_kernel<ST, PR><<<gdn, MOE_THREADS, 0, s>>>(*a.down, a.d, n, sc.score, a.E, a.K, a.Ie, sc.act, sc.part,
-                                                      sc.counters, x);
-  LUMINA_LAUNCH_CHECK();
+  LUMINA_CUDA_TRY(launch_pdl(moe_down_kernel<ST, PR>, gdn, dim3(MOE_THREADS), 0, s, *a.down, a.d, n,
+                             (const float*)sc.score, a.E, a.K, a.Ie, (const float*)sc.act, sc.part, sc.counters, x));
   return LUMINA_OK;
 }
 
 }  // namespace
 
 int launch_moe(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
-  moe_route_kernel<<<dim3(n, a.E), ROUTE_THREADS, 0, s>>>(x, a.d, a.norm_w, a.eps, a.router_w, a.router_b, a.E,
-                                                           sc.h, sc.score);
-  LUMINA_LAUNCH_CHECK();
+  LUMINA_CUDA_TRY(launch_pdl(moe_route_kernel, dim3(n, a.E), dim3(ROUTE_THREADS), (size_t)a.d * 8, s,
+                             (const float*)x, a.d, a.norm_w, a.eps, a.router_w, a.router_b, a.E, sc.h, sc.score));
   const bool h16 = a.gate_up->fp16_scales;
   if (n == 1) return h16 ? launch_experts<__half, 1>(a, n, sc, x, s) : launch_experts<float, 1>(a, n, sc, x, s);
   return h16 ? launch_experts<__half, MOE_ROWS>(a, n, sc, x, s) : launch_experts<float, MOE_ROWS>(a, n, sc, x, s);
