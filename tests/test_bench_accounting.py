@@ -1,0 +1,44 @@
+"""bench.py's byte accounting and argument rules (CPU): the config-3 sweep's
+bytes per call, the virtual-MoE records' shapes and map, and the refusal of
+invalid timing arguments."""
+import numpy as np
+import pytest
+
+import bench
+from lumina_b200 import synthetic
+
+
+def test_sweep_bytes_formula():
+    # N*K*b/8 codes + N*ceil(K/g)*2 fp16 scales + batch*K*4 in + batch*N*4 out
+    assert bench.sweep_bytes(4096, 4096, 4, 64, 1) == 4096 * 2048 + 4096 * 64 * 2 + 4096 * 4 + 4096 * 4
+    assert bench.sweep_bytes(4096, 11008, 3, 64, 4) == 4096 * 4128 + 4096 * 172 * 2 + 4 * 11008 * 4 + 4 * 4096 * 4
+    assert bench.sweep_bytes(32000, 4096, 1, 128, 16) == 32000 * 512 + 32000 * 32 * 2 + 16 * 4096 * 4 + 16 * 32000 * 4
+
+
+def test_sweep_covers_config3():
+    assert set(bench.SWEEP_SHAPES) == {(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)}
+    assert [k for k, _, _ in bench.SWEEP_KINDS] == ["int4", "int3", "int2", "binary"]
+    assert bench.SWEEP_BATCHES == (1, 4, 16)
+
+
+def test_moe_records_layout():
+    cfg = dict(synthetic.LLAMA7B, num_hidden_layers=2)
+    recs = synthetic.QuantizedRecords(cfg, moe=(bench.MOE_EXPERTS, bench.MOE_TOP_K))
+    assert recs.moe_map == {0: {"experts": 8, "ie": 1376, "top_k": 2}, 1: {"experts": 8, "ie": 1376, "top_k": 2}}
+    shapes = {n: s for n, (_, s) in recs.order.items()}
+    assert shapes["model.layers.1.mlp.experts.gate_up_proj"] == (8 * 2 * 1376, 4096)
+    assert shapes["model.layers.1.mlp.experts.down_proj"] == (8 * 1376, 4096)
+    assert shapes["model.layers.1.mlp.gate.weight"] == (8, 4096)
+    assert shapes["model.layers.1.mlp.gate_bias"] == (8,)
+    assert not any(".mlp.gate_proj." in n or ".mlp.down_proj." in n for n in shapes)
+    # the routed MLP moves a quarter of the dense one's packed bytes at top-2 of 8
+    dense = 3 * 11008 * 4096
+    touched = bench.MOE_TOP_K * 3 * 1376 * 4096
+    assert touched * 4 == dense
+
+
+def test_warmup_floor():
+    with pytest.raises(SystemExit):
+        bench.main(["--warmup", "2", "--impl", "reference"])
+    with pytest.raises(SystemExit):
+        bench.main(["--moe", "--gpus", "2"])
