@@ -37,6 +37,11 @@ Besides the device-chained loop the line carries
 ``--impl reference`` runs only that CPU path (rank 0; other ranks exit 0).
 ``--moe`` measures the same decode on the virtual-MoE variant of the 7B
 shape (every SwiGLU split into 8 routed experts of 1376, top-2; one GPU).
+``--tiny`` runs the reference's CPU-runnable tiny configuration (64-token
+prompt, 128 greedy tokens) on the device and the reference's algorithm on
+the host.
+``--verify`` times the EAGLE tree verification of a 32-node draft tree over a
+4096-token prompt, and the prefill of that prompt.
 ``--sweep`` prints one line per case of the decode-only GEMV sweep (int4 /
 int3 / int2 / binary x the four 7B projection shapes x batch 1, 4, 16).
 """
@@ -327,10 +332,158 @@ def run_sweep(args):
     return 0
 
 
+class _IdTok:
+    """Token ids in, token ids out (the prompts here are id lists)."""
+
+    def encode(self, p):
+        return [int(t) for t in p]
+
+    def decode(self, ids):
+        return " ".join(str(int(i)) for i in ids)
+
+
+TINY_PROMPT, TINY_DECODE = 64, 128
+
+
+def run_tiny(args):
+    """The reference's CPU-runnable configuration (4 layers, d 256, vocab
+    4096, int4 g64, fp32 KV): a 64-token random prompt, then 128 greedy
+    decode tokens at batch 1. Device-chained decode (CUDA events), the public
+    ``generate`` call end to end (prefill + host sampler, wall clock, the
+    way the reference reports tokens_per_second, chat.py:404-407), and the
+    reference's algorithm on the host cores (the oracle port over the same
+    quantized weights). Prints one JSON line; the config is latency-bound,
+    so no roofline fraction is reported."""
+    import torch
+    from lumina_b200 import synthetic
+    from lumina_b200.engine import CudaChatModel, generate
+    torch.cuda.set_device(0)
+    cfg = dict(synthetic.TINY)
+    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=0)
+    model = CudaChatModel._from_records(recs, synthetic.hf_cfg(cfg), _IdTok(), 4, 4, 1e-6, cfg["rope_theta"], 0,
+                                        False, 512, 128, 16, 0, 1)
+    try:
+        prompt = synthetic.prompt_ids(cfg, TINY_PROMPT, seed=0)
+        first = int(np.argmax(model.forward(prompt, 0)[0].astype(np.float64)))
+        for _ in range(args.warmup):
+            model.decode_greedy(first, TINY_DECODE)
+            model.kv_truncate(TINY_PROMPT)
+        toks, dev_ms, kernels = model.decode_greedy(first, TINY_DECODE, timed=True)
+        generate(model, prompt, max_tokens=TINY_DECODE)  # warm the per-token graph
+        r = generate(model, prompt, max_tokens=TINY_DECODE)
+        recs_host = {name: recs[name] for name in recs.order}  # the same seeded, quantized tensors
+    finally:
+        model.close()
+    cb = None
+    if not args.no_cpu_baseline:
+        from oracle import lumina_format as lf
+        from oracle.decode import OracleModel, generate as ogen
+        # the reference's load-time dequant of the same codes (adapters/lumina.py:135-150)
+        t = {n: (np.asarray(r.data, np.float32) if r.kind == "raw" else
+                 lf.dequant(r.kind, lf.unpack_codes(r.codes, r.shape, r.pack), r.scales, r.group))
+             for n, r in recs_host.items()}
+        om = OracleModel(t, synthetic.hf_cfg(cfg), theta=cfg["rope_theta"])
+        ogen(om, prompt, 4)  # converts the fp32 weights once, as the reference caches them
+        t0 = time.perf_counter()
+        otoks = ogen(om, prompt, TINY_DECODE)
+        cpu_s = time.perf_counter() - t0
+        cb = {"value": TINY_DECODE / cpu_s, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+              "sample": f"the whole workload: {TINY_PROMPT}-token prefill + {TINY_DECODE} greedy tokens, numpy fp32",
+              "same_tokens": list(otoks) == list(r["tokens"])}
+    print(json.dumps({"bench": "tiny_decode", "workload": "tiny decoder (4 layers, d 256, 4 heads x 64, ffn 688, "
+                      "vocab 4096), Lumina int4 g64, fp32 KV, 64-token prompt, 128 greedy tokens, batch 1",
+                      "decode_tokens_per_s": TINY_DECODE / (dev_ms / 1e3), "ms_per_token": dev_ms / TINY_DECODE,
+                      "kernels_per_token": kernels,
+                      "e2e_generate_tokens_per_s": r["tokens_per_second"], "e2e_seconds": r["seconds"],
+                      # generate's first token is the prefill argmax; the chain starts after it
+                      "same_tokens_chained_and_generate": [first] + list(toks)[:-1] == list(r["tokens"]),
+                      "cpu_baseline": cb}), flush=True)
+    return 0
+
+
+# EAGLE tree of BASELINE config 5: depth 5, 32 nodes (root + 31 to verify)
+VERIFY_PROMPT = 4096
+VERIFY_BRANCHING = (4, 2, 1, 1)  # children per node at depths 0..3
+
+
+def verify_tree_shape():
+    """parents, depths of a depth-5, 32-node draft tree: the root's 4
+    children, 2 children each, then single chains, plus 3 nodes at depth 5."""
+    parents, depths, frontier = [-1], [0], [0]
+    for b in VERIFY_BRANCHING:
+        nxt = []
+        for p in frontier:
+            for _ in range(b):
+                parents.append(p)
+                depths.append(depths[p] + 1)
+                nxt.append(len(parents) - 1)
+        frontier = nxt
+    for p in frontier[:32 - len(parents)]:
+        parents.append(p)
+        depths.append(depths[p] + 1)
+    return parents, depths
+
+
+def run_verify(args):
+    """Tree verification on the 7B int4 model: prefill a 4096-token random
+    prompt (time to first token), then repeat the one-forward verification
+    of a 31-child draft tree (ancestry bias, true positions; the reference's
+    verify_tree, eagle.py:259-291) through the public engine call, rolling
+    the KV back after each. Wall clock around synchronous calls; prints one
+    JSON line."""
+    import torch
+    from lumina_b200 import synthetic
+    from lumina_b200.engine import CudaChatModel, verify_tree
+    torch.cuda.set_device(0)
+    cfg = dict(synthetic.LLAMA7B)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=0)
+    model = CudaChatModel._from_records(recs, synthetic.hf_cfg(cfg), None, 32, 32, 1e-6, 1e4, 0, True,
+                                        VERIFY_PROMPT + 64, 512, 16, 0, 1)
+    try:
+        prompt = synthetic.prompt_ids(cfg, VERIFY_PROMPT, seed=0)
+        model.forward(prompt[:512], 0)  # warm the prefill kernels
+        model.kv_truncate(0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.forward(prompt, 0)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        parents, depths = verify_tree_shape()
+        rng = np.random.default_rng(5)
+        ids = [prompt[-1]] + [int(t) for t in rng.integers(0, cfg["vocab_size"], len(parents) - 1)]
+        for _ in range(args.warmup):
+            verify_tree(model, VERIFY_PROMPT, ids, parents, depths)
+            model.kv_truncate(VERIFY_PROMPT)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            lg, order = verify_tree(model, VERIFY_PROMPT, ids, parents, depths)
+            model.kv_truncate(VERIFY_PROMPT)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        print(json.dumps({"bench": "tree_verify", "workload": "llama2-7b-shape int4 g64, fp16 KV, "
+                          f"{VERIFY_PROMPT}-token prompt, depth-{max(depths)} {len(parents)}-node draft tree",
+                          "verify_rows": len(order), "ms_per_verify": dt / args.steps * 1e3,
+                          "verify_rows_per_s": len(order) * args.steps / dt,
+                          "prefill_tokens_per_s": VERIFY_PROMPT / prefill_s, "prefill_s": prefill_s,
+                          "steps": args.steps, "warmup": args.warmup,
+                          "timing": "wall clock around synchronous engine calls (bias build, logits D2H included)"}),
+              flush=True)
+    finally:
+        model.close()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--sweep", action="store_true",
                     help="GEMV sweep over bit widths x 7B shapes x batch 1/4/16 (JSON line per case)")
+    ap.add_argument("--tiny", action="store_true",
+                    help="the reference's CPU-runnable tiny config: decode tok/s, generate e2e, CPU baseline")
+    ap.add_argument("--verify", action="store_true",
+                    help="EAGLE tree verification (4096-token prompt, 32-node tree) and prefill rate")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
@@ -352,6 +505,10 @@ def main(argv=None):
         return run_reference(args, cfg)
     if args.sweep:
         return run_sweep(args)
+    if args.verify:
+        return run_verify(args)
+    if args.tiny:
+        return run_tiny(args)
 
     import torch
     import torch.distributed as dist

@@ -113,21 +113,30 @@ def _quantize_gpu(w, bits: int, group: int):
     """Lumina round-to-nearest codes with the MSE scale search of
     ptq_ladder.py:215-249 (seven absmax multipliers, first minimum wins) in
     fp32 on the GPU, scales rounded to fp16 values. `w` is a (rows, cols)
-    float32 CUDA tensor with cols a multiple of `group`. Returns (codes
-    uint8 (rows, cols), scales float32 (rows, cols/group)). This makes
-    benchmark inputs: it is the reference's quantizer restated in torch,
-    not code under test."""
+    float32 CUDA tensor; a last group narrower than `group` is scored over
+    its own columns, as the reference does. Returns (codes uint8 (rows,
+    cols), scales float32 (rows, ceil(cols/group))). This makes benchmark
+    inputs: it is the reference's quantizer restated in torch, not code
+    under test."""
     import torch
     L = (1 << bits) - 1
     rows, cols = w.shape
-    wg = w.view(rows, cols // group, group)
+    ng = -(-cols // group)
+    pad = ng * group - cols
+    if pad:
+        w = torch.nn.functional.pad(w, (0, pad))  # zeros never raise a group's absmax
+    wg = w.view(rows, ng, group)
+    valid = torch.ones(ng, group, device=w.device, dtype=w.dtype)
+    if pad:
+        valid[-1, group - pad:] = 0.0
+    cnt = valid.sum(-1)
     amax = wg.abs().amax(-1).clamp_min(1e-12)
     best_e = best_s = None
     for f in _MULTIPLIERS:
         s = (amax * f).clamp_min(1e-12)
         wn = wg / s[..., None]
         c = torch.clamp(torch.round((wn + 1.0) * (L / 2.0)), 0, L)
-        e = ((wn - (c * (2.0 / L) - 1.0)) ** 2).mean(-1)
+        e = (((wn - (c * (2.0 / L) - 1.0)) ** 2) * valid).sum(-1) / cnt
         if best_e is None:
             best_e, best_s = e, s
         else:
@@ -136,7 +145,7 @@ def _quantize_gpu(w, bits: int, group: int):
             best_s = torch.where(take, s, best_s)
     s16 = best_s.half().float()
     c = torch.clamp(torch.round((wg / s16[..., None] + 1.0) * (L / 2.0)), 0, L).to(torch.uint8)
-    return c.view(rows, cols), s16
+    return c.view(rows, ng * group)[:, :cols].contiguous(), s16
 
 
 def _pack_gpu(c, bits: int):
