@@ -46,3 +46,27 @@ def gemv(codes, scales, group, bits, x, block=32, qmax=32767):
     t = 2 * d - L * q.sum(axis=2)[:, None, :]
     s = np.asarray(scales, dtype=np.float64)[:, (np.arange(nblk) * block) // group]  # (N, nblk)
     return (t * sx[:, None, :].astype(np.float64) * s[None]).sum(axis=2) / L
+
+
+def moe_gate_up(codes, scales, h, group=64):
+    """The routed gate/up arithmetic of moe_gu_kernel for one row h:
+    per 32-column chunk, s/15 * (2 * sum h*c - 15 * sum h), in float32."""
+    codes = np.asarray(codes, np.float32)
+    h = np.asarray(h, np.float32)
+    N, K = codes.shape
+    out = np.zeros(N, np.float32)
+    for c0 in range(0, K, 32):
+        hc = h[c0:c0 + 32]
+        dot = (codes[:, c0:c0 + 32] * hc).sum(axis=1, dtype=np.float32)
+        s = np.asarray(scales, np.float32)[:, c0 // group]
+        out += s * (np.float32(2) * dot - np.float32(15) * hc.sum(dtype=np.float32))
+    return out / np.float32(15)
+
+
+def moe_down(codes, scales, a, group=64):
+    """The transposed down arithmetic of moe_down_kernel: y = sum_i a_i * s_i
+    * (2 c_i - 15) / 15 over the rows of down (groups along the output)."""
+    codes = np.asarray(codes, np.float32)
+    s = np.repeat(np.asarray(scales, np.float32), group, axis=1)[:, :codes.shape[1]]
+    coef = np.asarray(a, np.float32)[:, None] * s
+    return (coef * (np.float32(2) * codes - np.float32(15))).sum(axis=0, dtype=np.float32) / np.float32(15)

@@ -74,3 +74,26 @@ def test_topk_rule_matches_numpy_argsort(E):
         dev = _device_topk(tied.tolist(), k)
         ref = np.argsort(-tied[None], axis=1)[0, :k]
         assert sorted(tied[dev].tolist()) == sorted(tied[ref].tolist())
+
+
+def test_device_moe_arithmetic_equals_dequant_math():
+    """The routed kernels never dequantize: gate/up use
+    s/15 * (2 sum h c - 15 sum h) per 32-column chunk and down uses
+    a * s * (2c - 15) / 15. Both equal the reference's dequant-then-multiply
+    (adapters/lumina.py:135-139, qwen_next.py:69-75) up to fp32 rounding."""
+    import kernel_model
+    from oracle import lumina_format as lf
+    rng = np.random.default_rng(11)
+    Ie, D = 86, 256
+    codes = rng.integers(0, 16, (2 * Ie, D))
+    scales = (np.abs(rng.standard_normal((2 * Ie, D // 64))) * 0.02 + 1e-3).astype(np.float32)
+    h = rng.standard_normal(D).astype(np.float32)
+    W = lf.dequant("int4", codes.astype(np.uint8), scales, 64)
+    np.testing.assert_allclose(kernel_model.moe_gate_up(codes, scales, h), W.astype(np.float64) @ h,
+                               rtol=1e-5, atol=1e-6)
+    dcodes = rng.integers(0, 16, (Ie, D))
+    dscales = (np.abs(rng.standard_normal((Ie, D // 64))) * 0.02 + 1e-3).astype(np.float32)
+    a = rng.standard_normal(Ie).astype(np.float32)
+    Wd = lf.dequant("int4", dcodes.astype(np.uint8), dscales, 64)
+    np.testing.assert_allclose(kernel_model.moe_down(dcodes, dscales, a), Wd.T.astype(np.float64) @ a,
+                               rtol=1e-5, atol=1e-6)
