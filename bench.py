@@ -274,12 +274,34 @@ def sweep_bytes(N, K, bits, group, batch):
     return N * ((K * bits + 7) // 8) + N * (-(-K // group)) * 2 + batch * K * 4 + batch * N * 4
 
 
+def cpu_gemv_us(N, K, batch, cache):
+    """The reference's chat-path GEMV on the host cores: fp32 BLAS
+    ``h @ W`` over weights dequantized once and kept transposed
+    (chat.py:223-243), whatever the code width. Median of 3 calls after a
+    warm one; memoised per shape and batch."""
+    key = (N, K, batch)
+    if key not in cache:
+        rng = np.random.default_rng(N + K)
+        wt = ((rng.random((K, N), dtype=np.float32) - 0.5) * 0.07).astype(np.float32)
+        x = rng.standard_normal((batch, K)).astype(np.float32)
+        out = np.empty((batch, N), np.float32)
+        np.dot(x, wt, out=out)
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            np.dot(x, wt, out=out)
+            ts.append(time.perf_counter() - t0)
+        cache[key] = float(np.median(ts)) * 1e6
+    return cache[key]
+
+
 def run_sweep(args):
     """Decode-only GEMV sweep: each bit width x shape x batch through the
     public lumina_gemv entry point. A set of weight copies larger than 3x the
     L2 is cycled so every call streams its weights from HBM; the calls are
     captured in one CUDA graph and timed with CUDA events on its stream.
-    Prints one JSON line per case."""
+    Beside each case, the reference's own GEMV on the host cores
+    (``cpu_gemv_us``). Prints one JSON line per case."""
     import torch
     from lumina_b200.cuda import Weight
     from lumina_b200.packing import to_file_layout
@@ -287,6 +309,7 @@ def run_sweep(args):
     peak, peak_kind = peaks()
     os.environ["LUMINA_INT4_LAYOUT"] = "mma"  # int4 in the decode model's tensor-pipe layout
     rng = np.random.default_rng(0)
+    cpu_cache = {}
     for kind, bits, group in SWEEP_KINDS:
         for N, K in SWEEP_SHAPES:
             ng = -(-K // group)
@@ -327,7 +350,10 @@ def run_sweep(args):
                 print(json.dumps({"sweep": "gemv", "kind": kind, "group": group, "N": N, "K": K, "batch": batch,
                                   "us_per_call": ms * 1e3, "bytes_per_call": b, "gbs": b / (ms * 1e-3) / 1e9,
                                   "frac": b / (ms * 1e-3) / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
-                                  "weight_copies": copies}), flush=True)
+                                  "weight_copies": copies,
+                                  "cpu_us_per_call": cpu_gemv_us(N, K, batch, cpu_cache), "cpu_cores": blas_threads(),
+                                  "cpu_kind": "the reference's chat-path GEMV: fp32 BLAS over dequantized weights"}),
+                      flush=True)
             del ws
     return 0
 

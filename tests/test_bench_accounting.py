@@ -42,3 +42,10 @@ def test_warmup_floor():
         bench.main(["--warmup", "2", "--impl", "reference"])
     with pytest.raises(SystemExit):
         bench.main(["--moe", "--gpus", "2"])
+
+
+def test_cpu_gemv_leg_times_and_memoises():
+    cache = {}
+    t = bench.cpu_gemv_us(256, 512, 4, cache)
+    assert t > 0 and cache == {(256, 512, 4): t}
+    assert bench.cpu_gemv_us(256, 512, 4, cache) == t
