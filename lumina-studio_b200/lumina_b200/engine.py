@@ -121,6 +121,20 @@ class DeviceKV:
         return self.model.kv_read(lyr, start, n)
 
 
+def share_nccl_id(uid: bytes, group=None) -> bytes:
+    """Rank 0's 128-byte NCCL id, handed to every rank of the
+    torch.distributed group (the other ranks' ``uid`` is ignored). A rank
+    that never joins, or a rank 0 that died, makes this raise -- a
+    connection error, or the group's timeout -- instead of waiting forever;
+    create the group with a short timeout."""
+    import torch.distributed as dist
+    box = [bytes(uid)]
+    dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+    if not isinstance(box[0], (bytes, bytearray)) or len(box[0]) != 128:
+        raise LuminaError(5, "NCCL id exchange returned %r" % type(box[0]).__name__)
+    return bytes(box[0])
+
+
 def moe_map_from_header(header: dict) -> dict:
     """{layer: entry} from a .lumina header's "virtual_moe" map, whose keys
     are tensor-name prefixes (serve.py:1357-1366)."""
@@ -309,9 +323,7 @@ class CudaChatModel:
         uid = (ctypes.c_uint8 * 128)()
         if dist.get_rank(group) == 0:
             check(self.lib.lumina_nccl_unique_id(uid), self.lib)
-        box = [bytes(uid)]
-        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0, group=group)
-        uid = (ctypes.c_uint8 * 128).from_buffer_copy(box[0])
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(share_nccl_id(bytes(uid), group))
         check(self.lib.lumina_model_init_tp(self.h, uid), self.lib)
 
     def close(self):
