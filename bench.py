@@ -427,7 +427,7 @@ def run_tiny(args):
     return 0
 
 
-# EAGLE tree of BASELINE config 5: depth 5, 32 nodes (root + 31 to verify)
+# EAGLE draft tree of the 7B tree-speculation workload: depth 5, 32 nodes (root + 31 to verify)
 VERIFY_PROMPT = 4096
 VERIFY_BRANCHING = (4, 2, 1, 1)  # children per node at depths 0..3
 

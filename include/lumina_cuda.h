@@ -109,6 +109,28 @@ int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, flo
 int lumina_gemv_noalloc(const lumina_weight* w, const float* x_dev, int batch, int ldx,
                         float* y_dev, int ldy, void* stream);
 
+/* Timeouts. Kernels that wait on their own shared-memory transfers (the
+ * decode GEMVs) bound every wait; one that gives up ORs a bit into a
+ * per-device fault word and returns, leaving its outputs unwritten. Every
+ * synchronous entry (lumina_gemv_host, lumina_forward, lumina_layer_forward,
+ * lumina_decode_step, lumina_decode_greedy, lumina_profile_gemv) clears the
+ * word as it starts and returns LUMINA_E_CUDA ("a device wait timed out")
+ * when it is set at the end. lumina_gemv and lumina_gemv_noalloc are
+ * asynchronous: after synchronizing their stream, the caller reads (and with
+ * `clear`, resets) the word here. The tops-style reference reported no
+ * errors at all (tops_int8.c: void returns); the dict convention of
+ * tops.py:296-314 carries this one to Python callers. */
+int lumina_fault_status(int device, int* word_host, int clear);
+/* Testing aid: the polls a kernel makes on a pending transfer before it gives
+ * up (default 2^24, about a second); 0 makes every such wait give up without
+ * polling, so that tests can check that a timeout surfaces as an error and
+ * that the next call succeeds. A negative value restores the default.
+ * Applies to kernels launched after the call; a CUDA graph keeps the value
+ * its capture saw. The transfers themselves always complete: a kernel whose
+ * wait gave up still waits, with the default limit, for its copies in
+ * flight before it exits. */
+int lumina_debug_wait_limit(long long spins);
+
 /* ---- int8 fused GEMV family (TOPS semantics, MoE-runtime path) -------- */
 /* Host-pointer entries with the exact argument meaning of the TOPS C ABI
  * (caller owns every buffer, row-major (N, K) weights). */
@@ -187,6 +209,13 @@ int lumina_kv_read(const lumina_model* m, int layer, int start, int n,
 /* EAGLE commit (eagle.py:340-350): rows base+src[i] -> base+i for i < n on
  * every layer, then length = base + n. */
 int lumina_kv_commit_rows(lumina_model* m, int base, const int* src_host, int n);
+
+/* Single-query attention of q (host fp32, (n_heads, head_dim) of this shard)
+ * over rows [0, len) of layer `layer`: softmax(q K^T / sqrt(hd)) V per head
+ * with every cached key visible and no bias — the decode row of chat.py:
+ * 264-281 (sq = 1), on the kernel the decode step runs. out_host receives
+ * (n_heads, head_dim) fp32. Synchronous. */
+int lumina_kv_attend(lumina_model* m, int layer, const float* q_host, float* out_host);
 
 /* One decoder layer over n rows of hidden state (device fp32, (n, d_model),
  * updated in place): the drop-in for ChatModel._layer(x, lyr, cache, pos0,

@@ -232,15 +232,8 @@ int launch_one(const float* q, int nh, int nkv, const void* kc, const void* vc, 
                const DevParams* P, float* out, float sdiv, cudaStream_t s) {
   auto kern = attnc_kernel<HD, KT>;
   constexpr int smem = AttnCfg<HD, KT>::SMEM;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) {
-      set_error("attention (cluster) attribute: %s", cudaGetErrorString(e));
-      return LUMINA_E_CUDA;
-    }
-    configured = true;
-  }
+  const int rc = set_smem_limit((const void*)kern, smem, "attention (cluster)");
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ATTNC_CLUSTER, nh);
   cfg.blockDim = dim3(128);

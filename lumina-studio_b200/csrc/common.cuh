@@ -85,6 +85,16 @@ __device__ __forceinline__ void pdl_wait() {
 
 int sm_count();
 
+// Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
+// current device (cached per kernel and device, thread-safe).
+int set_smem_limit(const void* func, size_t bytes, const char* what);
+
+// Polls a kernel makes on a pending shared-memory transfer before it gives up
+// and sets the device fault word: WAIT_SPIN_DEFAULT (about a second) unless
+// lumina_debug_wait_limit changed it. Passed to kernels as an argument.
+constexpr long long WAIT_SPIN_DEFAULT = 1LL << 24;
+long long wait_spin_limit();
+
 // Launch a kernel with the programmatic-stream-serialization attribute so that
 // it may begin while its predecessor drains (kernels call pdl_wait() before
 // touching data the predecessor wrote).

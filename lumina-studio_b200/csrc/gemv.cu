@@ -180,6 +180,7 @@ int gemv_fused_launch(const lumina_weight* w, const float* x, int ldx, int batch
   fa.eps = eps;
   fa.K = w->cols;
   fa.fault = fault;
+  fa.spin = wait_spin_limit();
   const bool norm = norm_w != nullptr;
   switch (w->bits) {
     case 4: return gemv_fused_bits<4>(fa, w, batch, epi, norm, s);

@@ -362,8 +362,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (long i = 0; i < MBAR_SPIN_LIMIT; ++i)
+// false once `limit` polls found the phase still pending (limit 0: at once)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit = MBAR_SPIN_LIMIT) {
+  for (long long i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
@@ -399,6 +401,7 @@ struct FusedArgs {
   int sbuf_bytes;  // one scale buffer (R * spr)
   int ring_bytes;  // one warp's code ring (S stages)
   int* fault;
+  long long spin;  // polls before a wait on a scale copy gives up (wait_spin_limit())
 };
 
 template <int BITS, int R, int U, int S, int NB, typename ST, int EPI, bool NORM>
@@ -659,14 +662,15 @@ gemv_fused_kernel(FusedArgs fa) {
     pre.kv_off = ep_off;
     pre.pos = ep_pos;
   }
-  bool ok = true;
+  int failed = -1;  // the task whose scale copy a wait gave up on
   for (int st = 0; st < total; ++st) {
     const int k = st / cx.n_it, it = st % cx.n_it;
     cx.issue(st + S - 1);  // refill the stage consumed last step
     if (it == 0) {
       if (lane == 0 && k + 1 < my_tasks) cx.issue_scales(k + 1);
-      if (!mbar_wait_bounded(&bars[k & 1], (uint32_t)((k >> 1) & 1))) {
-        ok = false;
+      const bool landed = mbar_wait_bounded(&bars[k & 1], (uint32_t)((k >> 1) & 1), fa.spin);
+      if (!__all_sync(0xffffffffu, landed)) {
+        failed = k;
         break;
       }
       const int row0 = cx.task_of(k) * R;
@@ -702,13 +706,15 @@ gemv_fused_kernel(FusedArgs fa) {
     }
   }
   cp_async_wait<0>();
-  if (!ok) {
-    // a scale copy never landed: record it, let in-flight copies finish
-    // (bounded) before this CTA's shared memory is released, and stop
+  if (failed >= 0) {
+    // a scale copy did not land in time: record it, and let this warp's
+    // scale copies still in flight (tasks `failed` and, if it was issued,
+    // `failed` + 1, each on its own buffer and phase) land, waiting with the
+    // full limit, before the CTA's shared memory is released
     if (lane == 0) {
       atomicOr(fa.fault, 1);
-      mbar_wait_bounded(&bars[0], 0);
-      mbar_wait_bounded(&bars[1], 0);
+      for (int k = failed; k < failed + 2 && k < my_tasks; ++k)
+        mbar_wait_bounded(&bars[k & 1], (uint32_t)((k >> 1) & 1));
     }
     __syncwarp();
   }
@@ -770,15 +776,8 @@ inline int dispatch_bits(const GemvArgs& a, int nb, int fp16, int epi, cudaStrea
 template <int BITS, int R, int U, int S, int NB, typename ST, int EPI, bool NORM>
 inline int launch_fused(const FusedArgs& fa, size_t smem, cudaStream_t s) {
   auto kern = gemv_fused_kernel<BITS, R, U, S, NB, ST, EPI, NORM>;
-  static size_t configured = 0;  // largest dynamic shared size granted so far
-  if (smem > configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      set_error("gemv_fused attribute (%zu bytes): %s", smem, cudaGetErrorString(e));
-      return LUMINA_E_CUDA;
-    }
-    configured = smem;
-  }
+  const int rc = set_smem_limit((const void*)kern, smem, "gemv_fused");
+  if (rc) return rc;
   const int grid = std::max(1, std::min(sm_count(), (fa.n_tasks + FW - 1) / FW));
   const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(FW * 32), smem, s, fa);
   if (e != cudaSuccess) {

@@ -358,15 +358,8 @@ static int launch_mma(const MmaArgs& a, cudaStream_t s) {
   if (NORM && nbp > MW * 16) return LUMINA_E_UNSUPPORTED;  // one-pass row norm
   const size_t smem = (size_t)nbp * NB * (64 + 8) + (size_t)MT * MKS * 16 * NB * 4;
   if (smem > 227 * 1024 - 2048) return LUMINA_E_UNSUPPORTED;
-  static size_t configured = 0;
-  if (smem > configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      set_error("gemv_mma attribute (%zu bytes): %s", smem, cudaGetErrorString(e));
-      return LUMINA_E_CUDA;
-    }
-    configured = smem;
-  }
+  const int rc = set_smem_limit((const void*)kern, smem, "gemv_mma");
+  if (rc) return rc;
   const int grid = std::max(1, std::min(sm_count(), a.n_rg));
   const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(MW * 32), smem, s, a);
   if (e != cudaSuccess) {

@@ -80,6 +80,7 @@ struct TcArgs {
   RopeKV rk;
   int nb;       // live batch rows (<= NB)
   int* fault;
+  long long spin;  // polls before a wait on a ring stage gives up (wait_spin_limit())
 };
 
 template <typename ST>
@@ -261,7 +262,7 @@ gemv_tc_kernel(TcArgs a) {
   const uint4* xbl = xb + (g & (NC - 1)) * 4 + t;  // column g, or any valid one
   const int2* fql = fq + (t & (NB - 1));           // batch row t, or any valid one
   float acc0 = 0.f, acc1 = 0.f;  // rows g, g+8 of batch row t
-  bool ok = true;
+  int failed = -1;  // the unit a wait gave up on
   int tile = 0, ku = 0;
   if (n_mine > 0) {
     tile = wu0 / a.UT;
@@ -269,9 +270,9 @@ gemv_tc_kernel(TcArgs a) {
   }
   for (int j = 0; j < n_mine; ++j) {
     const int p0 = ku * KS, np = min(P - p0, KS);
-    const bool landed = mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1));
+    const bool landed = mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1), a.spin);
     if (!__all_sync(0xffffffffu, landed)) {
-      ok = false;
+      failed = j;
       break;
     }
     const uint8_t* st = ring + (size_t)(j % TS) * a.stage_bytes;
@@ -352,12 +353,15 @@ gemv_tc_kernel(TcArgs a) {
     acc0 = acc1 = 0.f;
     ++tile;
   }
-  if (!ok) {
-    // a stage never landed: record it and let this warp's copies in flight
-    // finish (bounded) before the CTA's shared memory is released
+  if (failed >= 0) {
+    // a stage did not land in time: record it, and let this warp's units
+    // still in flight land before the CTA's shared memory is released. Units
+    // failed .. failed + TS - 1 (those issued) occupy distinct stages; unit j
+    // completes phase j / TS of stage j % TS. These waits take the full limit.
     if (lane == 0) {
       atomicOr(a.fault, 2);
-      for (int i = 0; i < TS; ++i) mbar_wait_bounded(&bars[i], 0);
+      const int issued = min(n_mine, failed + TS);
+      for (int j = failed; j < issued; ++j) mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1));
     }
     __syncwarp();
   }
@@ -366,15 +370,8 @@ gemv_tc_kernel(TcArgs a) {
 template <int NB, typename ST, int EPI, bool NORM, int KS>
 int launch_tc(const TcArgs& a, size_t smem, int grid, cudaStream_t s) {
   auto kern = gemv_tc_kernel<NB, ST, EPI, NORM, KS>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      set_error("gemv_tc attribute (%zu bytes): %s", smem, cudaGetErrorString(e));
-      return LUMINA_E_CUDA;
-    }
-    configured = smem;
-  }
+  const int rc = set_smem_limit((const void*)kern, smem, "gemv_tc");
+  if (rc) return rc;
   const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(TW * 32), smem, s, a);
   if (e != cudaSuccess) {
     set_error("gemv_tc launch: %s", cudaGetErrorString(e));
@@ -448,6 +445,7 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   if (rk) a.rk = *rk;
   a.nb = batch;
   a.fault = fault;
+  a.spin = wait_spin_limit();
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
   const int per = (a.T16 + sm_count() - 1) / sm_count();

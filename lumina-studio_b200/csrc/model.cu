@@ -79,9 +79,6 @@ struct lumina_model {
   int* chain_tokens = nullptr;            // [max_seq] generated tokens
   int* chain_count = nullptr;
   int chain_kernels = 0;                  // kernel nodes in chain_graph
-  void* mk_plan = nullptr;                // persistent decode-step kernel (decode_mk.cu), or null
-  unsigned int* mk_sync = nullptr;
-  float* mk_part = nullptr;
   MoeScratch moe{};                       // virtual-MoE scratch (null without MoE layers)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int graph_splits = 0;
@@ -495,6 +492,21 @@ int uniform_len(const lumina_model* m, int* len) {
   return LUMINA_OK;
 }
 
+// End of a synchronous entry: the fault word joins the copies on the model
+// stream, the stream is drained, and a set word (a bounded wait in a GEMV
+// gave up during this call) becomes the call's error and is cleared.
+int finish_checked(lumina_model* m, const char* what) {
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->fault_host, fault_flag_ptr(), sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  if (*m->fault_host) {
+    const int word = *m->fault_host;
+    *m->fault_host = 0;
+    cudaMemset(fault_flag_ptr(), 0, sizeof(int));
+    return fault_error(what, word);
+  }
+  return LUMINA_OK;
+}
+
 // Whole forward of n tokens at positions pos0.. (chunked by max_rows); head
 // logits of the last row or every row go to m->logits.
 int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int* pos_override, const float* bias,
@@ -516,6 +528,7 @@ int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int*
     }
   const int V = m->head_rows * std::max(1, m->c.tp_size);
   std::vector<int> pos(m->c.max_rows);
+  TRY(clear_fault_async(m->stream));
   for (int c0 = 0; c0 < n; c0 += m->c.max_rows) {
     const int cn = std::min(m->c.max_rows, n - c0);
     TRY(ensure_blocks(m, len + cn));
@@ -540,43 +553,7 @@ int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int*
       }
     }
   }
-  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  return LUMINA_OK;
-}
-
-// the persistent decode step (one new row, embed .. head), greedy: commit
-// the argmax as the next token on the device
-int launch_mk(lumina_model* m, bool greedy) {
-  MkRun r{};
-  r.x = m->x;
-  r.q_buf = m->q_buf;
-  r.attn = m->attn;
-  r.ffn_buf = m->ffn_buf;
-  r.kpool = m->kpool;
-  r.vpool = m->vpool;
-  r.layer_elems = m->layer_elems;
-  r.kv_fp16 = m->c.kv_fp16;
-  r.bt = m->bt_dev;
-  r.bs = m->c.block_size;
-  r.cos_t = m->rope_cos;
-  r.sin_t = m->rope_sin;
-  r.P = m->P_dev;
-  r.rowpos = m->rowpos_dev;
-  r.tokens = m->tokens_dev;
-  r.embed = m->embed;
-  r.embed_rows = m->embed_rows;
-  r.head = m->head;
-  r.vocab = m->head_rows;
-  r.logits = m->logits;
-  r.amax_key = m->amax_key_dev;
-  r.greedy = greedy ? 1 : 0;
-  r.chain_tokens = m->chain_tokens;
-  r.chain_count = m->chain_count;
-  r.max_splits = m->max_splits;
-  r.max_seq = m->c.max_seq;
-  r.part = m->mk_part;
-  r.sync = m->mk_sync;
-  return decode_mk_launch(m->mk_plan, r, m->stream);
+  return finish_checked(m, "forward");
 }
 
 int capture_step(lumina_model* m) {
@@ -586,7 +563,8 @@ int capture_step(lumina_model* m) {
   int rc = LUMINA_OK;
   const int V = m->head_rows * std::max(1, m->c.tp_size);
   do {
-    if (cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+    if (clear_fault_async(s) != LUMINA_OK ||
+        cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(m->rowpos_dev, m->rowpos_host, sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(m->tokens_dev, m->tokens_host, sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess) {
       set_error("capture: param copy");
@@ -594,17 +572,13 @@ int capture_step(lumina_model* m) {
       break;
     }
     const bool fused_argmax = m->comm == nullptr;
-    if (m->mk_plan) {
-      if ((rc = launch_mk(m, false))) break;
-    } else {
-      if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
-                             fused_argmax ? m->amax_key_dev : nullptr, s)))
-        break;
-      for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
-      if (rc) break;
-      if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
-      if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
-    }
+    if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
+                           fused_argmax ? m->amax_key_dev : nullptr, s)))
+      break;
+    for (int l = 0; l < m->c.n_layer && !rc; ++l) rc = run_layer(m, l, 1, nullptr);
+    if (rc) break;
+    if ((rc = run_head(m, 0, 1, fused_argmax ? m->amax_key_dev : nullptr))) break;
+    if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
     if (cudaMemcpyAsync(m->logits_host, m->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaMemcpyAsync(m->argmax_host, m->argmax_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaMemcpyAsync(m->amax_key_host, m->amax_key_dev, 8, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
@@ -658,10 +632,6 @@ int capture_chain(lumina_model* m) {
   const int V = m->head_rows * std::max(1, m->c.tp_size);
   const bool fused_argmax = m->comm == nullptr;
   do {
-    if (m->mk_plan) {
-      rc = launch_mk(m, true);
-      break;
-    }
     if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
                            fused_argmax ? m->amax_key_dev : nullptr, s)))
       break;
@@ -1008,36 +978,6 @@ int lumina_model_finalize(lumina_model* m) {
     TRY(dalloc(m, (void**)&m->moe.counters, (size_t)(m->d / 64) * 4));
     LUMINA_CUDA_TRY(cudaMemset(m->moe.counters, 0, (size_t)(m->d / 64) * 4));
   }
-  {
-    // the persistent decode step when LUMINA_MEGAKERNEL=1 and the model fits it
-    const char* e = getenv("LUMINA_MEGAKERNEL");
-    if (e && strcmp(e, "1") == 0 && !m->comm && c.tp_size <= 1) {
-      MkSetup ms;
-      ms.n_layer = c.n_layer;
-      ms.d = m->d;
-      ms.nh = m->nh;
-      ms.nkv = m->nkv;
-      ms.hd = m->hd;
-      ms.ffn = m->ffn;
-      ms.eps = c.eps;
-      ms.kv_fp16 = c.kv_fp16;
-      ms.block_size = c.block_size;
-      for (const Layer& Ly : m->L) {
-        ms.w.push_back({Ly.qkv, Ly.o, Ly.gu, Ly.down});
-        ms.in_norm.push_back(Ly.in_norm);
-        ms.post_norm.push_back(Ly.post_norm);
-      }
-      void* plan = nullptr;
-      const int rc = decode_mk_prepare(&plan, ms);
-      if (rc == LUMINA_OK) {
-        m->mk_plan = plan;
-        TRY(dalloc(m, (void**)&m->mk_sync, decode_mk_sync_words(plan) * 4));
-        TRY(dalloc(m, (void**)&m->mk_part, decode_mk_part_floats(m->nh, m->hd, c.max_seq) * 4));
-      } else if (rc != LUMINA_E_UNSUPPORTED) {
-        return rc;
-      }
-    }
-  }
   LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
   if (!fault_flag_ptr()) {
     set_error("model_finalize: fault flag unavailable");
@@ -1067,7 +1007,6 @@ int lumina_model_free(lumina_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
   if (m->chain_graph) cudaGraphExecDestroy(m->chain_graph);
-  if (m->mk_plan) decode_mk_free(m->mk_plan);
   if (m->ev0) cudaEventDestroy(m->ev0);
   if (m->ev1) cudaEventDestroy(m->ev1);
   if (m->comm) ncclCommDestroy(m->comm);
@@ -1195,6 +1134,29 @@ int lumina_kv_commit_rows(lumina_model* m, int base, const int* src_host, int n)
   return LUMINA_OK;
 }
 
+int lumina_kv_attend(lumina_model* m, int layer, const float* q_host, float* out_host) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(q_host && out_host, "kv_attend: null pointer");
+  LUMINA_CHECK_ARG(layer >= 0 && layer < m->c.n_layer, "kv_attend: layer %d", layer);
+  const int len = m->layer_len[layer];
+  LUMINA_CHECK_ARG(len >= 1, "kv_attend: layer %d holds no rows", layer);
+  Guard g(m->device);
+  const size_t qn = (size_t)m->nh * m->hd;
+  DevParams& P = *m->P_host;
+  P.n = 1;
+  P.t_prev = len;  // no row of this call is new: every key is read after the dependency wait
+  P.t_tot = len;
+  P.n_splits = 1;
+  P.bias_ld = 0;
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, m->stream));
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->q_buf, q_host, qn * 4, cudaMemcpyHostToDevice, m->stream));
+  TRY(launch_attention_cluster(m->c.kv_fp16, m->hd, m->q_buf, m->nh, m->nkv, layer_k(m, layer), layer_v(m, layer),
+                               m->bt_dev, m->c.block_size, m->P_dev, m->attn, m->stream));
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(out_host, m->attn, qn * 4, cudaMemcpyDeviceToHost, m->stream));
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return LUMINA_OK;
+}
+
 int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int pos0, const int* pos_override_host,
                          const float* bias_host, void* stream) {
   TRY(check_ready(m));
@@ -1221,7 +1183,8 @@ int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int po
                                       (size_t)(t_prev + n) * 4, n, cudaMemcpyHostToDevice, m->stream));
   }
   LUMINA_CUDA_TRY(cudaMemcpyAsync(m->x, x_dev, (size_t)n * m->d * 4, cudaMemcpyDeviceToDevice, m->stream));
-  int rc = run_layer(m, layer, n, bias_host ? m->bias_dev : nullptr);
+  int rc = clear_fault_async(m->stream);
+  if (!rc) rc = run_layer(m, layer, n, bias_host ? m->bias_dev : nullptr);
   if (!rc) {
     cudaMemcpyAsync(x_dev, m->x, (size_t)n * m->d * 4, cudaMemcpyDeviceToDevice, m->stream);
     cudaEventRecord(ev, m->stream);
@@ -1229,9 +1192,9 @@ int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int po
     m->layer_len[layer] = t_prev + n;
   }
   // pinned params / host bias must outlive the copies that read them
-  cudaStreamSynchronize(m->stream);
+  const int rc2 = finish_checked(m, "layer_forward");
   cudaEventDestroy(ev);
-  return rc;
+  return rc ? rc : rc2;
 }
 
 int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0, const int* pos_override_host,
@@ -1262,8 +1225,10 @@ int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argm
   LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
   for (auto& v : m->layer_len) v = len + 1;
   if (*m->fault_host) {
-    set_error("decode_step: a device wait timed out (fault word %#x)", *m->fault_host);
-    return LUMINA_E_CUDA;
+    // the step graph clears the word as it starts, so the bits are this step's
+    const int word = *m->fault_host;
+    *m->fault_host = 0;
+    return fault_error("decode_step", word);
   }
   const int V = m->head_rows * m->c.tp_size;
   if (logits_host) memcpy(logits_host, m->logits_host, (size_t)V * 4);
@@ -1296,8 +1261,10 @@ int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, fl
   if (device_ms) LUMINA_CUDA_TRY(cudaEventElapsedTime(device_ms, m->ev0, m->ev1));
   if (kernels_per_step) *kernels_per_step = m->chain_kernels;
   if (*m->fault_host) {
-    set_error("decode_greedy: a device wait timed out (fault word %#x)", *m->fault_host);
-    return LUMINA_E_CUDA;
+    const int word = *m->fault_host;
+    *m->fault_host = 0;
+    cudaMemset(fault_flag_ptr(), 0, sizeof(int));
+    return fault_error("decode_greedy", word);
   }
   return LUMINA_OK;
 }
@@ -1334,6 +1301,7 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
     return LUMINA_OK;
   };
   // warm (attributes, first-use setup) outside the capture
+  TRY(clear_fault_async(m->stream));
   TRY(one_token(true));
   LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
   cudaGraph_t gr = nullptr;
@@ -1370,6 +1338,7 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
     set_error("profile_gemv: %s", cudaGetErrorString(es));
     return LUMINA_E_CUDA;
   }
+  TRY(finish_checked(m, "profile_gemv"));
   *ms_per_launch = ms / (float)(iters * launches);
   if (launches_per_token) *launches_per_token = launches;
   if (bytes_per_token) *bytes_per_token = bytes;

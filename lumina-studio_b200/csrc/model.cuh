@@ -71,44 +71,6 @@ constexpr int ATTNC_CLUSTER = 8;
 constexpr int ATTNC_CHUNK = 64;
 int launch_attention_cluster(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
                              const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s);
-// One decode step (batch 1, greedy or with logits) as one persistent
-// kernel (decode_mk.cu). Prepared once per model: LUMINA_E_UNSUPPORTED when
-// the model is outside its envelope (int4 g64 fp16-scale fragment-layout
-// weights, head_dim x KV element size = 256 bytes, no tensor parallelism).
-struct MkSetup {
-  int n_layer, d, nh, nkv, hd, ffn;
-  float eps;
-  int kv_fp16, block_size;
-  std::vector<std::array<const lumina_weight*, 4>> w;  // per layer: qkv, o, gate/up, down
-  std::vector<const float*> in_norm, post_norm;
-};
-struct MkRun {
-  float *x, *q_buf, *attn, *ffn_buf;
-  void *kpool, *vpool;
-  size_t layer_elems;
-  int kv_fp16;
-  const int* bt;
-  int bs;
-  const float *cos_t, *sin_t;
-  DevParams* P;
-  int *rowpos, *tokens;
-  const __half* embed;
-  int embed_rows;
-  const __half* head;
-  int vocab;
-  float* logits;
-  unsigned long long* amax_key;
-  int greedy;
-  int *chain_tokens, *chain_count;
-  int max_splits, max_seq;
-  float* part;         // decode_mk_part_floats() floats: attention partial states
-  unsigned int* sync;  // decode_mk_sync_words() words, zeroed by the launch
-};
-int decode_mk_prepare(void** plan, const MkSetup& s);
-size_t decode_mk_sync_words(const void* plan);
-size_t decode_mk_part_floats(int nh, int hd, int max_seq);
-int decode_mk_launch(void* plan, const MkRun& r, cudaStream_t s);
-void decode_mk_free(void* plan);
 
 // Virtual-MoE MLP (moe.cu): router scores, gate/up + SwiGLU of the picked
 // experts, transposed down projection + residual, in place on x.

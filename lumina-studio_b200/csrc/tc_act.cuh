@@ -1,6 +1,5 @@
 // Activation rows -> tensor-pipe B fragments: the prologue of the int4
-// decode GEMV (gemv_tc.cu) and of the GEMV phases of the persistent decode
-// step (decode_mk.cu).
+// decode GEMV (gemv_tc.cu).
 //
 // NB rows of K columns; item i (eight columns) is row b = i / 8P, pair
 // p = (i / 8) mod P, columns 64p + 8(i mod 8) .. +7, so eight consecutive

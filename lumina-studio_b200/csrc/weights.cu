@@ -3,8 +3,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "weights.cuh"
@@ -33,6 +36,34 @@ int sm_count() {
   }
   return n[dev];
 }
+
+// Dynamic shared-memory limits are a per-device attribute of a kernel: the
+// largest limit granted so far is remembered per (kernel, device), under one
+// lock, so a process that launches on several devices (or from several host
+// threads) raises the limit on each device it uses.
+int set_smem_limit(const void* func, size_t bytes, const char* what) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> granted;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: no current device", what);
+    return LUMINA_E_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& g = granted[std::make_pair(func, dev)];
+  if (bytes <= g) return LUMINA_OK;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) {
+    set_error("%s: shared-memory limit of %zu bytes on device %d: %s", what, bytes, dev, cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  g = bytes;
+  return LUMINA_OK;
+}
+
+static std::atomic<long long> g_wait_spins{WAIT_SPIN_DEFAULT};
+long long wait_spin_limit() { return g_wait_spins.load(std::memory_order_relaxed); }
 
 // RAII device switch: entries run on the object's device and restore the
 // caller's current device on return.
@@ -124,14 +155,20 @@ static void linspace_levels(int bits, double* out) {
 
 __constant__ double c_levels[4][16];
 
-// bit 0: a bounded mbarrier wait in a GEMV gave up
+// The device fault word: bit 0 = a bounded wait in gemv_fused_kernel gave
+// up, bit 1 = one in gemv_tc_kernel. Kernels only ever OR bits in; the host
+// reads and clears it (lumina_fault_status, and every synchronous entry).
 __device__ int g_fault_flag;
 
 int* fault_flag_ptr() {
+  static std::mutex mu;
   static int* p[64] = {nullptr};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
   if (!p[dev]) {
     void* a = nullptr;
     if (cudaGetSymbolAddress(&a, g_fault_flag) != cudaSuccess) {
@@ -151,6 +188,22 @@ int read_fault_flag(int* out) {
   }
   LUMINA_CUDA_TRY(cudaMemcpy(out, p, sizeof(int), cudaMemcpyDeviceToHost));
   return LUMINA_OK;
+}
+
+int clear_fault_async(cudaStream_t s) {
+  int* p = fault_flag_ptr();
+  if (!p) {
+    set_error("fault flag: symbol address unavailable");
+    return LUMINA_E_CUDA;
+  }
+  LUMINA_CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(int), s));
+  return LUMINA_OK;
+}
+
+int fault_error(const char* what, int word) {
+  set_error("%s: a device wait timed out (fault word %#x: %s%s)", what, word,
+            (word & 1) ? "gemv_fused_kernel " : "", (word & 2) ? "gemv_tc_kernel" : "");
+  return LUMINA_E_CUDA;
 }
 
 static int ensure_levels() {
@@ -494,6 +547,31 @@ int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx, 
   return gemv_launch(w, q, batch, y_dev, ldy, EPI_STORE, nullptr, 0, s);
 }
 
+int lumina_fault_status(int device, int* word, int clear) {
+  LUMINA_CHECK_ARG(word, "fault_status: null output");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    set_error("fault_status: device %d not available", device);
+    return LUMINA_E_ARG;
+  }
+  DeviceGuard g(device);
+  int* p = fault_flag_ptr();
+  if (!p) {
+    set_error("fault_status: fault word unavailable on device %d", device);
+    return LUMINA_E_CUDA;
+  }
+  LUMINA_CUDA_TRY(cudaDeviceSynchronize());
+  LUMINA_CUDA_TRY(cudaMemcpy(word, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear && *word) LUMINA_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+  return LUMINA_OK;
+}
+
+int lumina_debug_wait_limit(long long spins) {
+  g_wait_spins.store(spins < 0 ? WAIT_SPIN_DEFAULT : spins, std::memory_order_relaxed);
+  return LUMINA_OK;
+}
+
 int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, float* y_host) {
   LUMINA_CHECK_ARG(w && x_host && y_host, "gemv_host: null pointer");
   LUMINA_CHECK_ARG(batch >= 1 && batch <= 16, "gemv_host: batch %d not in 1..16", batch);
@@ -511,10 +589,17 @@ int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, flo
     set_error("gemv_host: H2D copy failed");
     rc = LUMINA_E_CUDA;
   }
+  if (!rc) rc = clear_fault_async(nullptr);
   if (!rc) rc = lumina_gemv(w, xd, batch, w->cols, yd, w->rows, nullptr);
   if (!rc && cudaMemcpy(y_host, yd, yb, cudaMemcpyDeviceToHost) != cudaSuccess) {
     set_error("gemv_host: D2H copy failed: %s", cudaGetErrorString(cudaGetLastError()));
     rc = LUMINA_E_CUDA;
+  }
+  int word = 0;
+  if (!rc) rc = read_fault_flag(&word);
+  if (!rc && word) {
+    cudaMemset(fault_flag_ptr(), 0, sizeof(int));
+    rc = fault_error("gemv_host", word);
   }
   cudaFree(xd);
   cudaFree(yd);

@@ -167,5 +167,9 @@ void actq_carve(void* base, int batch, int nblk_pad, ActQ* out);
 // Device-side error word: bounded waits that give up set a bit here.
 int read_fault_flag(int* out);
 int* fault_flag_ptr();
+// stream-ordered clear of the current device's fault word
+int clear_fault_async(cudaStream_t s);
+// LUMINA_E_CUDA with the text of a set fault word
+int fault_error(const char* what, int word);
 
 }  // namespace lumina

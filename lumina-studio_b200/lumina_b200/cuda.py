@@ -98,6 +98,9 @@ SIGNATURES = {
     "lumina_decode_step": [_VP, _I, _FP, _IP],
     "lumina_decode_greedy": [_VP, _I, _I, _IP, _FP, _IP],
     "lumina_profile_gemv": [_VP, _I, _FP, _IP, ctypes.POINTER(ctypes.c_double)],
+    "lumina_kv_attend": [_VP, _I, _FP, _FP],
+    "lumina_fault_status": [_I, _IP, _I],
+    "lumina_debug_wait_limit": [ctypes.c_longlong],
 }
 _RESTYPE = {"lumina_last_error": ctypes.c_char_p}
 
@@ -198,6 +201,21 @@ def ptr(arr: np.ndarray, ctype):
     return arr.ctypes.data_as(ctypes.POINTER(ctype))
 
 
+def fault_status(device: int = 0, clear: bool = True) -> int:
+    """The device's fault word after its queued work finished (non-zero: a
+    bounded wait inside an asynchronous GEMV gave up; see lumina_gemv)."""
+    lib = bound_lib()
+    w = ctypes.c_int(0)
+    check(lib.lumina_fault_status(int(device), ctypes.byref(w), 1 if clear else 0), lib)
+    return w.value
+
+
+def debug_wait_limit(spins: int) -> None:
+    """Testing aid: polls before a kernel's wait on a pending transfer gives
+    up (0 = at once, negative = the default of about a second)."""
+    check(bound_lib().lumina_debug_wait_limit(int(spins)))
+
+
 # ---------------------------------------------------------------------------
 # packed weights
 # ---------------------------------------------------------------------------
@@ -226,6 +244,12 @@ class Weight:
         """Hand ownership to a model (lumina_model_set_weight)."""
         self._owned = False
         return self.handle
+
+    def free(self):
+        """Free the device copy now (queued work that reads it must be done)."""
+        if self._owned and self.handle:
+            check(bound_lib().lumina_weight_free(self.handle))
+        self.handle = None
 
     def info(self) -> dict:
         lib = bound_lib()

@@ -357,6 +357,16 @@ class CudaChatModel:
         s = np.ascontiguousarray(src, dtype=np.int32)
         check(self.lib.lumina_kv_commit_rows(self.h, int(base), ptr(s, ctypes.c_int), len(s)), self.lib)
 
+    def kv_attend(self, lyr, q):
+        """Single-query attention of q (n_heads_local, hd) over every cached row
+        of layer ``lyr`` (chat.py:264-281 with one row, no bias), on the
+        device's decode-attention kernel."""
+        q = np.ascontiguousarray(q, dtype=np.float32).reshape(self.n_heads_local, self.hd)
+        out = np.empty_like(q)
+        check(self.lib.lumina_kv_attend(self.h, int(lyr), ptr(q, ctypes.c_float), ptr(out, ctypes.c_float)),
+              self.lib)
+        return out
+
     # -- forwards ------------------------------------------------------------
     def _layer(self, x, lyr, cache, pos0, attn_bias=None, pos_override=None):
         """chat.py:232-304 on the device. ``cache`` must be this model's

@@ -24,6 +24,10 @@ LLAMA7B = {"name": "llama7b", "num_hidden_layers": 32, "hidden_size": 4096,
            "num_attention_heads": 32, "num_key_value_heads": 32,
            "intermediate_size": 11008, "vocab_size": 32000, "rope_theta": 10000.0}
 
+# the 7B shape cut to two layers: every kernel instantiation of the 7B decode
+# (head_dim 128, fp16 KV, the 32000-row head) at a size the CPU oracle runs
+LLAMA7B_2L = dict(LLAMA7B, name="llama7b_2l", num_hidden_layers=2)
+
 
 def tensor_order(cfg: dict) -> list[tuple[str, tuple[int, ...]]]:
     """(name, shape) in generation order."""
@@ -89,6 +93,32 @@ def virtual_moe_weights(cfg: dict, experts: int = 8, top_k: int = 2, seed: int =
         w[p + "gate_bias"] = (rng.standard_normal(experts) * router_std).astype(np.float32)
         meta[p] = {"experts": experts, "ie": ie, "top_k": top_k, "router_feat": "raw", "layer": str(l)}
     return w, meta
+
+
+def random_int4_payloads(cfg: dict, seed: int = 0, group: int = 64) -> dict:
+    """convert_arrays-style payloads ``{name: ("raw", fp32) | ("int4",
+    (codes, scales))}`` of a seeded decoder whose projections are drawn
+    directly as Lumina int4 records: codes uniform over 0..15 (uint8,
+    (rows, cols)), group scales uniform in [0.03, 0.06) rounded to fp16
+    values (stored F32, as the converter writes them), so that the weights
+    s * (2c - 15) / 15 have a standard deviation near 0.02. Embedding and
+    lm_head are raw N(0, 0.02); RMSNorm weights are 1 + N(0, 0.1). Drawn in
+    ``tensor_order`` from one generator. Used for parity cases at full model
+    width, where running the quantizer over every matrix would dominate."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in tensor_order(cfg):
+        if len(shape) == 1:
+            out[name] = ("raw", (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32))
+        elif "embed" in name or "lm_head" in name:
+            out[name] = ("raw", (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)))
+        else:
+            rows, cols = shape
+            codes = rng.integers(0, 16, (rows, cols), dtype=np.uint8)
+            ng = -(-cols // group)
+            scales = rng.uniform(0.03, 0.06, (rows, ng)).astype(np.float16).astype(np.float32)
+            out[name] = ("int4", (codes, scales))
+    return out
 
 
 def prompt_ids(cfg: dict, n: int, seed: int = 0) -> list[int]:

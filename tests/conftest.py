@@ -56,3 +56,26 @@ def tiny_moe_file(tmp_path_factory):
     write_lumina(path, payloads, name="tiny_moe", rung="int4", group_size=64,
                  extra_header={"virtual_moe": meta})
     return path
+
+
+@pytest.fixture(scope="session")
+def wide_payloads():
+    """The 7B decode shape cut to two layers (synthetic.LLAMA7B_2L) as int4
+    g64 payloads with uniform codes and fp16-valued scales; the reference
+    decoded the same records for tests/golden/wide_decode.npz."""
+    from lumina_b200 import synthetic
+    return synthetic.random_int4_payloads(synthetic.LLAMA7B_2L, seed=0)
+
+
+@pytest.fixture(scope="session")
+def wide_oracle(wide_payloads):
+    """OracleModel over the wide payloads, dequantized as the reference's
+    loader does (fp64 product rounded to fp32, adapters/lumina.py:135-139)."""
+    from oracle import lumina_format as lf
+    from oracle.decode import OracleModel
+    from lumina_b200 import synthetic
+    t = {}
+    for name, (kind, payload) in wide_payloads.items():
+        t[name] = payload if kind == "raw" else lf.dequant(kind, payload[0], payload[1], 64)
+    cfg = synthetic.LLAMA7B_2L
+    return OracleModel(t, synthetic.hf_cfg(cfg), theta=cfg["rope_theta"])

@@ -372,10 +372,62 @@ def make_moe(ref, tmp):
     print("moe tokens[:8]", r["tokens"][:8], "min route gap %.3g" % min(gaps))
 
 
+WIDE = {"seed": 0, "prompt": 17, "forced": 2, "greedy": 6}
+
+
+def make_wide(ref, tmp):
+    """The 7B decode shape (d 4096, 32 heads x 128, ffn 11008, vocab 32000)
+    cut to two layers, int4 g64 (synthetic.random_int4_payloads: uniform
+    codes, fp16-valued scales), written by the reference's writer, read by
+    its loader and decoded by its ChatModel (theta 1e4). Records the hidden
+    rows after each layer of a 17-row prefill, the last row's logits over the
+    32000-row head, two teacher-forced decode steps' logits and six greedy
+    tokens, plus hashes of every stored record."""
+    from lumina_convert import write_lumina
+    from lumina_framework.adapters import load_model
+    from lumina_framework.chat import ChatModel, generate
+
+    cfg = synthetic.LLAMA7B_2L
+    payloads = synthetic.random_int4_payloads(cfg, seed=WIDE["seed"])
+    hashes = {}
+    for name, (kind, payload) in payloads.items():
+        hashes[name] = sha(payload) if kind == "raw" else sha(payload[0], payload[1])
+    path = os.path.join(tmp, "wide.lumina")
+    write_lumina(path, payloads, [], "llama7b_2l", "int4", group_size=64)
+    del payloads
+    lm = load_model(path)
+    model = ChatModel.from_tensors(lm.tensors.tensors, synthetic.hf_cfg(cfg), StubTok(), theta=cfg["rope_theta"])
+    del lm
+    prompt = synthetic.prompt_ids(cfg, WIDE["prompt"], seed=WIDE["seed"])
+    emb = model.t["model.embed_tokens.weight"].astype(np.float32)
+    head_t = model.head.T.astype(np.float32)
+    cache = {}
+    h = emb[np.array(prompt)]
+    out = {"prompt": np.array(prompt)}
+    for lyr in range(model.n_layer):
+        h = model._layer(h, lyr, cache, 0)
+        out[f"hidden_prefill_l{lyr}"] = h.astype(np.float32)
+    out["logits_prefill_last"] = (h[-1:] @ head_t)[0].astype(np.float32)
+    pos = len(prompt)
+    forced = [int(t) for t in np.random.default_rng(9).integers(0, cfg["vocab_size"], WIDE["forced"])]
+    for s, tk in enumerate(forced):
+        hh = emb[[tk]]
+        for lyr in range(model.n_layer):
+            hh = model._layer(hh, lyr, cache, pos)
+        pos += 1
+        out[f"logits_step{s}"] = (hh @ head_t)[0].astype(np.float32)
+    r = generate(model, prompt, max_tokens=WIDE["greedy"], rng=np.random.default_rng(0))
+    out.update({"forced": np.array(forced), "tokens": np.array(r["tokens"]),
+                "sha_names": np.array(sorted(hashes)),
+                "sha": np.array([hashes[k] for k in sorted(hashes)])})
+    np.savez_compressed(os.path.join(HERE, "wide_decode.npz"), **out)
+    print("wide tokens", r["tokens"])
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=("format", "tiny", "tops", "moe"), default=None,
+    ap.add_argument("--only", choices=("format", "tiny", "tops", "moe", "wide"), default=None,
                     help="regenerate one fixture family (tiny includes the EAGLE fixture)")
     args = ap.parse_args()
     ref = args.reference
@@ -393,6 +445,8 @@ def main():
             make_tops(ref)
         if want("moe"):
             make_moe(ref, tmp)
+        if want("wide"):
+            make_wide(ref, tmp)
 
 
 if __name__ == "__main__":

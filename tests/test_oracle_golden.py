@@ -252,3 +252,45 @@ def test_moe_oracle_matches_reference(golden, tiny_moe_model):
         pos += 1
         if f"logits_step{s}" in g:
             np.testing.assert_allclose((hh @ head)[0], g[f"logits_step{s}"], rtol=1e-5, atol=1e-7)
+
+
+# ---------------------------------------------------------------------------
+# the 7B decode width (head_dim 128, ffn 11008, vocab 32000), two layers:
+# tests/golden/wide_decode.npz
+# ---------------------------------------------------------------------------
+def test_wide_records_match_reference(golden, wide_payloads):
+    g = golden("wide_decode.npz")
+    names = [str(n) for n in g["sha_names"]]
+    assert names == sorted(wide_payloads)
+    for n, h in zip(names, g["sha"]):
+        kind, payload = wide_payloads[n]
+        got = _sha(payload) if kind == "raw" else _sha(payload[0], payload[1])
+        assert got == str(h), n
+
+
+def test_wide_oracle_matches_reference(golden, wide_oracle):
+    """The oracle's layer, head and greedy driver at 7B width agree with the
+    reference's outputs (BLAS summation order may differ between hosts, so
+    the bar is 1e-5 relative, not bit equality)."""
+    g = golden("wide_decode.npz")
+    m = wide_oracle
+    emb, head = m.embed(), m.head_t()
+    prompt = [int(t) for t in g["prompt"]]
+    cache = {}
+    h = emb[np.array(prompt)]
+
+    def rel(a, b):
+        return float(np.linalg.norm(np.float64(a) - b) / np.linalg.norm(np.float64(b)))
+
+    for lyr in range(m.n_layer):
+        h = m.layer(h, lyr, cache, 0)
+        assert rel(h, g[f"hidden_prefill_l{lyr}"]) < 1e-5, lyr
+    assert rel((h[-1:] @ head)[0], g["logits_prefill_last"]) < 1e-5
+    pos = len(prompt)
+    for s, tk in enumerate(int(t) for t in g["forced"]):
+        hh = emb[[tk]]
+        for lyr in range(m.n_layer):
+            hh = m.layer(hh, lyr, cache, pos)
+        pos += 1
+        assert rel((hh @ head)[0], g[f"logits_step{s}"]) < 1e-5, s
+    assert generate(m, prompt, len(g["tokens"])) == [int(t) for t in g["tokens"]]
