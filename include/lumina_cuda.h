@@ -31,7 +31,7 @@ enum {
   LUMINA_E_UNSUPPORTED = 3,  /* valid input this build does not handle       */
   LUMINA_E_OOM = 4,          /* device allocation failed                     */
   LUMINA_E_STATE = 5,        /* call out of order (e.g. model not finalized) */
-  LUMINA_E_NCCL = 6,         /* NCCL error                                   */
+  LUMINA_E_NCCL = 6,         /* collective error (unused: no collective library) */
   LUMINA_E_SELFTEST = 7      /* numeric self-test mismatch                   */
 };
 
@@ -190,10 +190,18 @@ int lumina_model_set_moe(lumina_model* m, int layer, int experts, int ie, int to
 int lumina_model_finalize(lumina_model* m);
 int lumina_model_free(lumina_model* m);
 
-/* NCCL tensor parallelism: `unique_id` is the 128-byte ncclUniqueId that
- * rank 0 created with lumina_nccl_unique_id and every rank received. */
-int lumina_nccl_unique_id(uint8_t* id128_host);
-int lumina_model_init_tp(lumina_model* m, const uint8_t* id128_host);
+/* Tensor parallelism (tp_size > 1 in the config): each rank's sums after
+ * o_proj / down_proj and its vocab shard of the logits are exchanged over
+ * peer memory (NVLink) by one kernel per exchange, with no collective
+ * library. The reference has no multi-GPU path; this pair joins the ranks.
+ * After lumina_model_finalize every rank calls lumina_model_peer_handle (the
+ * 64-byte CUDA IPC handle of its exchange region), the handles travel to
+ * every rank in rank order (tp_size x 64 bytes), and each rank calls
+ * lumina_model_init_peers before its first forward. Every rank must then run
+ * the same forwards in the same order; a wait for a peer is bounded (about
+ * 10 s) and reports a timeout through the fault word. */
+int lumina_model_peer_handle(lumina_model* m, uint8_t* handle64_host);
+int lumina_model_init_peers(lumina_model* m, const uint8_t* handles_host);
 
 /* KV contract of chat.py (cache[lyr] = (k, v), rows (T, n_heads, hd)). */
 /* Rows held by `layer` (layer = -1: every layer, which must agree; layers

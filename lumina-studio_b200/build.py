@@ -23,22 +23,6 @@ INCLUDE = os.path.join(REPO, "include")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
-def nccl_dirs():
-    """NCCL headers and library of the PyTorch install (the same libnccl.so.2
-    torch.distributed loads, so one NCCL lives in the process)."""
-    try:
-        import nvidia.nccl as nn  # type: ignore
-        base = list(nn.__path__)[0]
-        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
-        if os.path.exists(os.path.join(inc, "nccl.h")):
-            return inc, lib
-    except Exception:
-        pass
-    if os.path.exists("/usr/include/nccl.h"):
-        return "/usr/include", "/usr/lib/x86_64-linux-gnu"
-    raise RuntimeError("nccl.h not found")
-
-
 def run(cmd, verbose):
     if verbose:
         print(" ".join(cmd))
@@ -54,13 +38,12 @@ def run(cmd, verbose):
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     nvcc = os.environ.get("NVCC", "nvcc")
-    nccl_inc, nccl_lib = nccl_dirs()
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     hdrs = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
     newest_hdr = max(os.path.getmtime(h) for h in hdrs)
     objs = []
     flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
-                    "-I", INCLUDE, "-I", CSRC, "-I", nccl_inc, "--expt-relaxed-constexpr"]
+                    "-I", INCLUDE, "-I", CSRC, "--expt-relaxed-constexpr"]
     if os.environ.get("LUMINA_PTXAS_VERBOSE"):
         flags += ["-Xptxas", "-v"]
     todo = []
@@ -78,8 +61,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             if os.environ.get("LUMINA_PTXAS_VERBOSE"):
                 sys.stdout.write(r.stderr)
     if force or not os.path.exists(OUT) or any(os.path.getmtime(o) > os.path.getmtime(OUT) for o in objs):
-        run([nvcc, "-shared", "-o", OUT] + objs + ARCH +
-            ["-L", nccl_lib, "-l:libnccl.so.2", "-Xlinker", "-rpath," + nccl_lib], verbose)
+        run([nvcc, "-shared", "-o", OUT] + objs + ARCH, verbose)
     return OUT
 
 

@@ -42,7 +42,7 @@ template <int HD, typename KT>
 __global__ void __launch_bounds__(128)
 attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
              const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
-             const DevParams* __restrict__ P, float* __restrict__ out, float sdiv) {
+             const DevParams* __restrict__ P, float* __restrict__ out, float sdiv, L2Prefetch pf) {
   using C = AttnCfg<HD, KT>;
   constexpr int CK = ATTNC_CHUNK, CS = ATTNC_CLUSTER;
   cg::cluster_group cluster = cg::this_cluster();
@@ -89,6 +89,7 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
   const int nchunks = (nk + CK - 1) / CK;
   issue(0, true);
   issue(1, true);
+  if (tid == 0) l2_prefetch_share(pf, h * CS + r, gridDim.y * CS);
   pdl_wait();
   // the new row, when it sits in a chunk requested before the wait
   if (knew >= k0 && knew < k1 && (knew - k0) / CK < 2) {
@@ -229,7 +230,7 @@ attnc_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict_
 
 template <int HD, typename KT>
 int launch_one(const float* q, int nh, int nkv, const void* kc, const void* vc, const int* bt, int bs,
-               const DevParams* P, float* out, float sdiv, cudaStream_t s) {
+               const DevParams* P, float* out, float sdiv, cudaStream_t s, const L2Prefetch* pf) {
   auto kern = attnc_kernel<HD, KT>;
   constexpr int smem = AttnCfg<HD, KT>::SMEM;
   const int rc = set_smem_limit((const void*)kern, smem, "attention (cluster)");
@@ -248,7 +249,9 @@ int launch_one(const float* q, int nh, int nkv, const void* kc, const void* vc, 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q, nh, nkv, (const KT*)kc, (const KT*)vc, bt, bs, P, out, sdiv);
+  const L2Prefetch none;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, kern, q, nh, nkv, (const KT*)kc, (const KT*)vc, bt, bs, P, out, sdiv, pf ? *pf : none);
   if (e != cudaSuccess) {
     set_error("attention (cluster) launch: %s", cudaGetErrorString(e));
     return LUMINA_E_CUDA;
@@ -259,12 +262,13 @@ int launch_one(const float* q, int nh, int nkv, const void* kc, const void* vc, 
 }  // namespace
 
 int launch_attention_cluster(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                             const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s) {
+                             const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s,
+                             const L2Prefetch* pf) {
   const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
-  if (hd == 128) return fp16 ? launch_one<128, __half>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s)
-                             : launch_one<128, float>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s);
-  if (hd == 64) return fp16 ? launch_one<64, __half>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s)
-                            : launch_one<64, float>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s);
+  if (hd == 128) return fp16 ? launch_one<128, __half>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s, pf)
+                             : launch_one<128, float>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s, pf);
+  if (hd == 64) return fp16 ? launch_one<64, __half>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s, pf)
+                            : launch_one<64, float>(q, nh, nkv, kc, vc, bt, bs, P, out, sdiv, s, pf);
   set_error("attention: head_dim %d not built (64, 128)", hd);
   return LUMINA_E_UNSUPPORTED;
 }

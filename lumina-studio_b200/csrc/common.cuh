@@ -85,6 +85,53 @@ __device__ __forceinline__ void pdl_wait() {
 
 int sm_count();
 
+// Bytes that the kernel launched next in the stream will stream from HBM,
+// pulled into L2 by the running kernel (one bulk prefetch per piece), so that
+// HBM keeps streaming across the launch boundary instead of idling while the
+// next kernel's CTAs start and issue their first requests. A hint only: it
+// moves no data a kernel reads through any path but L2.
+struct L2Prefetch {
+  const void* p[2] = {nullptr, nullptr};  // contiguous ranges, 16-byte aligned
+  unsigned long long n[2] = {0, 0};       // their sizes, multiples of 16 bytes
+  // the paged KV rows [0, *len) of one layer: blocks bt[0 .. ceil(*len / bs))
+  // of kc and vc, block_bytes each (a multiple of 16)
+  const void* kc = nullptr;
+  const void* vc = nullptr;
+  const int* bt = nullptr;
+  const int* len = nullptr;
+  int bs = 0;
+  unsigned block_bytes = 0;
+};
+
+__device__ __forceinline__ void l2_prefetch(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Worker w of nw (one thread each) prefetches its share of every range, in
+// pieces of at most 64 KB.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int w, int nw) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const unsigned long long n = pf.n[r];
+    if (!n) continue;
+    const unsigned long long per = ((n + nw - 1) / nw + 15) & ~15ull;
+    const unsigned long long s0 = (unsigned long long)w * per;
+    if (s0 >= n) continue;
+    const unsigned long long len = per < n - s0 ? per : n - s0;
+    const char* base = static_cast<const char*>(pf.p[r]) + s0;
+    for (unsigned long long o = 0; o < len; o += 65536)
+      l2_prefetch(base + o, (unsigned)(len - o < 65536 ? len - o : 65536));
+  }
+  if (pf.bt) {
+    const int nblk = (*pf.len + pf.bs - 1) / pf.bs;
+    for (int b = w; b < 2 * nblk; b += nw) {
+      const char* base = static_cast<const char*>((b & 1) ? pf.vc : pf.kc) + (size_t)pf.bt[b >> 1] * pf.block_bytes;
+      for (unsigned o = 0; o < pf.block_bytes; o += 65536)
+        l2_prefetch(base + o, pf.block_bytes - o < 65536u ? pf.block_bytes - o : 65536u);
+    }
+  }
+}
+
 // Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
 // current device (cached per kernel and device, thread-safe).
 int set_smem_limit(const void* func, size_t bytes, const char* what);

@@ -81,6 +81,7 @@ struct TcArgs {
   int nb;       // live batch rows (<= NB)
   int* fault;
   long long spin;  // polls before a wait on a ring stage gives up (wait_spin_limit())
+  L2Prefetch pf;   // the next kernel's bytes, pulled into L2 while this one runs
 };
 
 template <typename ST>
@@ -213,6 +214,7 @@ gemv_tc_kernel(TcArgs a) {
     i_tile = wu0 / a.UT;
     i_ku = wu0 - i_tile * a.UT;
   }
+  const uint64_t pol = l2_evict_first_policy();
   auto issue = [&](int j) {
     const int tile = i_tile, p0 = i_ku * KS, np = min(P - p0, KS);
     if (++i_ku == a.UT) {
@@ -224,8 +226,8 @@ gemv_tc_kernel(TcArgs a) {
     const uint32_t cb = (uint32_t)np * 512u, sb = (uint32_t)(G1 - G0) * SG;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_expect_tx(&bars[j % TS], cb + sb);
-    bulk_g2s(st, a.codes + ((size_t)tile * P + p0) * 512, cb, &bars[j % TS]);
-    bulk_g2s(st + KS * 512, a.scales + ((size_t)tile * a.ng + G0) * SG, sb, &bars[j % TS]);
+    bulk_g2s_hint(st, a.codes + ((size_t)tile * P + p0) * 512, cb, &bars[j % TS], pol);
+    bulk_g2s_hint(st + KS * 512, a.scales + ((size_t)tile * a.ng + G0) * SG, sb, &bars[j % TS], pol);
   };
 
   if (lane == 0) {
@@ -238,6 +240,7 @@ gemv_tc_kernel(TcArgs a) {
   //    before the dependency wait
   if (lane == 0) {
     for (int j = 0; j < min(TS, n_mine); ++j) issue(j);
+    l2_prefetch_share(a.pf, blockIdx.x * TW + warp, G * TW);
   }
   // norm weights never depend on the previous kernel either
   float wpre[TQ_CH][8];
@@ -411,7 +414,8 @@ int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bo
 }  // namespace
 
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
-                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk) {
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
+                   const L2Prefetch* pf) {
   if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
@@ -446,6 +450,7 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   a.nb = batch;
   a.fault = fault;
   a.spin = wait_spin_limit();
+  if (pf) a.pf = *pf;
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
   const int per = (a.T16 + sm_count() - 1) / sm_count();

@@ -1,8 +1,8 @@
 // Decode model: weight registry, paged KV, the dense decoder layer of
 // chat.py:_layer (232-304) on the device, whole forwards and a graph-replayed
-// greedy decode step. Optional NCCL tensor parallelism (column-parallel
-// q/k/v/gate/up/head, row-parallel o/down with an all-reduce after each).
-#include <nccl.h>
+// greedy decode step. Optional tensor parallelism (column-parallel
+// q/k/v/gate/up/head, row-parallel o/down) whose sums and logits gather run
+// over peer memory (peer.cu).
 
 #include <algorithm>
 #include <cmath>
@@ -83,7 +83,13 @@ struct lumina_model {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int graph_splits = 0;
   bool finalized = false;
-  ncclComm_t comm = nullptr;
+  // tensor parallelism: this rank's exchange region [flags][slot 0..2] and
+  // every rank's region as mapped here (this rank's own at [tp_rank])
+  char* exch = nullptr;
+  size_t exch_slot = 0;  // floats per slot
+  char* peer_exch[PEER_MAX] = {};
+  unsigned* peer_epoch = nullptr;  // PEER_CTAS exchange counters
+  bool peers_ready = false;
   std::vector<void*> allocs;
 };
 
@@ -302,31 +308,35 @@ size_t kv_es(const lumina_model* m) { return m->c.kv_fp16 ? 2 : 4; }
 char* layer_k(lumina_model* m, int l) { return (char*)m->kpool + (size_t)l * m->layer_elems * kv_es(m); }
 char* layer_v(lumina_model* m, int l) { return (char*)m->vpool + (size_t)l * m->layer_elems * kv_es(m); }
 
-int allreduce(lumina_model* m, float* buf, size_t n) {
-  if (!m->comm) return LUMINA_OK;
-  ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream);
-  if (r != ncclSuccess) {
-    set_error("ncclAllReduce: %s", ncclGetErrorString(r));
-    return LUMINA_E_NCCL;
+// slot `slot` of this rank's exchange region
+float* exch_slot_ptr(lumina_model* m, int slot) {
+  return reinterpret_cast<float*>(m->exch + PEER_FLAG_BYTES) + (size_t)slot * m->exch_slot;
+}
+
+// Exchange slot `slot` (n floats, written by the previous kernel) with every
+// rank: PEER_SUM adds the ranks' sum into out, PEER_GATHER writes the ranks'
+// slots side by side to out.
+int peer_exchange(lumina_model* m, int slot, int mode, size_t n, float* out) {
+  PeerArgs a{};
+  const int tp = m->c.tp_size;
+  for (int r = 0; r < tp; ++r) {
+    a.slot[r] = reinterpret_cast<const float*>(m->peer_exch[r] + PEER_FLAG_BYTES) + (size_t)slot * m->exch_slot;
+    a.flags[r] = reinterpret_cast<unsigned*>(m->peer_exch[r]);
   }
-  return LUMINA_OK;
-}
-
-__global__ void add_inplace_kernel(float* x, const float* a, size_t n) {
-  pdl_launch_dependents();
-  pdl_wait();
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    x[i] += a[i];
-}
-
-int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
-  const int grid = (int)std::min<size_t>((n + 255) / 256, 1024);
-  cudaError_t e = launch_pdl(add_inplace_kernel, dim3(std::max(grid, 1)), dim3(256), 0, m->stream, x, a, n);
-  if (e != cudaSuccess) {
-    set_error("add launch: %s", cudaGetErrorString(e));
+  a.epoch = m->peer_epoch;
+  a.tp = tp;
+  a.rank = m->c.tp_rank;
+  a.n = n;
+  a.out = out;
+  a.fault = fault_flag_ptr();
+  // peers run the same calls within moments of each other; 10 s is a hang
+  // guard, not a latency figure (a wait limit of 0 gives up at once)
+  a.timeout_ns = wait_spin_limit() == 0 ? 0ull : 10000000000ull;
+  if (!a.fault) {
+    set_error("peer exchange: fault word unavailable");
     return LUMINA_E_CUDA;
   }
-  return LUMINA_OK;
+  return launch_peer_exchange(a, mode, m->stream);
 }
 
 #define TRY(expr)            \
@@ -338,10 +348,10 @@ int add_inplace(lumina_model* m, float* x, const float* a, size_t n) {
 // y = W x (+ epilogue): the fused decode GEMV for 1, 2 or 4 rows, else (or
 // when the shape does not fit it) act_quant + the global-activation GEMV.
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
-             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk) {
+             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const L2Prefetch* pf = nullptr) {
   if (w->mma) {
     if (n <= 4) {
-      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
+      const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
@@ -355,13 +365,45 @@ int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, i
   return gemv_launch(w, m->aq, n, y, ldy, epi, resid, ldr, m->stream, rk);
 }
 
+// the first bytes of the LM head (the kernel after the last layer)
+L2Prefetch head_prefetch(const lumina_model* m) {
+  L2Prefetch pf;
+  pf.p[0] = m->head;
+  pf.n[0] = std::min<size_t>((size_t)m->head_rows * m->d * 2, (size_t)48 << 20) & ~size_t(15);
+  return pf;
+}
+
+// the packed weight the first GEMV of layer l streams
+const lumina_weight* qkv_weight(const lumina_model* m, int l) {
+  const Layer& Ly = m->L[l];
+  return Ly.qkv ? Ly.qkv : Ly.q;
+}
+
 // One decoder layer over n rows of m->x (device params already uploaded).
+// Each kernel of the layer pulls its successor's HBM bytes into L2 while it
+// runs (L2Prefetch): q/k/v the layer's cached KV rows, attention o_proj,
+// o_proj the MLP's gate/up, gate/up the down projection, down the next
+// layer's q/k/v (after the last layer, the first bytes of the head).
 int run_layer(lumina_model* m, int l, int n, const float* bias) {
   Layer& Ly = m->L[l];
   const int d = m->d, nh = m->nh, nkv = m->nkv, hd = m->hd;
   const int qw = nh * hd, kw = nkv * hd, width = qw + 2 * kw;
   cudaStream_t s = m->stream;
-  const bool tp = m->comm != nullptr;
+  const bool tp = m->c.tp_size > 1;
+  L2Prefetch pf_kv;
+  const unsigned kv_block_bytes = (unsigned)((size_t)nkv * m->c.block_size * hd * kv_es(m));
+  if (kv_block_bytes % 16 == 0) {
+    pf_kv.kc = layer_k(m, l);
+    pf_kv.vc = layer_v(m, l);
+    pf_kv.bt = m->bt_dev;
+    pf_kv.len = &m->P_dev->t_prev;
+    pf_kv.bs = m->c.block_size;
+    pf_kv.block_bytes = kv_block_bytes;
+  }
+  const L2Prefetch pf_o = prefetch_of(Ly.o);
+  const L2Prefetch pf_mlp = Ly.moe_e ? L2Prefetch{} : prefetch_of(Ly.gu ? Ly.gu : Ly.gate);
+  const L2Prefetch pf_down = Ly.moe_e ? L2Prefetch{} : prefetch_of(Ly.down);
+  const L2Prefetch pf_next = l + 1 < m->c.n_layer ? prefetch_of(qkv_weight(m, l + 1)) : head_prefetch(m);
   // 1) h = rmsnorm(x) -> q, k, v; RoPE; K/V appended (chat.py:240-263)
   if (Ly.qkv) {
     RopeKV rk{};
@@ -379,7 +421,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     rk.kv_fp16 = m->c.kv_fp16;
     rk.q_out = m->q_buf;
     rk.row_base = 0;
-    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk));
+    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, &pf_kv));
   } else {
     lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
     const int off[3] = {0, qw, qw + kw};
@@ -392,7 +434,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   const int splits = n > m->split_rows ? 1 : m->max_splits;
   if (n == 1 && !bias) {
     TRY(launch_attention_cluster(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
-                                 m->c.block_size, m->P_dev, m->attn, s));
+                                 m->c.block_size, m->P_dev, m->attn, s, &pf_o));
   } else {
     TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
                          m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml,
@@ -400,11 +442,10 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   }
   // 3) o_proj + residual (chat.py:282-283)
   if (tp) {
-    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->part, d, EPI_STORE, nullptr, 0, nullptr));
-    TRY(allreduce(m, m->part, (size_t)n * d));
-    TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, exch_slot_ptr(m, 0), d, EPI_STORE, nullptr, 0, nullptr, &pf_mlp));
+    TRY(peer_exchange(m, 0, PEER_SUM, (size_t)n * d, m->x));
   } else {
-    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, &pf_mlp));
   }
   // 4) rmsnorm -> virtual-MoE MLP (chat.py:284-299), residual in place
   if (Ly.moe_e) {
@@ -414,40 +455,39 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
-    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr));
+    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr,
+                 &pf_down));
   } else {
     TRY(gemv_any(m, Ly.gate, m->x, d, n, Ly.post_norm, m->g_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(gemv_any(m, Ly.up, m->x, d, n, Ly.post_norm, m->u_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(launch_swiglu(m->g_buf, m->u_buf, m->ffn_buf, n, m->ffn, m->ffn, s));
   }
   if (tp) {
-    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->part, d, EPI_STORE, nullptr, 0, nullptr));
-    TRY(allreduce(m, m->part, (size_t)n * d));
-    TRY(add_inplace(m, m->x, m->part, (size_t)n * d));
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, exch_slot_ptr(m, 1), d, EPI_STORE, nullptr, 0, nullptr,
+                 &pf_next));
+    TRY(peer_exchange(m, 1, PEER_SUM, (size_t)n * d, m->x));
   } else {
-    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr));
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, &pf_next));
   }
   return LUMINA_OK;
 }
 
 // head logits of `rows` rows starting at x row `first` (chat.py:388: no final
-// norm). Vocab-parallel under TP: each rank computes its slice, then an
-// all-gather assembles [rank0 | rank1 | ...].
+// norm). Vocab-parallel under TP: each rank computes its slice, then the peer
+// gather assembles [rank0 | rank1 | ...].
 int run_head(lumina_model* m, int first, int rows, unsigned long long* amax = nullptr) {
   const int V = m->head_rows;
-  if (!m->comm) {
+  // the next token's first GEMV (layer 0 q/k/v) into L2 meanwhile
+  const L2Prefetch pf = prefetch_of(qkv_weight(m, 0));
+  if (m->c.tp_size <= 1) {
     return launch_dense_gemv(m->head, V, m->d, m->x + (size_t)first * m->d, m->d, rows, m->logits, V, nullptr, 0,
-                             m->stream, amax);
+                             m->stream, amax, &pf);
   }
   const int tp = m->c.tp_size;
   for (int r = 0; r < rows; ++r) {
-    TRY(launch_dense_gemv(m->head, V, m->d, m->x + (size_t)(first + r) * m->d, m->d, 1, m->part, V, nullptr, 0,
-                          m->stream));
-    ncclResult_t e = ncclAllGather(m->part, m->logits + (size_t)r * V * tp, V, ncclFloat32, m->comm, m->stream);
-    if (e != ncclSuccess) {
-      set_error("ncclAllGather: %s", ncclGetErrorString(e));
-      return LUMINA_E_NCCL;
-    }
+    TRY(launch_dense_gemv(m->head, V, m->d, m->x + (size_t)(first + r) * m->d, m->d, 1, exch_slot_ptr(m, 2), V,
+                          nullptr, 0, m->stream, nullptr, r == 0 ? &pf : nullptr));
+    TRY(peer_exchange(m, 2, PEER_GATHER, (size_t)V, m->logits + (size_t)r * V * tp));
   }
   return LUMINA_OK;
 }
@@ -476,6 +516,15 @@ int check_ready(const lumina_model* m) {
   }
   if (!m->finalized) {
     set_error("model not finalized");
+    return LUMINA_E_STATE;
+  }
+  return LUMINA_OK;
+}
+
+// a forward of a tensor-parallel shard needs its peers
+int check_peers(const lumina_model* m) {
+  if (m->c.tp_size > 1 && !m->peers_ready) {
+    set_error("tensor-parallel model: lumina_model_init_peers has not run");
     return LUMINA_E_STATE;
   }
   return LUMINA_OK;
@@ -571,7 +620,7 @@ int capture_step(lumina_model* m) {
       rc = LUMINA_E_CUDA;
       break;
     }
-    const bool fused_argmax = m->comm == nullptr;
+    const bool fused_argmax = m->c.tp_size <= 1;
     if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
                            fused_argmax ? m->amax_key_dev : nullptr, s)))
       break;
@@ -630,7 +679,7 @@ int capture_chain(lumina_model* m) {
   LUMINA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = LUMINA_OK;
   const int V = m->head_rows * std::max(1, m->c.tp_size);
-  const bool fused_argmax = m->comm == nullptr;
+  const bool fused_argmax = m->c.tp_size <= 1;
   do {
     if ((rc = launch_embed(m->embed, m->d, m->embed_rows, m->tokens_dev, m->P_dev, m->x, 1,
                            fused_argmax ? m->amax_key_dev : nullptr, s)))
@@ -969,6 +1018,17 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
   TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
+  if (c.tp_size > 1) {
+    // the exchange region other ranks map (peer.cu): flags, then three slots
+    // (o_proj sums, down_proj sums, a logits shard) of this rank's contribution
+    static_assert(PEER_CTAS * PEER_MAX * 4 <= PEER_FLAG_BYTES, "exchange flags");
+    LUMINA_CHECK_ARG(c.tp_size <= PEER_MAX, "model_finalize: tp_size %d > %d", c.tp_size, PEER_MAX);
+    m->exch_slot = (std::max((size_t)R * m->d, (size_t)m->head_rows) + 63) / 64 * 64;
+    TRY(dalloc(m, (void**)&m->exch, PEER_FLAG_BYTES + 3 * m->exch_slot * 4));
+    LUMINA_CUDA_TRY(cudaMemset(m->exch, 0, PEER_FLAG_BYTES));
+    TRY(dalloc(m, (void**)&m->peer_epoch, PEER_CTAS * 4));
+    LUMINA_CUDA_TRY(cudaMemset(m->peer_epoch, 0, PEER_CTAS * 4));
+  }
   if (any_moe) {
     TRY(moe_prepare(m->d));
     TRY(dalloc(m, (void**)&m->moe.h, (size_t)R * m->d * 4));
@@ -1009,7 +1069,8 @@ int lumina_model_free(lumina_model* m) {
   if (m->chain_graph) cudaGraphExecDestroy(m->chain_graph);
   if (m->ev0) cudaEventDestroy(m->ev0);
   if (m->ev1) cudaEventDestroy(m->ev1);
-  if (m->comm) ncclCommDestroy(m->comm);
+  for (int r = 0; r < PEER_MAX; ++r)
+    if (m->peer_exch[r] && m->peer_exch[r] != m->exch) cudaIpcCloseMemHandle(m->peer_exch[r]);
   for (Layer& Ly : m->L) {
     if (Ly.qkv) {
       lumina_weight_free(Ly.qkv);
@@ -1042,31 +1103,41 @@ int lumina_model_free(lumina_model* m) {
   return LUMINA_OK;
 }
 
-int lumina_nccl_unique_id(uint8_t* id128) {
-  LUMINA_CHECK_ARG(id128, "nccl_unique_id: null out");
-  ncclUniqueId id;
-  ncclResult_t r = ncclGetUniqueId(&id);
-  if (r != ncclSuccess) {
-    set_error("ncclGetUniqueId: %s", ncclGetErrorString(r));
-    return LUMINA_E_NCCL;
-  }
-  static_assert(sizeof(id.internal) == 128, "ncclUniqueId size");
-  memcpy(id128, id.internal, 128);
+int lumina_model_peer_handle(lumina_model* m, uint8_t* handle64) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(handle64, "model_peer_handle: null out");
+  LUMINA_CHECK_ARG(m->c.tp_size > 1 && m->exch, "model_peer_handle: the model is not tensor-parallel");
+  Guard g(m->device);
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t size");
+  LUMINA_CUDA_TRY(cudaIpcGetMemHandle(&h, m->exch));
+  memcpy(handle64, &h, 64);
   return LUMINA_OK;
 }
 
-int lumina_model_init_tp(lumina_model* m, const uint8_t* id128) {
-  LUMINA_CHECK_ARG(m && id128, "model_init_tp: null pointer");
-  if (m->c.tp_size <= 1) return LUMINA_OK;
+int lumina_model_init_peers(lumina_model* m, const uint8_t* handles) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(handles, "model_init_peers: null handles");
+  LUMINA_CHECK_ARG(m->c.tp_size > 1 && m->exch, "model_init_peers: the model is not tensor-parallel");
+  LUMINA_CHECK_ARG(!m->peers_ready, "model_init_peers: already joined");
   Guard g(m->device);
-  ncclUniqueId id;
-  memcpy(id.internal, id128, 128);
-  ncclResult_t r = ncclCommInitRank(&m->comm, m->c.tp_size, id, m->c.tp_rank);
-  if (r != ncclSuccess) {
-    m->comm = nullptr;
-    set_error("ncclCommInitRank: %s", ncclGetErrorString(r));
-    return LUMINA_E_NCCL;
+  for (int r = 0; r < m->c.tp_size; ++r) {
+    if (r == m->c.tp_rank) {
+      m->peer_exch[r] = m->exch;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handles + (size_t)r * 64, 64);
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_error("model_init_peers: opening rank %d's exchange region: %s", r, cudaGetErrorString(e));
+      return LUMINA_E_CUDA;
+    }
+    m->peer_exch[r] = static_cast<char*>(p);
   }
+  m->peers_ready = true;
   return LUMINA_OK;
 }
 
@@ -1160,6 +1231,7 @@ int lumina_kv_attend(lumina_model* m, int layer, const float* q_host, float* out
 int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int pos0, const int* pos_override_host,
                          const float* bias_host, void* stream) {
   TRY(check_ready(m));
+  TRY(check_peers(m));
   LUMINA_CHECK_ARG(x_dev, "layer_forward: null x");
   LUMINA_CHECK_ARG(layer >= 0 && layer < m->c.n_layer, "layer_forward: layer %d", layer);
   LUMINA_CHECK_ARG(n >= 1 && n <= m->c.max_rows, "layer_forward: %d rows not in [1, %d]", n, m->c.max_rows);
@@ -1200,6 +1272,7 @@ int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int po
 int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0, const int* pos_override_host,
                    const float* bias_host, float* logits_host, int all_rows) {
   TRY(check_ready(m));
+  TRY(check_peers(m));
   LUMINA_CHECK_ARG(tokens_host && n >= 1, "forward: no tokens");
   Guard g(m->device);
   return forward_rows(m, tokens_host, n, pos0, pos_override_host, bias_host, all_rows, logits_host);
@@ -1207,6 +1280,7 @@ int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0, con
 
 int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argmax_host) {
   TRY(check_ready(m));
+  TRY(check_peers(m));
   LUMINA_CHECK_ARG(token >= 0 && token < m->embed_rows, "decode_step: token %d out of range", token);
   Guard g(m->device);
   int len = 0;
@@ -1233,13 +1307,15 @@ int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argm
   const int V = m->head_rows * m->c.tp_size;
   if (logits_host) memcpy(logits_host, m->logits_host, (size_t)V * 4);
   if (argmax_host)
-    *argmax_host = m->comm ? *m->argmax_host : (int)(0xFFFFFFFFu - (unsigned)(*m->amax_key_host & 0xFFFFFFFFull));
+    *argmax_host = m->c.tp_size > 1 ? *m->argmax_host
+                                    : (int)(0xFFFFFFFFu - (unsigned)(*m->amax_key_host & 0xFFFFFFFFull));
   return LUMINA_OK;
 }
 
 int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, float* device_ms,
                          int* kernels_per_step) {
   TRY(check_ready(m));
+  TRY(check_peers(m));
   LUMINA_CHECK_ARG(token >= 0 && token < m->embed_rows, "decode_greedy: token %d out of range", token);
   LUMINA_CHECK_ARG(n >= 1 && tokens_host, "decode_greedy: bad n / output");
   Guard g(m->device);
@@ -1290,7 +1366,10 @@ int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* l
       const int ldx[4] = {d, qw, d, m->ffn};
       const int nproj = Ly.moe_e ? 2 : 4;  // a virtual-MoE MLP is not a packed GEMV
       for (int i = 0; i < nproj; ++i) {
-        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr));
+        // each GEMV pulls the next one's weights into L2, as in the decode step
+        const lumina_weight* nxt = i + 1 < nproj ? ws[i + 1] : qkv_weight(m, (l + 1) % m->c.n_layer);
+        const L2Prefetch pf = prefetch_of(nxt);
+        TRY(gemv_any(m, ws[i], xs[i], ldx[i], 1, norms[i], ys[i], lds[i], epis[i], nullptr, 0, nullptr, &pf));
         if (count) {
           ++launches;
           const int out_rows = epis[i] == EPI_SWIGLU ? ws[i]->rows / 2 : ws[i]->rows;

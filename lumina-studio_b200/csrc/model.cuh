@@ -70,7 +70,8 @@ int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const v
 constexpr int ATTNC_CLUSTER = 8;
 constexpr int ATTNC_CHUNK = 64;
 int launch_attention_cluster(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                             const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s);
+                             const int* bt, int bs, const DevParams* P, float* out, cudaStream_t s,
+                             const L2Prefetch* pf = nullptr);
 
 // Virtual-MoE MLP (moe.cu): router scores, gate/up + SwiGLU of the picked
 // experts, transposed down projection + residual, in place on x.
@@ -106,8 +107,27 @@ int moe_check(const MoeLayerArgs& a);
 int moe_prepare(int d);
 int launch_moe(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s);
 
+// Tensor-parallel exchange over peer memory (peer.cu).
+constexpr int PEER_MAX = 8;        // ranks
+constexpr int PEER_CTAS = 32;      // CTAs of every exchange (each owns one flag slot per rank)
+constexpr int PEER_THREADS = 256;
+constexpr size_t PEER_FLAG_BYTES = 4096;  // PEER_CTAS x PEER_MAX u32, padded
+enum { PEER_SUM = 0, PEER_GATHER = 1 };
+struct PeerArgs {
+  const float* slot[PEER_MAX];  // this exchange's slot on every rank (rank order)
+  unsigned* flags[PEER_MAX];    // every rank's flag array
+  unsigned* epoch;              // this rank's per-CTA exchange counters
+  int tp, rank;
+  size_t n;                     // floats per rank's contribution
+  float* out;                   // PEER_SUM: x += sum (n floats); PEER_GATHER: tp * n floats
+  int* fault;
+  unsigned long long timeout_ns;
+};
+int launch_peer_exchange(const PeerArgs& a, int mode, cudaStream_t s);
+
 int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, int batch, float* y, int ldy,
-                      const float* resid, int ldr, cudaStream_t s, unsigned long long* amax = nullptr);
+                      const float* resid, int ldr, cudaStream_t s, unsigned long long* amax = nullptr,
+                      const L2Prefetch* pf = nullptr);
 int launch_gather_rows(const lumina_weight& out, const lumina_weight& s0, const lumina_weight& s1,
                        const lumina_weight& s2, const int* sel, const int* srow, cudaStream_t s);
 int launch_swiglu(const float* g, const float* u, float* o, int n, int ffn, int ld, cudaStream_t s);

@@ -247,13 +247,14 @@ template <int NB, int EPI>
 __global__ void __launch_bounds__(256)
 dense_gemv_kernel(const __half* __restrict__ W, int N, int K, const float* __restrict__ x, int ldx,
                   float* __restrict__ y, int ldy, const float* __restrict__ resid, int ldr,
-                  unsigned long long* __restrict__ amax) {
+                  unsigned long long* __restrict__ amax, L2Prefetch pf) {
   unsigned long long best = 0ull;
   constexpr int R = 2;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n_tasks = (N + R - 1) / R;
   const int n8 = K / 8;
   pdl_launch_dependents();
+  if (lane == 0) l2_prefetch_share(pf, blockIdx.x * 8 + warp, gridDim.x * 8);
   bool waited = false;
   for (int task = blockIdx.x * 8 + warp; task < n_tasks; task += gridDim.x * 8) {
     const int row0 = task * R;
@@ -539,7 +540,8 @@ int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const v
 }
 
 int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, int batch, float* y, int ldy,
-                      const float* resid, int ldr, cudaStream_t s, unsigned long long* amax) {
+                      const float* resid, int ldr, cudaStream_t s, unsigned long long* amax, const L2Prefetch* pf) {
+  const L2Prefetch none;
   if (K % 8) {
     set_error("dense gemv: K=%d must be a multiple of 8", K);
     return LUMINA_E_UNSUPPORTED;
@@ -555,7 +557,7 @@ int launch_dense_gemv(const __half* W, int N, int K, const float* x, int ldx, in
     const float* rp = resid ? resid + (size_t)done * ldr : nullptr;
 #define DG(NB_, E_) \
   RET_LAUNCH(launch_pdl(dense_gemv_kernel<NB_, E_>, dim3(grid), dim3(256), 0, s, W, N, K, xp, ldx, yp, ldy, rp, ldr, \
-                        done == 0 ? amax : nullptr))
+                        done == 0 ? amax : nullptr, (done == 0 && pf) ? *pf : none))
     if (resid) {
       if (nb == 4) DG(4, EPI_RESID); else if (nb == 2) DG(2, EPI_RESID); else DG(1, EPI_RESID);
     } else {

@@ -49,6 +49,22 @@ struct lumina_weight {
 
 namespace lumina {
 
+// device bytes of the codes and of the scales of a weight
+inline size_t weight_code_bytes(const lumina_weight& w) { return (size_t)w.rows_pad * w.row_bytes; }
+inline size_t weight_scale_bytes(const lumina_weight& w) {
+  return w.mma ? (size_t)w.rows_pad * w.n_groups * (w.fp16_scales ? 2 : 4) : (size_t)w.rows_pad * w.spr;
+}
+// an L2 prefetch of a whole weight (codes and scales)
+inline L2Prefetch prefetch_of(const lumina_weight* w) {
+  L2Prefetch pf;
+  if (!w) return pf;
+  pf.p[0] = w->codes;
+  pf.n[0] = weight_code_bytes(*w) & ~size_t(15);
+  pf.p[1] = w->scales;
+  pf.n[1] = weight_scale_bytes(*w) & ~size_t(15);
+  return pf;
+}
+
 template <int BITS>
 struct Layout {
   static constexpr int CHUNK_WORDS = (BITS == 3) ? 12 : 4;
@@ -155,8 +171,10 @@ int gemv_mma_launch(const lumina_weight* w, const float* x, int ldx, int batch, 
 // int4 decode GEMV on the tensor pipe (gemv_tc.cu), batch 1, 2 or 4 (3 runs
 // as 4), weights in the fragment layout with group = 64 * 2^k.
 // LUMINA_E_UNSUPPORTED when the shape does not fit.
+// `pf` (may be null): the next kernel's bytes to pull into L2 meanwhile.
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
-                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk);
+                   float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
+                   const L2Prefetch* pf = nullptr);
 
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);

@@ -87,8 +87,8 @@ SIGNATURES = {
     "lumina_model_set_moe": [_VP, _I, _I, _I, _I],
     "lumina_model_finalize": [_VP],
     "lumina_model_free": [_VP],
-    "lumina_nccl_unique_id": [_U8P],
-    "lumina_model_init_tp": [_VP, _U8P],
+    "lumina_model_peer_handle": [_VP, _U8P],
+    "lumina_model_init_peers": [_VP, _U8P],
     "lumina_kv_length": [_VP, _I, _IP],
     "lumina_kv_truncate": [_VP, _I],
     "lumina_kv_read": [_VP, _I, _I, _I, _FP, _FP],

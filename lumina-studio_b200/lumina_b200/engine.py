@@ -11,10 +11,12 @@ Mirrors the interface of src/lumina_framework/chat.py for this path:
     per-layer drop-in (chat.py:232-304); ``cache`` is the model's
     ``DeviceKV``, whose ``cache[lyr] = (k, v)`` entries expose ``.shape``,
     ``[:n]`` and ``np.asarray`` like the reference's numpy tuples.
-  * ``generate`` / ``generate_cached`` / ``verify_tree`` /
-    ``commit_verified`` — the reference drivers (chat.py:307-551,
-    eagle.py:259-357) with the KV slicing and row gathers done as block-table
-    operations on the device; the sampler ``pick`` stays on the host.
+  * ``generate`` / ``generate_cached`` / ``generate_spec`` / ``verify_tree``
+    / ``commit_verified`` — replacements of the reference drivers
+    (chat.py:307-648, eagle.py:259-357) with the KV slicing and row gathers
+    done as block-table operations on the device; the sampler ``pick`` stays
+    on the host. The reference's own drivers build a numpy ``cache`` dict
+    and cannot run on this model, so these are the drivers to call.
 
 There is no CPU path: without the CUDA library these raise ``LuminaError``.
 """
@@ -121,18 +123,20 @@ class DeviceKV:
         return self.model.kv_read(lyr, start, n)
 
 
-def share_nccl_id(uid: bytes, group=None) -> bytes:
-    """Rank 0's 128-byte NCCL id, handed to every rank of the
-    torch.distributed group (the other ranks' ``uid`` is ignored). A rank
-    that never joins, or a rank 0 that died, makes this raise -- a
-    connection error, or the group's timeout -- instead of waiting forever;
-    create the group with a short timeout."""
+def gather_peer_handles(handle: bytes, group=None) -> list:
+    """Every rank's 64-byte exchange-region handle, in rank order, over the
+    torch.distributed group. A rank that never joins (or died) makes this
+    raise -- a connection error, or the group's timeout -- instead of waiting
+    forever; create the group with a short timeout."""
     import torch.distributed as dist
-    box = [bytes(uid)]
-    dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0, group=group)
-    if not isinstance(box[0], (bytes, bytearray)) or len(box[0]) != 128:
-        raise LuminaError(5, "NCCL id exchange returned %r" % type(box[0]).__name__)
-    return bytes(box[0])
+    if not isinstance(handle, (bytes, bytearray)) or len(handle) != 64:
+        raise LuminaError(1, "peer handle must be 64 bytes")
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    for r, h in enumerate(out):
+        if not isinstance(h, (bytes, bytearray)) or len(h) != 64:
+            raise LuminaError(5, "peer handle exchange: rank %d sent %r" % (r, type(h).__name__))
+    return [bytes(h) for h in out]
 
 
 def moe_map_from_header(header: dict) -> dict:
@@ -313,18 +317,19 @@ class CudaChatModel:
         return obj
 
     def init_tp(self, group=None):
-        """Join this model's NCCL communicator: rank 0 of the torch.distributed
-        group makes the NCCL id, every rank receives it over the group and
-        joins (the library's all-reduces after o_proj / down_proj and the
-        logits all-gather use it). No-op when the model is not sharded."""
+        """Join the other ranks of this tensor-parallel model: every rank's
+        exchange-region handle goes to every rank over the torch.distributed
+        group (rank r of the group must hold shard tp_rank = r), and each
+        rank maps its peers' regions; the sums after o_proj / down_proj and
+        the logits gather then run over peer memory. No-op when the model is
+        not sharded."""
         if self.tp_size <= 1:
             return
-        import torch.distributed as dist
-        uid = (ctypes.c_uint8 * 128)()
-        if dist.get_rank(group) == 0:
-            check(self.lib.lumina_nccl_unique_id(uid), self.lib)
-        uid = (ctypes.c_uint8 * 128).from_buffer_copy(share_nccl_id(bytes(uid), group))
-        check(self.lib.lumina_model_init_tp(self.h, uid), self.lib)
+        h = (ctypes.c_uint8 * 64)()
+        check(self.lib.lumina_model_peer_handle(self.h, h), self.lib)
+        allh = b"".join(gather_peer_handles(bytes(h), group))
+        buf = (ctypes.c_uint8 * len(allh)).from_buffer_copy(allh)
+        check(self.lib.lumina_model_init_peers(self.h, buf), self.lib)
 
     def close(self):
         if getattr(self, "h", None):
@@ -596,6 +601,92 @@ def generate_cached(model: CudaChatModel, prompt, max_tokens: int = 32, budget_s
             "tokens_per_second": len(out) / dt if dt else 0.0, "seconds": dt,
             "stats": {"steps": steps, "prefill_reused": reused, "prefill_computed": len(delta)},
             "cache_state": st}
+
+
+# ---------------------------------------------------------------------------
+# prompt-lookup speculative decoding (chat.py:553-648)
+# ---------------------------------------------------------------------------
+def pld_draft(ids: list, n: int = 4, gram: int = 3) -> list:
+    """The continuation of the latest earlier occurrence of the last ``gram``
+    tokens, up to ``n`` tokens; [] when there is none (chat.py:553-569)."""
+    if len(ids) < gram + 1:
+        return []
+    key = ids[-gram:]
+    for i in range(len(ids) - gram - 1, -1, -1):
+        if ids[i:i + gram] == key:
+            cont = ids[i + gram:i + gram + n]
+            if cont:
+                return cont
+    return []
+
+
+def _spec_stats(drafted, accepted, target_forwards, tokens_out):
+    """SpecStats.as_dict (spec.py:26-53) for the counters this driver keeps."""
+    return {"drafted": drafted, "accepted": accepted,
+            "acceptance_rate": accepted / drafted if drafted else 0.0,
+            "tokens_per_target_forward": tokens_out / target_forwards if target_forwards else 0.0,
+            "target_forwards": target_forwards, "draft_forwards": 0, "tokens_out": tokens_out,
+            "seconds_draft": 0.0, "seconds_verify": 0.0}
+
+
+def generate_spec(model: CudaChatModel, prompt, max_tokens: int = 32, budget_s: float = 300.0,
+                  stop_ids: tuple = (151643,), draft_n: int = 4, rng=None) -> dict:
+    """chat.generate_spec (chat.py:572-648) on the device: prompt-lookup
+    drafts verified by one multi-row forward (the draft rows' logits come
+    back from the device), greedy acceptance, and the rollback of
+    chat.py:636-638 as a KV truncation (a block-table length edit) before the
+    bonus token's single-row forward. Replaces the reference driver, whose
+    ``cache`` is a numpy dict; tokens and accounting are the reference's."""
+    t0 = time.perf_counter()
+    drafted_n = accepted_n = forwards = tokens_out = 0
+    ids = model.tok.encode(prompt)
+    model.kv_truncate(0)
+    h_lg = model.forward(ids, 0)[0]
+    pos, out = len(ids), []
+    while len(out) < max_tokens and time.perf_counter() - t0 < budget_s:
+        drafted = pld_draft(ids + out, draft_n)
+        if not drafted:
+            nxt = int(np.argmax(h_lg))
+            if nxt in stop_ids:
+                break
+            out.append(nxt)
+            h_lg, _ = model.decode_step(nxt)
+            h_lg = h_lg.copy()
+            pos += 1
+            forwards += 1
+            tokens_out += 1
+            continue
+        drafted_n += len(drafted)
+        t_lg = model.forward(drafted, pos, all_rows=True)
+        forwards += 1
+        acc = []
+        bonus = int(np.argmax(t_lg[-1]))
+        for k, tok in enumerate(drafted):
+            pred = h_lg if k == 0 else t_lg[k - 1]
+            if int(np.argmax(pred)) == tok:
+                acc.append(tok)
+            else:
+                bonus = int(np.argmax(pred))
+                break
+        accepted_n += len(acc)
+        tokens_out += len(acc) + 1
+        for a in acc + [bonus]:
+            if a in stop_ids:
+                out.append(a)
+                dt = time.perf_counter() - t0
+                return {"text": model.tok.decode(out), "tokens": out,
+                        "spec": _spec_stats(drafted_n, accepted_n, forwards, tokens_out),
+                        "tokens_per_second": len(out) / dt if dt else 0.0, "seconds": dt}
+            out.append(a)
+        model.kv_truncate(pos + len(acc))
+        h_lg = model.forward([bonus], pos + len(acc))[0]
+        forwards += 1
+        pos += len(acc) + 1
+    dt = time.perf_counter() - t0
+    out = out[:max_tokens]
+    return {"text": model.tok.decode(out), "tokens": out,
+            "spec": _spec_stats(drafted_n, accepted_n, forwards, tokens_out),
+            "tokens_per_second": len(out) / dt if dt else 0.0, "seconds": dt}
 
 
 # ---------------------------------------------------------------------------

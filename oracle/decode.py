@@ -18,6 +18,7 @@ by the reference itself):
     ±40 clip :300-304, virtual-MoE branch :285-299)
   * ``generate`` / ``generate_cached``  chat.py:307-407, 410-551 (greedy
     ``pick`` path; no final norm before the head, :388/:529)
+  * ``pld_draft`` / ``generate_spec``  chat.py:553-648
   * ``build_tree_mask`` spec.py:56-83; ``verify_tree`` eagle.py:259-291;
     ``commit_verified`` eagle.py:294-357
   * ``moe_grouped_forward`` qwen_next.py:31-78 (unit weights)
@@ -267,6 +268,79 @@ def generate_cached(model: OracleModel, ids: list[int], max_tokens: int,
     st["ids"] = list(ids) + out
     st["pos"] = pos
     return out, {"prefill_reused": reused, "prefill_computed": len(delta)}, st
+
+
+def pld_draft(ids: list[int], n: int = 4, gram: int = 3) -> list[int]:
+    """Prompt-lookup draft (chat.py:553-569)."""
+    if len(ids) < gram + 1:
+        return []
+    key = ids[-gram:]
+    for i in range(len(ids) - gram - 1, -1, -1):
+        if ids[i:i + gram] == key:
+            cont = ids[i + gram:i + gram + n]
+            if cont:
+                return cont
+    return []
+
+
+def generate_spec(model: OracleModel, ids: list[int], max_tokens: int,
+                  draft_n: int = 4, stop_ids=(151643,)):
+    """Greedy ``generate_spec`` (chat.py:572-648): prompt-lookup drafts,
+    one multi-row verify, acceptance by argmax, rollback of the KV to the
+    accepted prefix (:636-638) and a single-row forward of the bonus token.
+    Returns (tokens, [drafted, accepted, target_forwards, tokens_out])."""
+    emb, head = model.embed(), model.head_t()
+    cache: dict = {}
+    h = emb[np.array(ids)]
+    for lyr in range(model.n_layer):
+        h = model.layer(h, lyr, cache, 0)
+    pos, out = len(ids), []
+    drafted_n = accepted_n = forwards = tokens_out = 0
+    while len(out) < max_tokens:
+        drafted = pld_draft(ids + out, draft_n)
+        if not drafted:
+            nxt = int(np.argmax((h[-1:] @ head)[0]))
+            if nxt in stop_ids:
+                break
+            out.append(nxt)
+            h = emb[[nxt]]
+            for lyr in range(model.n_layer):
+                h = model.layer(h, lyr, cache, pos)
+            pos += 1
+            forwards += 1
+            tokens_out += 1
+            continue
+        drafted_n += len(drafted)
+        hh = emb[np.array(drafted)]
+        for lyr in range(model.n_layer):
+            hh = model.layer(hh, lyr, cache, pos)
+        forwards += 1
+        t_lg = hh @ head
+        h_lg = (h[-1:] @ head)[0]
+        acc = []
+        bonus = int(np.argmax(t_lg[-1]))
+        for k, tok in enumerate(drafted):
+            pred = h_lg if k == 0 else t_lg[k - 1]
+            if int(np.argmax(pred)) == tok:
+                acc.append(tok)
+            else:
+                bonus = int(np.argmax(pred))
+                break
+        accepted_n += len(acc)
+        tokens_out += len(acc) + 1
+        for a in acc + [bonus]:
+            out.append(a)
+            if a in stop_ids:
+                return out, [drafted_n, accepted_n, forwards, tokens_out]
+        for lyr in range(model.n_layer):
+            k, v = cache[lyr]
+            cache[lyr] = (k[:pos + len(acc)], v[:pos + len(acc)])
+        h = emb[[bonus]]
+        for lyr in range(model.n_layer):
+            h = model.layer(h, lyr, cache, pos + len(acc))
+        forwards += 1
+        pos += len(acc) + 1
+    return out[:max_tokens], [drafted_n, accepted_n, forwards, tokens_out]
 
 
 def build_tree_mask(parents):

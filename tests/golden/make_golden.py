@@ -372,6 +372,26 @@ def make_moe(ref, tmp):
     print("moe tokens[:8]", r["tokens"][:8], "min route gap %.3g" % min(gaps))
 
 
+def make_spec(ref, tmp):
+    """Prompt-lookup speculative decoding (chat.generate_spec, chat.py:
+    572-648) on the tiny model: a prompt whose tail repeats an earlier span
+    (so the first drafts come from the prompt), 48 tokens, drafts of 4.
+    Records the tokens and the SpecStats counters."""
+    from lumina_framework.chat import ChatModel, generate_spec
+
+    cfg = synthetic.TINY
+    tensors, _, _ = tiny_lumina(tmp)
+    model = ChatModel.from_tensors(tensors, synthetic.hf_cfg(cfg), StubTok(), theta=cfg["rope_theta"])
+    p = synthetic.prompt_ids(cfg, 64, seed=0)
+    prompt = p[:40] + p[8:20]
+    r = generate_spec(model, prompt, max_tokens=48, draft_n=4, rng=np.random.default_rng(0))
+    sp = r["spec"]
+    out = {"prompt": np.array(prompt), "tokens": np.array(r["tokens"]),
+           "counts": np.array([sp["drafted"], sp["accepted"], sp["target_forwards"], sp["tokens_out"]])}
+    np.savez_compressed(os.path.join(HERE, "tiny_spec.npz"), **out)
+    print("spec tokens[:8]", r["tokens"][:8], "drafted/accepted/forwards/out", out["counts"].tolist())
+
+
 WIDE = {"seed": 0, "prompt": 17, "forced": 2, "greedy": 6}
 
 
@@ -427,7 +447,7 @@ def make_wide(ref, tmp):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=("format", "tiny", "tops", "moe", "wide"), default=None,
+    ap.add_argument("--only", choices=("format", "tiny", "tops", "moe", "wide", "spec"), default=None,
                     help="regenerate one fixture family (tiny includes the EAGLE fixture)")
     args = ap.parse_args()
     ref = args.reference
@@ -447,6 +467,8 @@ def main():
             make_moe(ref, tmp)
         if want("wide"):
             make_wide(ref, tmp)
+        if want("spec"):
+            make_spec(ref, tmp)
 
 
 if __name__ == "__main__":

@@ -91,6 +91,21 @@ def test_prefix_cache_scenarios(model, golden):
         assert len(st["ids"]) == model.kv_length()
 
 
+def test_generate_spec_matches_reference(model, golden):
+    """Prompt-lookup speculative decoding (chat.generate_spec) on the device:
+    the reference's tokens and its drafted / accepted / forward counts; the
+    rollbacks are KV truncations, and the KV ends one row past the last
+    accepted token as in the reference."""
+    from lumina_b200.engine import generate_spec
+    g = golden("tiny_spec.npz")
+    prompt = [int(t) for t in g["prompt"]]
+    r = generate_spec(model, prompt, max_tokens=48, draft_n=4)
+    assert r["tokens"] == [int(t) for t in g["tokens"]]
+    sp = r["spec"]
+    assert [sp["drafted"], sp["accepted"], sp["target_forwards"], sp["tokens_out"]] == [int(c) for c in g["counts"]]
+    assert sp["drafted"] > 0 and sp["accepted"] > 0
+
+
 def test_kv_block_indexing_bit_exact(model):
     """Truncation and re-append land rows at the same page slots: decode
     steps repeated after a truncation (mid-page and on a page boundary)

@@ -1,6 +1,6 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): the tiny int4
-model sharded over two ranks (heads, group-aligned FFN slices, vocab), NCCL
-all-reduce after o_proj / down_proj and an all-gather of the logits, must
+model sharded over two ranks (heads, group-aligned FFN slices, vocab), the
+peer-memory sums after o_proj / down_proj and the logits gather, must
 reproduce the reference's recorded logits (2e-3 relative L2), the TP=1
 model's greedy tokens, and each rank's KV heads."""
 import os

@@ -10,7 +10,7 @@ from conftest import GOLDEN
 from oracle import lumina_format as lf
 from oracle import quant, tops
 from oracle.decode import (OracleModel, build_tree_mask, commit_rows, generate,
-                           generate_cached, verify_tree)
+                           generate_cached, generate_spec, verify_tree)
 from lumina_b200 import synthetic
 
 
@@ -151,6 +151,13 @@ def test_prefix_cache_scenarios(golden, tiny_model):
         toks, stats, st = generate_cached(tiny_model, p, n, state=st)
         assert toks == [int(t) for t in g[f"cached{j}_tokens"]]
         assert [stats["prefill_reused"], stats["prefill_computed"]] == list(g[f"cached{j}_stats"])
+
+
+def test_spec_decode_matches_reference(golden, tiny_model):
+    g = golden("tiny_spec.npz")
+    toks, counts = generate_spec(tiny_model, [int(t) for t in g["prompt"]], 48, draft_n=4)
+    assert toks == [int(t) for t in g["tokens"]]
+    assert counts == [int(c) for c in g["counts"]]
 
 
 def test_tree_mask_and_verify(golden, tiny_model):

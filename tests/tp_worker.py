@@ -1,7 +1,7 @@
 """One rank of the tensor-parallel decode check (run under torchrun by
-tests/test_gpu_tp.py): builds its shard of the tiny int4 model, joins the
-NCCL communicator, runs prefill, teacher-forced steps and a device-chained
-greedy run, and writes its results to <out>.rank<r>.npz."""
+tests/test_gpu_tp.py): builds its shard of the tiny int4 model, maps the
+other rank's exchange region, runs prefill, teacher-forced steps and a
+device-chained greedy run, and writes its results to <out>.rank<r>.npz."""
 import os
 import sys
 
