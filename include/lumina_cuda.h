@@ -88,6 +88,17 @@ int lumina_weight_dequant(const lumina_weight* w, float* out_dev, void* stream);
  * one device race on it). */
 int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx,
                 float* y_dev, int ldy, void* stream);
+/* y[m, n] = sum_k x[m, k] * W[n, k] for `rows` hidden rows at once (any
+ * count): the projection of a prompt prefill or a tree verification, where
+ * ChatModel._layer runs h @ W with sq > 1 (chat.py:239-243). Built for int4
+ * weights in the tensor-core fragment layout (LUMINA_E_UNSUPPORTED
+ * otherwise): the codes are turned into the reference's fp16 weights in
+ * shared memory (chat.py:140 rounds the dequantized weights to fp16), x is
+ * rounded to fp16, and tcgen05 tensor cores accumulate in fp32. Uses a
+ * per-device fp16 activation scratch the library grows on demand (calls that
+ * overlap on the GPU on one device race on it). Asynchronous on `stream`. */
+int lumina_gemm_rows(const lumina_weight* w, const float* x_dev, int rows, int ldx,
+                     float* y_dev, int ldy, void* stream);
 /* Same contraction with host buffers; copies in, runs, copies out, syncs. */
 int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, float* y_host);
 
@@ -109,14 +120,16 @@ int lumina_gemv_host(const lumina_weight* w, const float* x_host, int batch, flo
 int lumina_gemv_noalloc(const lumina_weight* w, const float* x_dev, int batch, int ldx,
                         float* y_dev, int ldy, void* stream);
 
-/* Timeouts. Kernels that wait on their own shared-memory transfers (the
- * decode GEMVs) bound every wait; one that gives up ORs a bit into a
- * per-device fault word and returns, leaving its outputs unwritten. Every
+/* Timeouts. Kernels that wait on their own asynchronous transfers or on
+ * peers (the decode GEMVs, the tcgen05 multi-row projection, the
+ * tensor-parallel exchange) bound every wait; one that gives up ORs a bit
+ * into a per-device fault word (1: gemv_fused, 2: gemv_tc, 4: peer exchange,
+ * 8: gemm_tc05) and returns, leaving its outputs unwritten. Every
  * synchronous entry (lumina_gemv_host, lumina_forward, lumina_layer_forward,
  * lumina_decode_step, lumina_decode_greedy, lumina_profile_gemv) clears the
  * word as it starts and returns LUMINA_E_CUDA ("a device wait timed out")
- * when it is set at the end. lumina_gemv and lumina_gemv_noalloc are
- * asynchronous: after synchronizing their stream, the caller reads (and with
+ * when it is set at the end. lumina_gemv, lumina_gemm_rows and
+ * lumina_gemv_noalloc are asynchronous: after synchronizing their stream, the caller reads (and with
  * `clear`, resets) the word here. The tops-style reference reported no
  * errors at all (tops_int8.c: void returns); the dict convention of
  * tops.py:296-314 carries this one to Python callers. */

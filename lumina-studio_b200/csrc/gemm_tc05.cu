@@ -1,0 +1,518 @@
+// Multi-row projection (prompt prefill, tree verification) on the 5th-gen
+// tensor cores: Y[m, n] = sum_k X[m, k] * W[n, k] for M token rows.
+//
+// The reference computes fp32 x @ W16 with W16 the fp16-rounded dequantized
+// weight (adapters/lumina.py:135-150, chat.py:140, chat.py:239-243 at sq > 1).
+// Here W16 is rebuilt on the fly: each K step, the CTA's threads read the
+// int4 codes of 128 weight rows x 64 columns (the tensor-core fragment layout
+// of weights.cuh, one 16-byte load per thread) and their group scales, and
+// write fp16(s * level(c)) into shared memory in the 128-byte-swizzled
+// K-major layout that tcgen05.mma reads; the activations arrive as fp16 rows
+// (act_f16_kernel: RMSNorm fused, K padded to 64) through a TMA tensor map
+// with the same swizzle. One thread issues tcgen05.mma.kind::f16 (M = 128
+// weight rows, N = BN token rows, K = 16, four per K step) accumulating in
+// fp32 in tensor memory across the whole K; tcgen05.commit frees a stage
+// when its MMAs have read it. The K loop keeps STAGES stages in flight: while
+// the tensor pipe works on step kb, the threads dequantize step kb + STAGES
+// - 1 into the stage that step kb - 1 released. After the last step the
+// accumulator goes from tensor memory to registers (tcgen05.ld, one TMEM lane
+// per weight row per thread) and through the epilogue (store, residual add,
+// SwiGLU over interleaved gate/up rows, or the store of q/k/v rows in their
+// original order for the RoPE + KV append kernel).
+//
+// Waits are bounded: a wait that gives up sets bit 3 of the device fault
+// word; the CTA then stops issuing work, lets its TMA loads and MMAs in flight
+// finish (waiting with the default limit), frees its tensor memory and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemv_impl.cuh"
+
+namespace lumina {
+
+namespace {
+
+constexpr int G5_BM = 128;                 // weight rows per CTA (the MMA's M)
+constexpr int G5_BK = 64;                  // K per stage: one 128-byte swizzle row of fp16
+constexpr int G5_STAGES = 4;
+constexpr int G5_THREADS = 256;            // 8 warps: all dequantize, all run the epilogue
+constexpr int G5_A_BYTES = G5_BM * G5_BK * 2;
+
+struct G5Args {
+  const uint8_t* codes;
+  const uint8_t* scales;
+  int rows;     // weight rows (N of the projection)
+  int P;        // K steps (64-column pairs)
+  int ng;       // scale groups per row
+  int gsh;      // log2(group / 64)
+  int T16;      // 16-row tiles of the weight
+  int M;        // token rows
+  float* y;
+  int ldy;
+  const float* resid;
+  int ldr;
+  int epi;      // G5_STORE, G5_RESID, G5_SWIGLU
+  int qk_rows;  // rows < qk_rows hold RoPE pairs adjacent (fused q/k/v): stored at their original index
+  int hd;
+  int* fault;
+  long long spin;
+};
+
+// ---- tcgen05 / TMA building blocks -----------------------------------------
+__device__ __forceinline__ void tc05_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc05_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (stride byte offset), leading byte offset 16 (unused with
+// this swizzle), descriptor version 1
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// instruction descriptor, kind::f16: fp16 A and B (K-major), fp32 D, M x N
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc05_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, int accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// the mbarrier completes one arrival once every tcgen05 op this thread issued so far is done
+__device__ __forceinline__ void tc05_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 16 fp32 columns of this warp's 32 TMEM lanes (one lane = one row per thread)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- dequantization of one K step ------------------------------------------
+// Thread (warp T, lane L = 4g + t) owns the 16-byte fragment word of 16-row
+// tile T at this K step: rows 16T + g (low nibbles) and 16T + g + 8 (high
+// nibbles), columns 32(j >> 1) + 16(j & 1) + 4t + q of byte q of word j.
+// Each run of four columns becomes one 8-byte store of four fp16 values at
+// the 128-byte-swizzled position: row r at r * 128, 16-byte chunk
+// (col / 8) XOR (r mod 8).
+template <typename ST>
+__device__ __forceinline__ void g5_dequant(const G5Args& a, uint8_t* As, int n0, int kb, int tid) {
+  const int T = tid >> 5, L = tid & 31, g = L >> 2, t = L & 3;
+  const int gt = (n0 >> 4) + T;
+  const int r0 = 16 * T + g, r1 = r0 + 8;
+  uint4 q = make_uint4(0u, 0u, 0u, 0u);
+  float s0 = 0.f, s1 = 0.f;
+  if (gt < a.T16) {
+    q = ldg_stream(a.codes + (((size_t)gt * a.P + kb) * 32 + L) * 16);
+    const uint8_t* sp = a.scales + (((size_t)gt * a.ng + (kb >> a.gsh)) * 8 + g) * 2 * sizeof(ST);
+    if constexpr (sizeof(ST) == 2) {
+      const __half2 h = *reinterpret_cast<const __half2*>(sp);
+      s0 = __low2float(h);
+      s1 = __high2float(h);
+    } else {
+      const float2 f = *reinterpret_cast<const float2*>(sp);
+      s0 = f.x;
+      s1 = f.y;
+    }
+  }
+  // w = s * (-1 + c * 2/15) = c * (2s/15) - s (adapters/lumina.py:135-139), in fp32, then fp16
+  const float k0 = s0 * (2.0f / 15.0f), k1 = s1 * (2.0f / 15.0f);
+  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c0 = (j >> 1) * 32 + (j & 1) * 16 + t * 4;
+    const uint32_t lo = words[j] & 0x0F0F0F0Fu, hi = (words[j] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t src = h ? hi : lo;
+      const float kk = h ? k1 : k0, ss = h ? s1 : s0;
+      float f[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        // 0x4B0000cc = 2^23 + c as fp32
+        const float m = __int_as_float((int)__byte_perm(src, 0x4B000000u, 0x7440u + b)) - 8388608.0f;
+        f[b] = fmaf(m, kk, -ss);
+      }
+      const __half2 p0 = __floats2half2_rn(f[0], f[1]), p1 = __floats2half2_rn(f[2], f[3]);
+      const int r = h ? r1 : r0;
+      uint8_t* dst = As + r * 128 + (((c0 >> 3) ^ (r & 7)) << 4) + ((c0 & 7) << 1);
+      asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(smem_u32(dst)), "r"(*reinterpret_cast<const uint32_t*>(&p0)),
+                   "r"(*reinterpret_cast<const uint32_t*>(&p1))
+                   : "memory");
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor pipe
+}
+
+// RoPE pair permutation of the fused q/k/v weight: row 2p + e of a head is
+// the original row p + e * hd / 2
+__device__ __forceinline__ int g5_orig_row(const G5Args& a, int row) {
+  if (row >= a.qk_rows) return row;
+  const int h = row / a.hd, rr = row - h * a.hd;
+  return h * a.hd + (rr >> 1) + (rr & 1) * (a.hd >> 1);
+}
+
+template <int BN, typename ST>
+__global__ void __launch_bounds__(G5_THREADS, 1)
+gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
+  constexpr int S = G5_STAGES;
+  constexpr int B_BYTES = BN * 128;
+  constexpr int STAGE = G5_A_BYTES + B_BYTES;
+  constexpr uint32_t IDESC = idesc_f16(G5_BM, BN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // activation tile landed
+  uint64_t* empty = full_b + S;                                      // stage's MMAs done
+  uint64_t* accum = empty + S;                                       // every MMA done
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_s;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * G5_BM, m0 = blockIdx.y * BN;
+  const int KB = a.P;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_b[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+    abort_s = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // weights never depend on the previous kernel: the first stages' codes go
+  // to shared memory before the dependency wait
+  for (int kb = 0; kb < S - 1 && kb < KB; ++kb) g5_dequant<ST>(a, smem + kb * STAGE, n0, kb, tid);
+  tc05_fence_before();
+  __syncthreads();
+  tc05_fence_after();
+  const uint32_t tmem = tmem_base;
+  pdl_launch_dependents();
+  pdl_wait();
+  int tma_issued = 0;  // thread 0: activation tiles requested
+  if (tid == 0) {
+    for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
+      mbar_expect_tx(&full_b[kb], B_BYTES);
+      tma_load_2d(smem + kb * STAGE + G5_A_BYTES, &tmx, kb * G5_BK, m0, &full_b[kb]);
+      ++tma_issued;
+    }
+  }
+  int tma_waited = 0;  // thread 0: activation tiles that landed and were consumed
+  for (int kb = 0; kb < KB; ++kb) {
+    const int s = kb % S;
+    __syncthreads();  // stage kb's weight tile is written (and fenced) by every thread
+    if (abort_s) break;
+    if (tid == 0) {
+      const bool landed = mbar_wait_bounded(&full_b[s], (uint32_t)((kb / S) & 1), a.spin);
+      if (!landed) {
+        atomicOr(a.fault, 8);
+        abort_s = 1;
+      } else {
+        ++tma_waited;
+        tc05_fence_after();
+        const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + G5_A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G5_BK / 16; ++kk)
+          tc05_mma(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), IDESC, (kb | kk) != 0);
+        tc05_commit(&empty[s]);
+      }
+    }
+    // stage kb + S - 1 into the stage step kb - 1 used, once its MMAs are done
+    const int nk = kb + S - 1;
+    if (nk < KB) {
+      const int ns = nk % S;
+      if (kb >= 1) {
+        const bool freed = mbar_wait_bounded(&empty[ns], (uint32_t)(((kb - 1) / S) & 1), a.spin);
+        if (!__all_sync(0xffffffffu, freed)) {
+          if (lane == 0) {
+            atomicOr(a.fault, 8);
+            abort_s = 1;
+          }
+          continue;  // the next barrier sees the abort
+        }
+      }
+      g5_dequant<ST>(a, smem + ns * STAGE, n0, nk, tid);
+      if (tid == 0) {
+        mbar_expect_tx(&full_b[ns], B_BYTES);
+        tma_load_2d(smem + ns * STAGE + G5_A_BYTES, &tmx, nk * G5_BK, m0, &full_b[ns]);
+        ++tma_issued;
+      }
+    }
+  }
+  __syncthreads();
+  bool ok = !abort_s;
+  if (tid == 0) {
+    if (!ok) {
+      // let every activation load in flight land before the stages go away
+      for (int i = tma_waited; i < tma_issued; ++i) mbar_wait_bounded(&full_b[i % S], (uint32_t)((i / S) & 1));
+    }
+    tc05_commit(accum);  // completes once every MMA issued above is done
+  }
+  const bool done = mbar_wait_bounded(accum, 0u, ok ? a.spin : MBAR_SPIN_LIMIT);
+  if (!done) {
+    if (lane == 0) atomicOr(a.fault, 8);
+    ok = false;
+  }
+  tc05_fence_after();
+  if (__syncthreads_and(ok ? 1 : 0)) {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and
+    // token columns [BN/2 (w / 4), BN/2 (w / 4 + 1))
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = n0 + 32 * quarter + lane;
+    constexpr int COLS = BN / 2;
+    for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+      if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int m = m0 + c0 + j;
+        if (a.epi == G5_SWIGLU) {
+          const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
+          if (m < a.M && !(lane & 1) && row + 1 < a.rows) {
+            const float gt = v[j];
+            const float e = expf(-fminf(fmaxf(gt, -40.f), 40.f));  // chat.py:300-302
+            a.y[(size_t)m * a.ldy + (row >> 1)] = gt / (1.0f + e) * up;
+          }
+        } else if (m < a.M && row < a.rows) {
+          if (a.epi == G5_RESID)
+            a.y[(size_t)m * a.ldy + row] = a.resid[(size_t)m * a.ldr + row] + v[j];
+          else
+            a.y[(size_t)m * a.ldy + g5_orig_row(a, row)] = v[j];
+        }
+      }
+    }
+  }
+  tc05_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+}
+
+// fp32 rows (optionally RMS-normalized, chat.py:63-66) -> fp16 rows of Kpad
+// columns, zeros past K
+template <bool NORM>
+__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int ldx, int K, int Kpad,
+                                                      const float* __restrict__ nw, float eps, __half* __restrict__ out) {
+  __shared__ float red[8];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  const float* xr = x + (size_t)m * ldx;
+  float rinv = 1.f;
+  if constexpr (NORM) {
+    float ss = 0.f;
+    for (int k = tid; k < K; k += 256) ss = fmaf(xr[k], xr[k], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[w];
+    rinv = 1.0f / sqrtf(tot / (float)K + eps);
+  }
+  __half* o = out + (size_t)m * Kpad;
+  for (int k = 2 * tid; k < Kpad; k += 512) {
+    float v0 = 0.f, v1 = 0.f;
+    if (k < K) v0 = NORM ? (xr[k] * rinv) * nw[k] : xr[k];
+    if (k + 1 < K) v1 = NORM ? (xr[k + 1] * rinv) * nw[k + 1] : xr[k + 1];
+    *reinterpret_cast<__half2*>(o + k) = __floats2half2_rn(v0, v1);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::mutex mu;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+template <int BN, typename ST>
+int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s) {
+  auto kern = gemm_tc05_kernel<BN, ST>;
+  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + BN * 128) + (2 * G5_STAGES + 1) * 8 + 1024;
+  const int rc = set_smem_limit((const void*)kern, smem, "gemm_tc05");
+  if (rc) return rc;
+  const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN);
+  const cudaError_t e = launch_pdl(kern, grid, dim3(G5_THREADS), smem, s, map, a);
+  if (e != cudaSuccess) {
+    set_error("gemm_tc05 launch: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+template <typename ST>
+int g5_bn(const CUtensorMap& map, const G5Args& a, int bn, cudaStream_t s) {
+  switch (bn) {
+    case 32: return g5_launch<32, ST>(map, a, s);
+    case 64: return g5_launch<64, ST>(map, a, s);
+    case 128: return g5_launch<128, ST>(map, a, s);
+    default: return g5_launch<256, ST>(map, a, s);
+  }
+}
+
+// per-device fp16 activation rows for lumina_gemm_rows (grown on demand)
+int x16_scratch(int device, size_t elems, __half** out) {
+  static std::mutex mu;
+  static __half* buf[64] = {};
+  static size_t cap[64] = {};
+  if (device < 0 || device >= 64) {
+    set_error("gemm_rows: bad device %d", device);
+    return LUMINA_E_ARG;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (cap[device] < elems) {
+    if (buf[device]) {
+      cudaDeviceSynchronize();  // queued work may still read the smaller buffer
+      cudaFree(buf[device]);
+      buf[device] = nullptr;
+      cap[device] = 0;
+    }
+    const size_t want = std::max(elems, (size_t)1 << 20);
+    if (cudaMalloc(&buf[device], want * 2) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("gemm_rows: cudaMalloc of %zu bytes failed", want * 2);
+      return LUMINA_E_OOM;
+    }
+    cap[device] = want;
+  }
+  *out = buf[device];
+  return LUMINA_OK;
+}
+
+}  // namespace
+
+size_t gemm_tc05_x16_elems(int rows, int cols) { return (size_t)rows * (size_t)((cols + 63) / 64 * 64); }
+
+int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
+                     __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
+                     cudaStream_t s) {
+  if (!w->mma || w->bits != 4 || (w->group % 64) || M < 1) return LUMINA_E_UNSUPPORTED;
+  const int gp = w->group / 64;
+  if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;
+  if (epi != G5_STORE && epi != G5_RESID && epi != G5_SWIGLU) return LUMINA_E_UNSUPPORTED;
+  if (epi == G5_SWIGLU && (w->rows & 1)) {
+    set_error("gemm_tc05: SwiGLU needs an even row count");
+    return LUMINA_E_ARG;
+  }
+  auto encode = tensor_map_encoder();
+  if (!encode) {
+    set_error("gemm_tc05: cuTensorMapEncodeTiled unavailable");
+    return LUMINA_E_CUDA;
+  }
+  int* fault = fault_flag_ptr();
+  if (!fault) {
+    set_error("gemm_tc05: fault flag unavailable");
+    return LUMINA_E_CUDA;
+  }
+  const int P = w->n_chunks / 2, Kpad = P * 64;
+  // 1) activations -> fp16 rows (RMSNorm fused)
+  {
+    const cudaError_t e = norm_w ? launch_pdl(act_f16_kernel<true>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
+                                              norm_w, eps, x16)
+                                 : launch_pdl(act_f16_kernel<false>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
+                                              norm_w, eps, x16);
+    if (e != cudaSuccess) {
+      set_error("act_f16 launch: %s", cudaGetErrorString(e));
+      return LUMINA_E_CUDA;
+    }
+  }
+  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  // 2) the fp16 rows as a 2-D tensor (K innermost), 64 x BN boxes, 128-byte swizzle
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)Kpad, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)Kpad * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)G5_BK, (cuuint32_t)bn};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) {
+    set_error("gemm_tc05: tensor map encode failed (%d)", (int)cr);
+    return LUMINA_E_CUDA;
+  }
+  G5Args a{};
+  a.codes = w->codes;
+  a.scales = w->scales;
+  a.rows = w->rows;
+  a.P = P;
+  a.ng = w->n_groups;
+  a.gsh = gp == 1 ? 0 : gp == 2 ? 1 : 2;
+  a.T16 = w->rows_pad / 16;
+  a.M = M;
+  a.y = y;
+  a.ldy = ldy;
+  a.resid = resid;
+  a.ldr = ldr;
+  a.epi = epi;
+  a.qk_rows = qk_rows;
+  a.hd = hd > 0 ? hd : 1;
+  a.fault = fault;
+  a.spin = wait_spin_limit();
+  return w->fp16_scales ? g5_bn<__half>(map, a, bn, s) : g5_bn<float>(map, a, bn, s);
+}
+
+}  // namespace lumina
+
+extern "C" int lumina_gemm_rows(const lumina_weight* w, const float* x_dev, int rows, int ldx, float* y_dev, int ldy,
+                                void* stream) {
+  using namespace lumina;
+  LUMINA_CHECK_ARG(w && x_dev && y_dev, "gemm_rows: null pointer");
+  LUMINA_CHECK_ARG(rows >= 1, "gemm_rows: %d rows", rows);
+  LUMINA_CHECK_ARG(ldx >= w->cols && ldy >= w->rows, "gemm_rows: ldx %d / ldy %d smaller than (%d, %d)", ldx, ldy,
+                   w->cols, w->rows);
+  if (!w->mma || w->bits != 4) {
+    set_error("gemm_rows: built for int4 weights in the tensor-core fragment layout");
+    return LUMINA_E_UNSUPPORTED;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != w->device) cudaSetDevice(w->device);
+  __half* x16 = nullptr;
+  int rc = x16_scratch(w->device, gemm_tc05_x16_elems(rows, w->cols), &x16);
+  if (!rc)
+    rc = gemm_tc05_launch(w, x_dev, ldx, rows, nullptr, 0.f, x16, y_dev, ldy, G5_STORE, nullptr, 0, 0, 0,
+                          (cudaStream_t)stream);
+  if (prev >= 0 && prev != w->device) cudaSetDevice(prev);
+  return rc;
+}

@@ -59,6 +59,7 @@ struct lumina_model {
   float *x = nullptr, *qkv_buf = nullptr, *q_buf = nullptr, *attn = nullptr, *ffn_buf = nullptr;
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
+  __half* x16 = nullptr;  // fp16 activation rows of the tcgen05 projections
   int max_splits = 32, split_rows = 64;
   ActQ aq{};
   void* kv_tmp = nullptr;
@@ -347,11 +348,29 @@ int peer_exchange(lumina_model* m, int slot, int mode, size_t n, float* out) {
 
 // y = W x (+ epilogue): the fused decode GEMV for 1, 2 or 4 rows, else (or
 // when the shape does not fit it) act_quant + the global-activation GEMV.
+// rows from which a projection runs as a tcgen05 GEMM instead of the
+// batched tensor-pipe GEMV
+constexpr int TC05_MIN_ROWS = 8;
+
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
              int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const L2Prefetch* pf = nullptr) {
   if (w->mma) {
     if (n <= 4) {
       const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    }
+    if (n >= TC05_MIN_ROWS && m->x16) {
+      // several rows (prefill, tree verification): tcgen05 GEMM; the fused
+      // q/k/v rows go to qkv_buf in their original order for the RoPE + KV
+      // append kernel
+      const bool qkv = epi == EPI_ROPE_KV;
+      const int g5 = epi == EPI_RESID ? G5_RESID : epi == EPI_SWIGLU ? G5_SWIGLU : G5_STORE;
+      const int width = rk ? (rk->nh + 2 * rk->nkv) * rk->hd : 0;
+      int rc = gemm_tc05_launch(w, x, ldx, n, norm, m->c.eps, m->x16, qkv ? m->qkv_buf : y, qkv ? width : ldy, g5,
+                                resid, ldr, qkv ? (rk->nh + rk->nkv) * rk->hd : 0, rk ? rk->hd : 0, m->stream);
+      if (rc == LUMINA_OK && qkv)
+        rc = launch_rope_append(rk->kv_fp16, m->qkv_buf, rk->nh, rk->nkv, rk->hd, rk->cos_t, rk->sin_t, rk->row_pos,
+                                m->P_dev, rk->block_table, rk->bs, rk->kcache, rk->vcache, rk->q_out, n, m->stream);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     const int rc = gemv_mma_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk);
@@ -1004,6 +1023,7 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->part_ml, (size_t)m->max_splits * m->split_rows * m->nh * 2 * 4));
   const int kmax = std::max(std::max(m->d, qw), m->ffn);
   const int nblk_pad = ((kmax + 31) / 32 + 4) / 4 * 4;  // whole chunks for every kind
+  if (R >= TC05_MIN_ROWS) TRY(dalloc(m, (void**)&m->x16, gemm_tc05_x16_elems(R, kmax) * 2));
   void* aqb = nullptr;
   TRY(dalloc(m, &aqb, actq_scratch_bytes(R, nblk_pad)));
   actq_carve(aqb, R, nblk_pad, &m->aq);

@@ -155,9 +155,10 @@ static void linspace_levels(int bits, double* out) {
 
 __constant__ double c_levels[4][16];
 
-// The device fault word: bit 0 = a bounded wait in gemv_fused_kernel gave
-// up, bit 1 = one in gemv_tc_kernel. Kernels only ever OR bits in; the host
-// reads and clears it (lumina_fault_status, and every synchronous entry).
+// The device fault word: a bounded wait gave up in gemv_fused_kernel (bit
+// 0), gemv_tc_kernel (bit 1), the tensor-parallel peer exchange (bit 2) or
+// gemm_tc05_kernel (bit 3). Kernels only ever OR bits in; the host reads and
+// clears it (lumina_fault_status, and every synchronous entry).
 __device__ int g_fault_flag;
 
 int* fault_flag_ptr() {
@@ -201,8 +202,9 @@ int clear_fault_async(cudaStream_t s) {
 }
 
 int fault_error(const char* what, int word) {
-  set_error("%s: a device wait timed out (fault word %#x: %s%s)", what, word,
-            (word & 1) ? "gemv_fused_kernel " : "", (word & 2) ? "gemv_tc_kernel" : "");
+  set_error("%s: a device wait timed out (fault word %#x:%s%s%s%s)", what, word,
+            (word & 1) ? " gemv_fused_kernel" : "", (word & 2) ? " gemv_tc_kernel" : "",
+            (word & 4) ? " peer exchange" : "", (word & 8) ? " gemm_tc05_kernel" : "");
   return LUMINA_E_CUDA;
 }
 

@@ -176,6 +176,19 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
                    const L2Prefetch* pf = nullptr);
 
+// Multi-row int4 projection on tcgen05 (gemm_tc05.cu): x (M rows, stride
+// ldx, fp32) -> fp16 rows in x16 (gemm_tc05_x16_elems(M, cols) halves;
+// RMSNorm fused when norm_w is given) -> y (M rows, stride ldy). Epilogues:
+// G5_STORE (rows < qk_rows of a fused q/k/v weight are stored at their
+// un-permuted index, head size hd), G5_RESID (y = resid + W x), G5_SWIGLU
+// (interleaved gate/up rows -> silu(gate) * up at row / 2).
+// LUMINA_E_UNSUPPORTED when the weight is not int4 in the fragment layout.
+enum { G5_STORE = 0, G5_RESID = 1, G5_SWIGLU = 2 };
+size_t gemm_tc05_x16_elems(int rows, int cols);
+int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
+                     __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
+                     cudaStream_t s);
+
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);
 // Bytes of, and carving of, one activation scratch region at `base`.

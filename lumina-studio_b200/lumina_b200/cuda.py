@@ -77,6 +77,7 @@ SIGNATURES = {
     "lumina_gemv": [_VP, _VP, _I, _I, _VP, _I, _VP],
     "lumina_gemv_host": [_VP, _FP, _I, _FP],
     "lumina_gemv_noalloc": [_VP, _VP, _I, _I, _VP, _I, _VP],
+    "lumina_gemm_rows": [_VP, _VP, _I, _I, _VP, _I, _VP],
     "lumina_gemv_int8": [_I8P, _FP, _I8P, _FP, _FP, _I, _I],
     "lumina_gemv_q4_0": [_I8P, _FP, _U8P, _FP, _FP, _I, _I],
     "lumina_gemv_fp16": [_VP, _VP, _FP, _I, _I],
@@ -268,6 +269,11 @@ class Weight:
 
     def gemv(self, x_dev: int, batch: int, ldx: int, y_dev: int, ldy: int, stream: int = 0):
         check(bound_lib().lumina_gemv(self.handle, x_dev, int(batch), int(ldx), y_dev, int(ldy), stream))
+
+    def gemm_rows(self, x_dev: int, rows: int, ldx: int, y_dev: int, ldy: int, stream: int = 0):
+        """y = x W^T for many rows (prefill / verification) on tcgen05; int4
+        weights in the tensor-core fragment layout."""
+        check(bound_lib().lumina_gemm_rows(self.handle, x_dev, int(rows), int(ldx), y_dev, int(ldy), stream))
 
     def gemv_noalloc(self, x_dev: int, batch: int, ldx: int, y_dev: int, ldy: int, stream: int = 0):
         """``gemv`` without any device allocation: the activation scratch is

@@ -123,3 +123,34 @@ def test_async_gemv_leaves_fault_word(zero_wait, kind):
     assert cuda.fault_status(0) == 0
     assert rel_l2(yd.cpu().numpy(), x @ Wd.T) < REL_L2
     assert rel_l2(w.gemv_host(x), x @ Wd.T) < REL_L2
+
+
+def test_gemm_rows_timeout(zero_wait, monkeypatch):
+    """The tcgen05 multi-row projection: with waits that give up, bit 3 of
+    the fault word is set and nothing hangs (the kernel still lets its TMA
+    loads and MMAs land and frees its tensor memory); with the default limit
+    the next call gives the reference math."""
+    import torch
+    from lumina_b200.cuda import Weight
+    cuda = zero_wait
+    monkeypatch.setenv("LUMINA_INT4_LAYOUT", "mma")
+    rows, cols, group, M = 512, 1024, 64, 40
+    rng = np.random.default_rng(6)
+    codes = rng.integers(0, 16, (rows, cols)).astype(np.uint8)
+    scales = (rng.random((rows, cols // group)) * 0.05 + 0.01).astype(np.float16).astype(np.float32)
+    w = Weight.upload("int4", group, "nibble", lf.pack_codes_nibble(codes), scales, rows, cols)
+    try:
+        x = rng.standard_normal((M, cols)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+        w.gemm_rows(xd.data_ptr(), M, cols, yd.data_ptr(), rows)
+        torch.cuda.synchronize()
+        assert cuda.fault_status(0) & 8
+        cuda.debug_wait_limit(-1)
+        w.gemm_rows(xd.data_ptr(), M, cols, yd.data_ptr(), rows)
+        torch.cuda.synchronize()
+        assert cuda.fault_status(0) == 0
+        W16 = lf.dequant("int4", codes, scales, group).astype(np.float16).astype(np.float32)
+        assert rel_l2(yd.cpu().numpy(), x @ W16.T) < REL_L2
+    finally:
+        w.free()
