@@ -5,7 +5,7 @@ fp16 activation rows by TMA, fp32 accumulation in tensor memory.
 Two bars: against the reference's math (fp32 x @ fp16-rounded dequantized
 W, chat.py:140 + 239-243) within 2e-3 relative L2, and against the same
 contraction with x rounded to fp16 (the kernel's own input rounding) within
-1e-5 -- a wrong swizzle, descriptor or tile placement shows up as an O(1)
+5e-5 (fp32 accumulation over up to 11008 terms) -- a wrong swizzle, descriptor or tile placement shows up as an O(1)
 error there, not a rounding-sized one."""
 import numpy as np
 import pytest
@@ -15,7 +15,7 @@ from oracle import lumina_format as lf
 pytestmark = pytest.mark.gpu
 
 REL_L2 = 2e-3
-EXACT = 1e-5
+EXACT = 5e-5
 
 
 def rel_l2(a, b):
