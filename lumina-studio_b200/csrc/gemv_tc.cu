@@ -100,9 +100,12 @@ __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, flo
 // Epilogue of one finished 16-row tile for batch row t (lane t of each row
 // group g): v0 = row g, v1 = row g + 8, already / 15. Paired epilogues (rows
 // 2i, 2i+1) take the odd row from the neighbouring row group's lane.
+// ep_s: the operands staged in shared memory by the prologue -- residual
+// rows [res0, res0 + MT*16) of each batch row (EPI_RESID), or the RoPE
+// cos / sin rows of each batch row's position (EPI_ROPE_KV).
 template <int NB, int EPI>
 __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0, float v1, int lane,
-                                            const int* kv_blk, const int* kv_off, const int* kv_pos) {
+                                            const int* kv_blk, const int* kv_off, const float* ep_s, int res0) {
   const int g = lane >> 2, t = lane & 3;
   const bool live = t < NB && t < a.nb;
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
@@ -112,7 +115,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0,
       const int row = row0 + g + 8 * h;
       if (row < a.rows) {
         float v = h ? v1 : v0;
-        if constexpr (EPI == EPI_RESID) v = a.resid[(size_t)t * a.ldr + row] + v;
+        if constexpr (EPI == EPI_RESID) v = ep_s[t * (a.MT * 16) + (row - res0)] + v;
         a.y[(size_t)t * a.ldy + row] = v;
       }
     }
@@ -139,8 +142,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0,
           const bool isq = row < qrows;
           const int rr = isq ? row : row - qrows;
           const int hh = rr / k.hd, p = (rr % k.hd) >> 1;
-          const int pos = kv_pos[t];
-          const float c = k.cos_t[(size_t)pos * half + p], s = k.sin_t[(size_t)pos * half + p];
+          const float c = ep_s[t * half + p], s = ep_s[(NB + t) * half + p];
           // rotate-half RoPE, fp32 products rounded separately (chat.py:99-100)
           const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
           const float o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
@@ -201,10 +203,11 @@ gemv_tc_kernel(TcArgs a) {
   int2* fq = reinterpret_cast<int2*>(xb + (size_t)P * NC * 4);
   int* cnt_s = reinterpret_cast<int*>(fq + (size_t)P * NB);
   float* part_s = reinterpret_cast<float*>(cnt_s + a.MT);
+  float* ep_s = part_s + TW * 2 * 16 * NB;  // staged epilogue operands (see tc_epilogue)
   uint8_t* ring = smem + a.x_bytes + (size_t)warp * TS * a.stage_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.x_bytes + (size_t)TW * TS * a.stage_bytes) + warp * TS;
   __shared__ float red[NB * TW];
-  __shared__ int ep_blk[NB], ep_off[NB], ep_pos[NB];
+  __shared__ int ep_blk[NB], ep_off[NB];
 
   // lane 0: unit j of this warp's run into stage j % TS (two bulk copies
   // completing on the stage's mbarrier); units are issued in order, so the
@@ -245,20 +248,41 @@ gemv_tc_kernel(TcArgs a) {
   // norm weights never depend on the previous kernel either
   float wpre[TQ_CH][8];
   if constexpr (NORM) tq_preload<NB>(wpre, a.norm_w, a.cols, P);
-  pdl_launch_dependents();
-  pdl_wait();
-
-  // 2) activation rows -> B fragments in shared memory
-  for (int i = threadIdx.x; i < a.MT; i += blockDim.x) cnt_s[i] = 0;
   if constexpr (EPI == EPI_ROPE_KV) {
+    // the KV slot and the rotation of each batch row: positions, KV length
+    // and block table are set before the step (host copy or the previous
+    // step's commit kernel), not by the kernels this one waits for
+    const int half = a.rk.hd / 2;
     if (threadIdx.x < NB && threadIdx.x < a.nb) {
       const int tt = *a.rk.t_prev + a.rk.row_base + threadIdx.x;
       ep_blk[threadIdx.x] = a.rk.block_table[tt / a.rk.bs];
       ep_off[threadIdx.x] = tt % a.rk.bs;
-      ep_pos[threadIdx.x] = a.rk.row_pos[threadIdx.x];
+    }
+    for (int i = threadIdx.x; i < a.nb * half; i += blockDim.x) {
+      const int t = i / half, p = i - t * half;
+      const size_t o = (size_t)a.rk.row_pos[t] * half + p;
+      ep_s[i] = a.rk.cos_t[o];
+      ep_s[NB * half + i] = a.rk.sin_t[o];
     }
   }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // 2) activation rows -> B fragments in shared memory; the residual rows
+  //    of this CTA's tiles stream into shared memory meanwhile (cp.async)
+  for (int i = threadIdx.x; i < a.MT; i += blockDim.x) cnt_s[i] = 0;
+  if constexpr (EPI == EPI_RESID) {
+    const int r0 = ctile0 * 16, nr = min(ctile1 * 16, a.rows) - r0;
+    for (int i = threadIdx.x; i < a.nb * nr; i += blockDim.x) {
+      const int t = i / nr, r = i - t * nr;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ep_s + t * (a.MT * 16) + r)),
+                   "l"(a.resid + (size_t)t * a.ldr + r0 + r)
+                   : "memory");
+    }
+    cp_async_commit();
+  }
   tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red);
+  if constexpr (EPI == EPI_RESID) cp_async_wait<0>();
   __syncthreads();
 
   // 3) this warp's units
@@ -352,7 +376,7 @@ gemv_tc_kernel(TcArgs a) {
         }
       }
     }
-    if (have) tc_epilogue<NB, EPI>(a, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_pos);
+    if (have) tc_epilogue<NB, EPI>(a, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_s, ctile0 * 16);
     acc0 = acc1 = 0.f;
     ++tile;
   }
@@ -463,7 +487,8 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   for (int ks : {8, 6, 4}) {
     if (ks % gp) continue;
     a.UT = (a.P + ks - 1) / ks;
-    a.x_bytes = (a.P * 2 * NB * 64 + a.P * NB * 8 + a.MT * 4 + TW * 2 * 16 * NB * 4 + 127) / 128 * 128;
+    const int ep_floats = epi == EPI_RESID ? a.MT * 16 * NB : epi == EPI_ROPE_KV && rk ? 2 * NB * (rk->hd / 2) : 0;
+    a.x_bytes = (a.P * 2 * NB * 64 + a.P * NB * 8 + a.MT * 4 + TW * 2 * 16 * NB * 4 + ep_floats * 4 + 127) / 128 * 128;
     const int groups = std::max(1, ks >> a.gsh);
     a.stage_bytes = (ks * 512 + groups * 16 * es + 127) / 128 * 128;
     const size_t smem = (size_t)a.x_bytes + (size_t)TW * TS * a.stage_bytes + TW * TS * 8;

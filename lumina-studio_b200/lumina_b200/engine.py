@@ -234,8 +234,13 @@ class CudaChatModel:
             recs = {n: f.record(n) for n in f.names()}
             if moe_map is None:
                 moe_map = moe_map_from_header(f.header)
+            shard = f.header.get("tp_shard")
+            if shard is not None and (int(shard["rank"]), int(shard["size"])) != (tp_rank, tp_size):
+                raise LuminaError(1, "%s holds the shard of rank %s of %s, not %d of %d"
+                                  % (path, shard["rank"], shard["size"], tp_rank, tp_size))
             return cls._from_records(recs, cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16,
-                                     max_seq, max_rows, block_size, tp_rank, tp_size, moe_map=moe_map)
+                                     max_seq, max_rows, block_size, tp_rank, tp_size, moe_map=moe_map,
+                                     presharded=shard is not None)
 
     @classmethod
     def from_payloads(cls, payloads: dict, cfg: dict, tok=None, group_size: int = 64, **kw):
@@ -262,7 +267,9 @@ class CudaChatModel:
 
     @classmethod
     def _from_records(cls, recs, cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16, max_seq,
-                      max_rows, block_size, tp_rank, tp_size, moe_map=None):
+                      max_rows, block_size, tp_rank, tp_size, moe_map=None, presharded=False):
+        """``presharded``: the records already are this rank's shard (a file
+        written by shards.write_tp_shards), so they are not sliced again."""
         from . import sharding
         emb = recs["model.embed_tokens.weight"]
         if emb.kind != "raw":
@@ -274,7 +281,7 @@ class CudaChatModel:
         ffn = (recs[f"model.layers.{dense[0]}.mlp.gate_proj.weight"].shape[0] if dense
                else max(m["ie"] for m in moe.values()))
         head = recs.get("lm_head.weight")
-        vocab = (head or emb).shape[0]
+        vocab = (head or emb).shape[0] * (tp_size if presharded and head is not None else 1)
         obj = cls._shell(cfg, tok, n_heads, n_kv, eps, theta, device, kv_fp16, max_seq, max_rows,
                          block_size, tp_rank, tp_size, d_model, ffn, vocab)
         obj.moe = moe
@@ -283,7 +290,8 @@ class CudaChatModel:
             if head is not None:
                 if head.kind != "raw":
                     raise LuminaError(3, "quantized lm_head is not on this path")
-                obj._set_tensor("lm_head.weight", sharding.vocab_shard(head.data, tp_rank, tp_size))
+                obj._set_tensor("lm_head.weight", head.data if presharded
+                                else sharding.vocab_shard(head.data, tp_rank, tp_size))
             for l in range(nl):
                 p = f"model.layers.{l}."
                 for nm in ("input_layernorm.weight", "post_attention_layernorm.weight"):
@@ -308,7 +316,8 @@ class CudaChatModel:
                     rec = recs[p + nm]
                     if rec.kind == "raw":
                         raise LuminaError(3, f"{p + nm} is stored raw; only packed projections are built")
-                    rec = sharding.shard_record(rec, nm, tp_rank, tp_size, obj.hd)
+                    if not presharded:
+                        rec = sharding.shard_record(rec, nm, tp_rank, tp_size, obj.hd)
                     obj._set_weight(p + nm, upload_record(rec, device))
             obj._finalize(emb.data)
         except Exception:

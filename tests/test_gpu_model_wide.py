@@ -34,13 +34,21 @@ class StubTok:
 
 
 @pytest.fixture(scope="module")
-def wide(wide_payloads):
+def wide(wide_payloads, tmp_path_factory):
+    """The model through the file path a user takes: the records written as
+    a .lumina file (the oracle writer, byte-identical to the reference's),
+    memory-mapped and uploaded packed by CudaChatModel.from_lumina."""
+    import time
     import torch
     assert torch.cuda.is_available()
+    from oracle.lumina_format import write_lumina
     from lumina_b200.engine import CudaChatModel
-    m = CudaChatModel.from_payloads(wide_payloads, synthetic.hf_cfg(CFG), StubTok(), group_size=64,
-                                    n_heads=32, n_kv=32, theta=CFG["rope_theta"], kv_fp16=True,
-                                    max_seq=4160, max_rows=128, block_size=16)
+    path = str(tmp_path_factory.mktemp("wide") / "wide.lumina")
+    write_lumina(path, wide_payloads, name="llama7b_2l", rung="int4", group_size=64)
+    t0 = time.perf_counter()
+    m = CudaChatModel.from_lumina(path, synthetic.hf_cfg(CFG), StubTok(), theta=CFG["rope_theta"],
+                                  kv_fp16=True, max_seq=4160, max_rows=128, block_size=16)
+    print("from_lumina of a 7B-width 2-layer file: %.2f s" % (time.perf_counter() - t0))
     yield m
     m.close()
 

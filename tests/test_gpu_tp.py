@@ -76,3 +76,18 @@ def test_tp2_matches_reference_and_tp1(tiny_file, tmp_path):
     for k in range(2):
         assert rel_l2(res[k]["kv0_k"], k1[:, k * half:(k + 1) * half]) < 1e-5
         assert rel_l2(res[k]["kv0_v"], v1[:, k * half:(k + 1) * half]) < 1e-5
+    # the same two ranks loading per-rank shard files (shards.write_tp_shards)
+    # compute the same bits
+    from lumina_b200.shards import write_tp_shards
+    sd = str(tmp_path / "shards")
+    write_tp_shards(tiny_file, 2, synthetic.TINY["hidden_size"] // synthetic.TINY["num_attention_heads"], sd)
+    out2 = str(tmp_path / "tp_sh")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", f"--master-port={port + 1}",
+                        os.path.join(REPO, "tests", "tp_worker.py"), tiny_file, golden, out2, sd],
+                       env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    for k in range(2):
+        a, b = np.load(f"{out}.rank{k}.npz"), np.load(f"{out2}.rank{k}.npz")
+        for key in a.files:
+            assert np.array_equal(a[key], b[key]), (k, key)

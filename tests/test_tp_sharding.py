@@ -106,3 +106,31 @@ def test_ffn_bounds_cover_group_aligned(ffn, group, tp):
     sizes = [e - s for s, e in b]
     # one whole group apart at most (plus the short last group)
     assert max(sizes) - min(sizes) <= group + (-ffn % group)
+
+
+def test_shard_files_hold_each_ranks_slice(tiny_file, tmp_path):
+    """write_tp_shards: every rank's file holds exactly shard_record's slice
+    of each projection (codes as stored, scales), the vocab slice of the
+    head, the replicated raw tensors, and the tp_shard marker the loader
+    checks."""
+    from lumina_b200 import sharding
+    from lumina_b200.loader import LuminaFile
+    from lumina_b200.shards import _SHARDED, _layer_part, write_tp_shards
+    for tp in (2, 4):
+        paths = write_tp_shards(tiny_file, tp, 64, str(tmp_path / f"tp{tp}"))
+        assert len(paths) == tp
+        with LuminaFile(tiny_file) as full:
+            for r, p in enumerate(paths):
+                with LuminaFile(p) as f:
+                    assert f.header["tp_shard"] == {"rank": r, "size": tp}
+                    assert sorted(f.names()) == sorted(full.names())
+                    for n in full.names():
+                        a, b = full.record(n), f.record(n)
+                        if a.kind == "raw":
+                            want = sharding.vocab_shard(a.data, r, tp) if n == "lm_head.weight" else a.data
+                            assert b.kind == "raw" and np.array_equal(b.data, want), n
+                            continue
+                        part = _layer_part(n)
+                        w = sharding.shard_record(a, part, r, tp, 64) if part in _SHARDED else a
+                        assert (b.kind, b.shape, b.group, b.pack) == (w.kind, w.shape, w.group, w.pack), n
+                        assert np.array_equal(b.codes, w.codes) and np.array_equal(b.scales, w.scales), n

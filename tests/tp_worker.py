@@ -20,7 +20,9 @@ class StubTok:
         return " ".join(map(str, ids))
 
 
-def main(path, golden, out):
+def main(path, golden, out, shard_dir=None):
+    """With ``shard_dir`` every rank loads its own shard file written there by
+    shards.write_tp_shards (instead of slicing the full file at load)."""
     from datetime import timedelta
     import torch
     import torch.distributed as dist
@@ -31,6 +33,9 @@ def main(path, golden, out):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=torch.device(f"cuda:{local}"))
     g = np.load(golden)
+    if shard_dir:
+        base = os.path.splitext(os.path.basename(path))[0]
+        path = os.path.join(shard_dir, f"{base}.tp{world}.rank{rank}.lumina")
     m = CudaChatModel.from_lumina(path, synthetic.hf_cfg(synthetic.TINY), StubTok(),
                                   theta=synthetic.TINY["rope_theta"], max_seq=512, max_rows=128, device=local,
                                   tp_rank=rank, tp_size=world)
@@ -52,4 +57,4 @@ def main(path, golden, out):
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:4])
+    main(*sys.argv[1:5])
