@@ -62,9 +62,16 @@ def test_forward_reports_timeout_then_recovers(tiny, golden, zero_wait):
     g = golden("tiny_decode.npz")
     prompt = [int(t) for t in g["prompt"]]
     tiny.kv_truncate(0)
+    # the prefill (tcgen05 projections) with waits that give up, then with
+    # the default limit
+    with pytest.raises(LuminaError, match="gemm_tc05_kernel"):
+        tiny.forward(prompt[:-1], 0)
+    zero_wait.debug_wait_limit(-1)
+    tiny.kv_truncate(0)
     tiny.forward(prompt[:-1], 0)
     # one row: the tensor-pipe decode GEMV (gemv_tc_kernel) with waits that give up
-    with pytest.raises(LuminaError, match="timed out"):
+    zero_wait.debug_wait_limit(0)
+    with pytest.raises(LuminaError, match="gemv_tc_kernel"):
         tiny.forward(prompt[-1:], len(prompt) - 1)
     zero_wait.debug_wait_limit(-1)
     assert zero_wait.fault_status(0) == 0  # the failing call cleared the word
