@@ -114,34 +114,47 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 // ---- dequantization of one K step ------------------------------------------
 // Thread (warp T, lane L = 4g + t) owns the 16-byte fragment word of 16-row
-// tile T at this K step: rows 16T + g (low nibbles) and 16T + g + 8 (high
+// tile T at each K step: rows 16T + g (low nibbles) and 16T + g + 8 (high
 // nibbles), columns 32(j >> 1) + 16(j & 1) + 4t + q of byte q of word j.
+// The word and the two rows' group scales are loaded G5_PD steps before they
+// are dequantized (a register queue), so no step waits on its own load.
 // Each run of four columns becomes one 8-byte store of four fp16 values at
 // the 128-byte-swizzled position: row r at r * 128, 16-byte chunk
 // (col / 8) XOR (r mod 8).
+constexpr int G5_PD = 4;  // K steps between a code load and its use
+
+struct G5Frag {
+  uint4 q;
+  float s0, s1;
+};
+
 template <typename ST>
-__device__ __forceinline__ void g5_dequant(const G5Args& a, uint8_t* As, int n0, int kb, int tid) {
-  const int T = tid >> 5, L = tid & 31, g = L >> 2, t = L & 3;
+__device__ __forceinline__ G5Frag g5_load(const G5Args& a, int n0, int kb, int tid) {
+  const int T = tid >> 5, L = tid & 31, g = L >> 2;
   const int gt = (n0 >> 4) + T;
-  const int r0 = 16 * T + g, r1 = r0 + 8;
-  uint4 q = make_uint4(0u, 0u, 0u, 0u);
-  float s0 = 0.f, s1 = 0.f;
-  if (gt < a.T16) {
-    q = ldg_stream(a.codes + (((size_t)gt * a.P + kb) * 32 + L) * 16);
+  G5Frag f{make_uint4(0u, 0u, 0u, 0u), 0.f, 0.f};
+  if (gt < a.T16 && kb < a.P) {
+    f.q = ldg_stream(a.codes + (((size_t)gt * a.P + kb) * 32 + L) * 16);
     const uint8_t* sp = a.scales + (((size_t)gt * a.ng + (kb >> a.gsh)) * 8 + g) * 2 * sizeof(ST);
     if constexpr (sizeof(ST) == 2) {
       const __half2 h = *reinterpret_cast<const __half2*>(sp);
-      s0 = __low2float(h);
-      s1 = __high2float(h);
+      f.s0 = __low2float(h);
+      f.s1 = __high2float(h);
     } else {
-      const float2 f = *reinterpret_cast<const float2*>(sp);
-      s0 = f.x;
-      s1 = f.y;
+      const float2 v = *reinterpret_cast<const float2*>(sp);
+      f.s0 = v.x;
+      f.s1 = v.y;
     }
   }
+  return f;
+}
+
+__device__ __forceinline__ void g5_dequant(const G5Frag& fr, uint8_t* As, int tid) {
+  const int T = tid >> 5, L = tid & 31, g = L >> 2, t = L & 3;
+  const int r0 = 16 * T + g, r1 = r0 + 8;
   // w = s * (-1 + c * 2/15) = c * (2s/15) - s (adapters/lumina.py:135-139), in fp32, then fp16
-  const float k0 = s0 * (2.0f / 15.0f), k1 = s1 * (2.0f / 15.0f);
-  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+  const float k0 = fr.s0 * (2.0f / 15.0f), k1 = fr.s1 * (2.0f / 15.0f);
+  const uint32_t words[4] = {fr.q.x, fr.q.y, fr.q.z, fr.q.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c0 = (j >> 1) * 32 + (j & 1) * 16 + t * 4;
@@ -149,7 +162,7 @@ __device__ __forceinline__ void g5_dequant(const G5Args& a, uint8_t* As, int n0,
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t src = h ? hi : lo;
-      const float kk = h ? k1 : k0, ss = h ? s1 : s0;
+      const float kk = h ? k1 : k0, ss = h ? fr.s1 : fr.s0;
       float f[4];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
@@ -167,6 +180,26 @@ __device__ __forceinline__ void g5_dequant(const G5Args& a, uint8_t* As, int n0,
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor pipe
 }
+
+// the register queue: entry i holds step (next + i)
+template <typename ST>
+struct G5Queue {
+  G5Frag e[G5_PD];
+  int next;  // step of e[0]
+  __device__ __forceinline__ void init(const G5Args& a, int n0, int tid) {
+    next = 0;
+#pragma unroll
+    for (int i = 0; i < G5_PD; ++i) e[i] = g5_load<ST>(a, n0, i, tid);
+  }
+  // dequantize step `next` into As and load step next + G5_PD
+  __device__ __forceinline__ void pop(const G5Args& a, uint8_t* As, int n0, int tid) {
+    g5_dequant(e[0], As, tid);
+#pragma unroll
+    for (int i = 0; i + 1 < G5_PD; ++i) e[i] = e[i + 1];
+    e[G5_PD - 1] = g5_load<ST>(a, n0, next + G5_PD, tid);
+    ++next;
+  }
+};
 
 // RoPE pair permutation of the fused q/k/v weight: row 2p + e of a head is
 // the original row p + e * hd / 2
@@ -213,7 +246,9 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   }
   // weights never depend on the previous kernel: the first stages' codes go
   // to shared memory before the dependency wait
-  for (int kb = 0; kb < S - 1 && kb < KB; ++kb) g5_dequant<ST>(a, smem + kb * STAGE, n0, kb, tid);
+  G5Queue<ST> wq;
+  wq.init(a, n0, tid);
+  for (int kb = 0; kb < S - 1 && kb < KB; ++kb) wq.pop(a, smem + kb * STAGE, n0, tid);
   tc05_fence_before();
   __syncthreads();
   tc05_fence_after();
@@ -262,7 +297,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
           continue;  // the next barrier sees the abort
         }
       }
-      g5_dequant<ST>(a, smem + ns * STAGE, n0, nk, tid);
+      wq.pop(a, smem + ns * STAGE, n0, tid);  // step nk (steps are dequantized in order)
       if (tid == 0) {
         mbar_expect_tx(&full_b[ns], B_BYTES);
         tma_load_2d(smem + ns * STAGE + G5_A_BYTES, &tmx, nk * G5_BK, m0, &full_b[ns]);

@@ -352,14 +352,19 @@ int peer_exchange(lumina_model* m, int slot, int mode, size_t n, float* out) {
 // batched tensor-pipe GEMV
 constexpr int TC05_MIN_ROWS = 8;
 
+// `exact_rows`: keep several-row projections on the int16-activation path
+// (about 5e-5 relative) instead of the fp16-activation tcgen05 GEMM (about
+// 3e-4): the projections that feed a virtual-MoE router, whose top-k choice
+// flips at score gaps of 1e-4 .. 1e-3.
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
-             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const L2Prefetch* pf = nullptr) {
+             int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const L2Prefetch* pf = nullptr,
+             bool exact_rows = false) {
   if (w->mma) {
     if (n <= 4) {
       const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
-    if (n >= TC05_MIN_ROWS && m->x16) {
+    if (n >= TC05_MIN_ROWS && m->x16 && !exact_rows) {
       // several rows (prefill, tree verification): tcgen05 GEMM; the fused
       // q/k/v rows go to qkv_buf in their original order for the RoPE + KV
       // append kernel
@@ -440,7 +445,8 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     rk.kv_fp16 = m->c.kv_fp16;
     rk.q_out = m->q_buf;
     rk.row_base = 0;
-    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, &pf_kv));
+    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, &pf_kv,
+                 Ly.moe_e > 0));
   } else {
     lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
     const int off[3] = {0, qw, qw + kw};
@@ -464,7 +470,7 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, exch_slot_ptr(m, 0), d, EPI_STORE, nullptr, 0, nullptr, &pf_mlp));
     TRY(peer_exchange(m, 0, PEER_SUM, (size_t)n * d, m->x));
   } else {
-    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, &pf_mlp));
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, &pf_mlp, Ly.moe_e > 0));
   }
   // 4) rmsnorm -> virtual-MoE MLP (chat.py:284-299), residual in place
   if (Ly.moe_e) {
