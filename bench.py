@@ -605,6 +605,20 @@ def main(argv=None):
         h2d = 32 + 4 + 4          # DevParams, row position, token
         d2h = model.vocab * 4 + 4 + 8 + 4  # logits, argmax, argmax key, fault word
 
+        # decode attention alone (attnc_kernel, every layer) at the prompt's
+        # KV length and at the 4096 rows of the tree-speculation workload
+        attn = {}
+        peak_a, _ = peaks()
+        for T in (PROMPT, 4096):
+            if model.kv_length() < T:
+                extra = synthetic.prompt_ids(cfg, T, seed=1)[model.kv_length():T]
+                model.forward(extra, model.kv_length())
+            model.kv_truncate(T)
+            ms_a, by_a = model.profile_attention(4)
+            attn[f"T{T}"] = {"us_per_launch": ms_a * 1e3, "bytes_per_launch": by_a,
+                             "GB/s": by_a / (ms_a * 1e-3) / 1e9, "frac": by_a / (ms_a * 1e-3) / 1e9 / peak_a}
+        model.kv_truncate(PROMPT)
+
         # roofline of the dominant kernel (packed GEMV), replayed alone
         ms_launch, launches, alg_bytes = model.profile_gemv(4)
         per_launch = alg_bytes / launches
@@ -638,6 +652,7 @@ def main(argv=None):
                 "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "api": "CudaChatModel.decode_step + host greedy pick",
                         "same_tokens_as_chained": same},
+                "attention": attn,
                 "clocks": clk, "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
                 "token_hbm_bytes": tok_bytes, "token_hbm_frac": tok_bytes / (dev_ms / args.steps * 1e-3) / 1e9 / peak,
                 "model_build_s": build_s}

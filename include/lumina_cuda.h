@@ -281,6 +281,13 @@ int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, fl
 int lumina_profile_gemv(lumina_model* m, int iters, float* ms_per_launch, int* launches_per_token,
                         double* bytes_per_token);
 
+/* Measurement: replay the decode row's attention (attnc_kernel) of every
+ * layer at the current KV length `iters` times as one CUDA graph, timed with
+ * CUDA events on the model's stream: the mean duration of one launch (ms)
+ * and its algorithmic bytes (the K and V rows of every cached key of this
+ * shard's heads, q in, the output out). Leaves the KV rows unchanged. */
+int lumina_profile_attention(lumina_model* m, int iters, float* ms_per_launch, double* bytes_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

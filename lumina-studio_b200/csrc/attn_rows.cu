@@ -1,0 +1,305 @@
+// Attention of several query rows at once (prompt prefill, tree
+// verification): chat.py:264-281 with sq > 1 -- scores q.K^T / sqrt(hd), key
+// j visible to row r iff its position (j itself for a cached key, else the
+// position of the input row it came from) is <= row r's position, plus
+// min(0, bias[r, j]) when a bias is given (the tree ancestry mask of
+// eagle.py:259-291), softmax over the keys, times V.
+//
+// One CTA per (head, block of AR_BR = 64 query rows), four warps of 16 rows
+// each. The CTA streams the keys in tiles of AR_BC = 64 through shared
+// memory (double-buffered; fp16 cache rows by cp.async, fp32 cache rows
+// converted to fp16 on the way), so every K/V row is read once per 64 query
+// rows. Each warp computes its 16 x 64 score tile with mma.sync m16n8k16
+// (fp16 inputs, fp32 accumulation; q is rounded to fp16, the fp16 cache is
+// used as stored), masks it, keeps an online softmax per row in registers
+// (fp32, the running maximum subtracted), and multiplies the fp16
+// probabilities with the V tile on the tensor pipe (the score accumulators
+// become the A fragments directly). The output rows are divided by their
+// softmax sums at the end.
+#include "model.cuh"
+
+namespace lumina {
+
+namespace {
+
+constexpr int AR_BR = 64;   // query rows per CTA
+constexpr int AR_BC = 64;   // keys per tile
+constexpr int AR_THREADS = 128;
+
+template <int HD>
+struct ArCfg {
+  static constexpr int ROW = HD * 2 + 16;  // padded fp16 row (bytes): ldmatrix phases hit distinct banks
+  static constexpr int Q_BYTES = AR_BR * ROW;
+  static constexpr int KV_BYTES = AR_BC * ROW;
+  static constexpr int B_BYTES = AR_BR * AR_BC * 4;  // bias tile (fp32)
+  // [Q][2 x (K, V)][kpos 2 x AR_BC ints][bias 2 x tile]
+  static constexpr int SMEM_NOBIAS = Q_BYTES + 4 * KV_BYTES + 2 * AR_BC * 4;
+  static constexpr int SMEM_BIAS = SMEM_NOBIAS + 2 * B_BYTES;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(AR_THREADS)
+attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
+                 const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
+                 const int* __restrict__ row_pos, const float* __restrict__ bias, const DevParams* __restrict__ P,
+                 float* __restrict__ out, float sdiv) {
+  using C = ArCfg<HD>;
+  constexpr int NKK = HD / 16;  // k-steps of q.K^T
+  constexpr int NDT = HD / 8;   // n-tiles of P.V
+  const int h = blockIdx.x, r0 = blockIdx.y * AR_BR;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int n = P->n, T = P->t_tot, t_prev = P->t_prev, bias_ld = P->bias_ld;
+  if (r0 >= n) return;
+  const int kvh = h / (nh / nkv);
+  const size_t bstride = (size_t)nkv * bs * HD;
+
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint8_t* Qs = sm;
+  uint8_t* KVs = sm + C::Q_BYTES;  // [buf][K | V]
+  int* kpos_s = reinterpret_cast<int*>(sm + C::Q_BYTES + 4 * C::KV_BYTES);  // [buf][AR_BC]
+  float* bias_s = reinterpret_cast<float*>(kpos_s + 2 * AR_BC);             // [buf][AR_BR][AR_BC]
+
+  // tile kt of K, V (and positions, bias) into buffer kt & 1
+  const int nkt = (T + AR_BC - 1) / AR_BC;
+  auto load_tile = [&](int kt) {
+    const int b = kt & 1;
+    uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
+    uint8_t* vs = ks + C::KV_BYTES;
+    const int j0 = kt * AR_BC;
+    if constexpr (sizeof(KT) == 2) {
+      constexpr int CH = HD * 2 / 16;
+      for (int i = tid; i < AR_BC * CH; i += AR_THREADS) {
+        const int j = i / CH, ch = i - j * CH, key = j0 + j;
+        uint8_t* kd = ks + j * C::ROW + ch * 16;
+        uint8_t* vd = vs + j * C::ROW + ch * 16;
+        if (key < T) {
+          const size_t base = (size_t)block_table[key / bs] * bstride + ((size_t)kvh * bs + key % bs) * HD;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(kd)),
+                       "l"(reinterpret_cast<const uint8_t*>(kcache + base) + ch * 16) : "memory");
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(vd)),
+                       "l"(reinterpret_cast<const uint8_t*>(vcache + base) + ch * 16) : "memory");
+        } else {
+          *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    } else {
+      // fp32 cache rows: 4 values per load, rounded to fp16 into the tile
+      constexpr int CH = HD / 4;
+      for (int i = tid; i < AR_BC * CH; i += AR_THREADS) {
+        const int j = i / CH, ch = i - j * CH, key = j0 + j;
+        uint2 kh = make_uint2(0u, 0u), vh = make_uint2(0u, 0u);
+        if (key < T) {
+          const size_t base = (size_t)block_table[key / bs] * bstride + ((size_t)kvh * bs + key % bs) * HD;
+          const float4 kf = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kcache) + base + ch * 4);
+          const float4 vf = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vcache) + base + ch * 4);
+          kh = make_uint2(pack_h2(kf.x, kf.y), pack_h2(kf.z, kf.w));
+          vh = make_uint2(pack_h2(vf.x, vf.y), pack_h2(vf.z, vf.w));
+        }
+        *reinterpret_cast<uint2*>(ks + j * C::ROW + ch * 8) = kh;
+        *reinterpret_cast<uint2*>(vs + j * C::ROW + ch * 8) = vh;
+      }
+    }
+    for (int j = tid; j < AR_BC; j += AR_THREADS) {
+      const int key = j0 + j;
+      kpos_s[b * AR_BC + j] = key >= T ? 0x7fffffff : (key < t_prev ? key : row_pos[key - t_prev]);
+    }
+    if (bias) {
+      float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
+      for (int i = tid; i < AR_BR * AR_BC; i += AR_THREADS) {
+        const int rr = i / AR_BC, j = i - rr * AR_BC, row = r0 + rr, key = j0 + j;
+        bt[i] = (row < n && key < T) ? bias[(size_t)row * bias_ld + key] : 0.f;
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  load_tile(0);
+  // q rows of the block -> fp16 (rows past n are zero)
+  for (int i = tid; i < AR_BR * (HD / 4); i += AR_THREADS) {
+    const int rr = i / (HD / 4), c4 = i - rr * (HD / 4), row = r0 + rr;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < n) v = *reinterpret_cast<const float4*>(q + ((size_t)row * nh + h) * HD + c4 * 4);
+    *reinterpret_cast<uint2*>(Qs + rr * C::ROW + c4 * 8) = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+  }
+  const int ra = r0 + 16 * warp + g, rb = ra + 8;  // this lane's two rows
+  const int pa = ra < n ? row_pos[ra] : -1, pb = rb < n ? row_pos[rb] : -1;
+  __syncthreads();
+  uint32_t qa[NKK][4];
+#pragma unroll
+  for (int kk = 0; kk < NKK; ++kk)
+    ldsm_x4(qa[kk], Qs + (16 * warp + (lane & 15)) * C::ROW + (16 * kk + 8 * (lane >> 4)) * 2);
+
+  float o[NDT][4];
+#pragma unroll
+  for (int i = 0; i < NDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
+
+  for (int kt = 0; kt < nkt; ++kt) {
+    if (kt + 1 < nkt) {
+      load_tile(kt + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const int b = kt & 1;
+    const uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
+    const uint8_t* vs = ks + C::KV_BYTES;
+    const int* kp = kpos_s + b * AR_BC;
+    const float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
+    // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; nt += 2) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      s[nt + 1][0] = s[nt + 1][1] = s[nt + 1][2] = s[nt + 1][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < NKK; ++kk) {
+        // matrices: keys 8nt.. x dims lo / hi, keys 8(nt+1).. x dims lo / hi
+        uint32_t kb[4];
+        const int key = 8 * nt + (lane & 7) + 8 * (lane >> 4);
+        ldsm_x4(kb, ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
+        mma_f16(s[nt], qa[kk], kb[0], kb[1]);
+        mma_f16(s[nt + 1], qa[kk], kb[2], kb[3]);
+      }
+    }
+    // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
+    float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = 8 * nt + 2 * t + (e & 1);
+        const bool rowb = e >= 2;
+        const int rp = rowb ? pb : pa;
+        float v = -INFINITY;
+        if (rp >= 0 && kp[j] <= rp) {
+          v = __fdiv_rn(s[nt][e], sdiv);
+          if (bias) v += fminf(0.f, bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j]);
+        }
+        s[nt][e] = v;
+        if (rowb) mxb = fmaxf(mxb, v); else mxa = fmaxf(mxa, v);
+      }
+    }
+    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+    const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
+    const float aa = na == -INFINITY ? 1.f : expf(ma - na), ab = nb == -INFINITY ? 1.f : expf(mb - nb);
+    float sa = 0.f, sb = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool rowb = e >= 2;
+        const float m = rowb ? nb : na;
+        const float p = s[nt][e] == -INFINITY ? 0.f : expf(s[nt][e] - m);
+        s[nt][e] = p;
+        if (rowb) sb += p; else sa += p;
+      }
+    }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    la = la * aa + sa;
+    lb = lb * ab + sb;
+    ma = na;
+    mb = nb;
+#pragma unroll
+    for (int i = 0; i < NDT; ++i) {
+      o[i][0] *= aa;
+      o[i][1] *= aa;
+      o[i][2] *= ab;
+      o[i][3] *= ab;
+    }
+    // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa4[4];
+      pa4[0] = pack_h2(s[2 * kk][0], s[2 * kk][1]);
+      pa4[1] = pack_h2(s[2 * kk][2], s[2 * kk][3]);
+      pa4[2] = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa4[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < NDT; nd += 2) {
+        // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then dims 8(nd+1)..
+        uint32_t vb[4];
+        ldsm_x4_t(vb, vs + (16 * kk + (lane & 15)) * C::ROW + (8 * nd + 8 * (lane >> 4)) * 2);
+        mma_f16(o[nd], pa4, vb[0], vb[1]);
+        mma_f16(o[nd + 1], pa4, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // buffer b is free for tile kt + 2
+  }
+  // out[row][h][d] = o / l: lane holds rows a (o[.][0..1]) and b (o[.][2..3]), dims 8nd + 2t, +1
+  const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+#pragma unroll
+  for (int nd = 0; nd < NDT; ++nd) {
+    const int d = 8 * nd + 2 * t;
+    if (ra < n)
+      *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(o[nd][0] * ia, o[nd][1] * ia);
+    if (rb < n)
+      *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(o[nd][2] * ib, o[nd][3] * ib);
+  }
+}
+
+template <int HD, typename KT>
+int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc, const int* bt, int bs,
+                const int* row_pos, const float* bias, const DevParams* P, float* out, int max_n, float sdiv,
+                cudaStream_t s) {
+  auto kern = attn_rows_kernel<HD, KT>;
+  const size_t smem = bias ? ArCfg<HD>::SMEM_BIAS : ArCfg<HD>::SMEM_NOBIAS;
+  const int rc = set_smem_limit((const void*)kern, smem, "attention (rows)");
+  if (rc) return rc;
+  const dim3 grid(nh, (max_n + AR_BR - 1) / AR_BR);
+  const cudaError_t e = launch_pdl(kern, grid, dim3(AR_THREADS), smem, s, q, nh, nkv, (const KT*)kc, (const KT*)vc,
+                                   bt, bs, row_pos, bias, P, out, sdiv);
+  if (e != cudaSuccess) {
+    set_error("attention (rows) launch: %s", cudaGetErrorString(e));
+    return LUMINA_E_CUDA;
+  }
+  return LUMINA_OK;
+}
+
+}  // namespace
+
+int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
+                          const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
+                          int max_n, cudaStream_t s) {
+  const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
+  if (hd == 128) return fp16 ? launch_rows<128, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s)
+                             : launch_rows<128, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s);
+  if (hd == 64) return fp16 ? launch_rows<64, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s)
+                            : launch_rows<64, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s);
+  set_error("attention: head_dim %d not built (64, 128)", hd);
+  return LUMINA_E_UNSUPPORTED;
+}
+
+}  // namespace lumina

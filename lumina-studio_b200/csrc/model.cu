@@ -58,9 +58,7 @@ struct lumina_model {
   // activations
   float *x = nullptr, *qkv_buf = nullptr, *q_buf = nullptr, *attn = nullptr, *ffn_buf = nullptr;
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
-  float *part_o = nullptr, *part_ml = nullptr;
   __half* x16 = nullptr;  // fp16 activation rows of the tcgen05 projections
-  int max_splits = 32, split_rows = 64;
   ActQ aq{};
   void* kv_tmp = nullptr;
   float* bias_dev = nullptr;
@@ -72,7 +70,6 @@ struct lumina_model {
   unsigned long long* amax_key_dev = nullptr;   // fused head argmax (value, index) key
   unsigned long long* amax_key_host = nullptr;  // pinned
   int* fault_host = nullptr;                     // pinned copy of the device fault word
-  int* attn_counters = nullptr;
   float* logits_host = nullptr;  // pinned
   cudaStream_t stream = nullptr;
   cudaGraphExec_t step_graph = nullptr;
@@ -298,11 +295,6 @@ void release_blocks(lumina_model* m, int len) {
   }
 }
 
-int n_splits_for(int n, int t_tot, int max_splits, int split_rows) {
-  if (n > split_rows) return 1;
-  int s = (t_tot + 63) / 64;
-  return std::max(1, std::min(s, max_splits));
-}
 
 size_t kv_es(const lumina_model* m) { return m->c.kv_fp16 ? 2 : 4; }
 
@@ -456,14 +448,12 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
                            m->bt_dev, m->c.block_size, layer_k(m, l), layer_v(m, l), m->q_buf, n, s));
   }
   // 2) attention (chat.py:264-281)
-  const int splits = n > m->split_rows ? 1 : m->max_splits;
   if (n == 1 && !bias) {
     TRY(launch_attention_cluster(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
                                  m->c.block_size, m->P_dev, m->attn, s, &pf_o));
   } else {
-    TRY(launch_attention(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
-                         m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, m->part_o, m->part_ml,
-                         m->attn_counters, n, splits, s));
+    TRY(launch_attention_rows(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
+                              m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, n, s));
   }
   // 3) o_proj + residual (chat.py:282-283)
   if (tp) {
@@ -522,7 +512,7 @@ int upload_params(lumina_model* m, int n, int t_prev, const int* positions, cons
   P.n = n;
   P.t_prev = t_prev;
   P.t_tot = t_prev + n;
-  P.n_splits = n_splits_for(n, t_prev + n, m->max_splits, m->split_rows);
+  P.n_splits = 1;
   P.bias_ld = bias_ld;
   for (int i = 0; i < n; ++i) m->rowpos_host[i] = positions[i];
   if (tokens)
@@ -683,7 +673,7 @@ int capture_step(lumina_model* m) {
 // End of a chained greedy step: the argmax becomes the next step's token
 // and every per-step value advances by one row.
 __global__ void greedy_commit_kernel(const unsigned long long* key, const int* argmax, int* tokens, DevParams* P,
-                                     int* rowpos, int* out, int* count, int max_splits) {
+                                     int* rowpos, int* out, int* count) {
   pdl_launch_dependents();
   pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -694,8 +684,6 @@ __global__ void greedy_commit_kernel(const unsigned long long* key, const int* a
   P->t_prev += 1;
   P->t_tot += 1;
   rowpos[0] += 1;
-  const int s = (P->t_tot + 63) / 64;  // n_splits_for(1, t_tot)
-  P->n_splits = s < 1 ? 1 : (s > max_splits ? max_splits : s);
 }
 
 int capture_chain(lumina_model* m) {
@@ -715,8 +703,7 @@ int capture_chain(lumina_model* m) {
     if (!fused_argmax && (rc = launch_argmax(m->logits, V, m->argmax_dev, s))) break;
     const cudaError_t e =
         launch_pdl(greedy_commit_kernel, dim3(1), dim3(32), 0, s, (const unsigned long long*)(fused_argmax ? m->amax_key_dev : nullptr),
-                   (const int*)m->argmax_dev, m->tokens_dev, m->P_dev, m->rowpos_dev, m->chain_tokens, m->chain_count,
-                   m->max_splits);
+                   (const int*)m->argmax_dev, m->tokens_dev, m->P_dev, m->rowpos_dev, m->chain_tokens, m->chain_count);
     if (e != cudaSuccess) {
       set_error("capture: commit launch: %s", cudaGetErrorString(e));
       rc = LUMINA_E_CUDA;
@@ -1024,9 +1011,6 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->u_buf, (size_t)R * m->ffn * 4));
   TRY(dalloc(m, (void**)&m->part, (size_t)std::max(R * m->d, m->head_rows) * 4));
   TRY(dalloc(m, (void**)&m->logits, (size_t)R * V * 4));
-  m->split_rows = std::min(64, R);
-  TRY(dalloc(m, (void**)&m->part_o, (size_t)m->max_splits * m->split_rows * qw * 4));
-  TRY(dalloc(m, (void**)&m->part_ml, (size_t)m->max_splits * m->split_rows * m->nh * 2 * 4));
   const int kmax = std::max(std::max(m->d, qw), m->ffn);
   const int nblk_pad = ((kmax + 31) / 32 + 4) / 4 * 4;  // whole chunks for every kind
   if (R >= TC05_MIN_ROWS) TRY(dalloc(m, (void**)&m->x16, gemm_tc05_x16_elems(R, kmax) * 2));
@@ -1043,7 +1027,6 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->amax_key_dev, 8));
   TRY(dalloc(m, (void**)&m->chain_tokens, (size_t)(c.max_seq + 1) * 4));
   TRY(dalloc(m, (void**)&m->chain_count, 4));
-  TRY(dalloc(m, (void**)&m->attn_counters, (size_t)m->split_rows * m->nh * 4));
   if (c.tp_size > 1) {
     // the exchange region other ranks map (peer.cu): flags, then three slots
     // (o_proj sums, down_proj sums, a logits shard) of this rank's contribution
@@ -1064,7 +1047,6 @@ int lumina_model_finalize(lumina_model* m) {
     TRY(dalloc(m, (void**)&m->moe.counters, (size_t)(m->d / 64) * 4));
     LUMINA_CUDA_TRY(cudaMemset(m->moe.counters, 0, (size_t)(m->d / 64) * 4));
   }
-  LUMINA_CUDA_TRY(cudaMemset(m->attn_counters, 0, (size_t)m->split_rows * m->nh * 4));
   if (!fault_flag_ptr()) {
     set_error("model_finalize: fault flag unavailable");
     return LUMINA_E_CUDA;
@@ -1316,7 +1298,7 @@ int lumina_decode_step(lumina_model* m, int token, float* logits_host, int* argm
   P.n = 1;
   P.t_prev = len;
   P.t_tot = len + 1;
-  P.n_splits = n_splits_for(1, len + 1, m->max_splits, m->split_rows);
+  P.n_splits = 1;
   P.bias_ld = 0;
   m->rowpos_host[0] = len;
   m->tokens_host[0] = token;
@@ -1368,6 +1350,71 @@ int lumina_decode_greedy(lumina_model* m, int token, int n, int* tokens_host, fl
     cudaMemset(fault_flag_ptr(), 0, sizeof(int));
     return fault_error("decode_greedy", word);
   }
+  return LUMINA_OK;
+}
+
+int lumina_profile_attention(lumina_model* m, int iters, float* ms_per_launch, double* bytes_per_launch) {
+  TRY(check_ready(m));
+  LUMINA_CHECK_ARG(iters >= 1 && ms_per_launch, "profile_attention: bad arguments");
+  int len = 0;
+  TRY(uniform_len(m, &len));
+  LUMINA_CHECK_ARG(len >= 1, "profile_attention: the KV cache is empty");
+  Guard g(m->device);
+  // the decode row's attention at the current length: every key visible, the
+  // last cached row standing in for the step's new row
+  DevParams& P = *m->P_host;
+  P.n = 1;
+  P.t_prev = len - 1;
+  P.t_tot = len;
+  P.n_splits = 1;
+  P.bias_ld = 0;
+  LUMINA_CUDA_TRY(cudaMemcpyAsync(m->P_dev, m->P_host, sizeof(DevParams), cudaMemcpyHostToDevice, m->stream));
+  auto all_layers = [&]() -> int {
+    for (int l = 0; l < m->c.n_layer; ++l)
+      TRY(launch_attention_cluster(m->c.kv_fp16, m->hd, m->q_buf, m->nh, m->nkv, layer_k(m, l), layer_v(m, l),
+                                   m->bt_dev, m->c.block_size, m->P_dev, m->attn, m->stream));
+    return LUMINA_OK;
+  };
+  TRY(all_layers());  // warm outside the capture
+  LUMINA_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  cudaGraph_t gr = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  LUMINA_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = LUMINA_OK;
+  for (int i = 0; i < iters && !rc; ++i) rc = all_layers();
+  const cudaError_t ec = cudaStreamEndCapture(m->stream, &gr);
+  if (rc || ec != cudaSuccess) {
+    if (gr) cudaGraphDestroy(gr);
+    if (!rc) set_error("profile_attention capture: %s", cudaGetErrorString(ec));
+    return rc ? rc : LUMINA_E_CUDA;
+  }
+  if (cudaGraphInstantiate(&ge, gr, 0) != cudaSuccess) {
+    cudaGraphDestroy(gr);
+    set_error("profile_attention: instantiate failed");
+    return LUMINA_E_CUDA;
+  }
+  cudaGraphDestroy(gr);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaGraphLaunch(ge, m->stream);
+  cudaEventRecord(e0, m->stream);
+  cudaGraphLaunch(ge, m->stream);
+  cudaEventRecord(e1, m->stream);
+  const cudaError_t es = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaGraphExecDestroy(ge);
+  if (es != cudaSuccess) {
+    set_error("profile_attention: %s", cudaGetErrorString(es));
+    return LUMINA_E_CUDA;
+  }
+  *ms_per_launch = ms / (float)(iters * m->c.n_layer);
+  // K and V rows read (this shard's heads), q read, output written
+  if (bytes_per_launch)
+    *bytes_per_launch = (double)len * 2.0 * m->nkv * m->hd * kv_es(m) + 2.0 * m->nh * m->hd * 4;
   return LUMINA_OK;
 }
 

@@ -13,7 +13,7 @@ struct DevParams {
   int n;         // rows in this forward
   int t_prev;    // KV length before the append
   int t_tot;     // t_prev + n
-  int n_splits;  // active attention splits
+  int n_splits;  // unused (1)
   int bias_ld;   // columns of the bias matrix (= t_tot)
   int pad[3];
 };
@@ -62,9 +62,11 @@ int launch_embed(const __half* emb, int d, int vocab, const int* tokens, const D
 int launch_rope_append(bool fp16, const float* qkv, int nh, int nkv, int hd, const float* cos_t, const float* sin_t,
                        const int* row_pos, const DevParams* P, const int* bt, int bs, void* kc, void* vc,
                        float* q_out, int max_n, cudaStream_t s);
-int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                     const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
-                     float* part_o, float* part_ml, int* counters, int max_n, int max_splits, cudaStream_t s);
+// attention of several query rows (prefill, tree verification) on the tensor
+// pipe: one CTA per (head, 64 rows), K/V tiles of 64 keys (attn_rows.cu)
+int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
+                          const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
+                          int max_n, cudaStream_t s);
 // single-query decode attention (one new row, no bias): one cluster of
 // ATTNC_CLUSTER CTAs per head, keys streamed in chunks of ATTNC_CHUNK
 constexpr int ATTNC_CLUSTER = 8;

@@ -86,152 +86,6 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, int nh, int nk
 }
 
 // ---------------------------------------------------------------------------
-// Attention over the paged cache (chat.py:264-281): one CTA per (head, row,
-// split). 16 groups of 8 lanes each run an online softmax over a strided
-// subset of the split's keys (a key row is read by its 8 lanes with 16-byte
-// loads), then the 16 partial states are merged in shared memory.
-// Masking: key j has position j while it is a prefix key, else the position
-// of its input row; allowed iff key_pos <= row_pos; an optional additive
-// bias b enters as min(0, b) (chat.py:266-274).
-// ---------------------------------------------------------------------------
-template <int HD, typename KT>
-__global__ void __launch_bounds__(128)
-attn_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
-            const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
-            const int* __restrict__ row_pos, const float* __restrict__ bias, const DevParams* __restrict__ P,
-            float* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml, float sdiv,
-            int* __restrict__ counters) {
-  constexpr int DL = HD / 8;  // dims per lane
-  const int h = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int n = P->n, T = P->t_tot, t_prev = P->t_prev, ns = P->n_splits;
-  if (r >= n || sp >= ns) return;
-  const int per = (T + ns - 1) / ns;
-  const int k0 = sp * per, k1 = min(T, k0 + per);
-  const int kvh = h / (nh / nkv);
-  const int g = threadIdx.x >> 3, gl = threadIdx.x & 7;
-  const unsigned gmask = 0xFFu << (8 * ((threadIdx.x & 31) >> 3));
-  const int rp = row_pos[r];
-  const size_t bstride = (size_t)nkv * bs * HD;
-
-  float qv[DL];
-  const float* qr = q + ((size_t)r * nh + h) * HD + gl * DL;
-#pragma unroll
-  for (int e = 0; e < DL; ++e) qv[e] = qr[e];
-
-  float m = -INFINITY, l = 0.f, o[DL];
-#pragma unroll
-  for (int e = 0; e < DL; ++e) o[e] = 0.f;
-
-  // keys of this group: j = k0 + g + 16 * i; two are fetched per burst so
-  // their K and V rows are in flight together
-  constexpr int KB = 2;
-  for (int j0 = k0 + g; j0 < k1; j0 += 16 * KB) {
-    float kf[KB][DL], vf[KB][DL], bj[KB];
-    bool use[KB];
-#pragma unroll
-    for (int i = 0; i < KB; ++i) {
-      const int j = j0 + 16 * i;
-      use[i] = j < k1;
-      bj[i] = 0.f;
-      if (use[i]) {
-        const int kp = j < t_prev ? j : row_pos[j - t_prev];
-        use[i] = kp <= rp;
-        if (use[i] && bias) {
-          bj[i] = fminf(0.f, bias[(size_t)r * P->bias_ld + j]);
-          use[i] = bj[i] != -INFINITY;
-        }
-      }
-      if (use[i]) {
-        const int blk = block_table[j / bs], off = j % bs;
-        const size_t base = (size_t)blk * bstride + ((size_t)kvh * bs + off) * HD + gl * DL;
-        load_kv<KT, DL>(kcache + base, kf[i]);
-        load_kv<KT, DL>(vcache + base, vf[i]);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < KB; ++i) {
-      if (!use[i]) continue;  // uniform within the 8-lane group
-      float d = 0.f;
-#pragma unroll
-      for (int e = 0; e < DL; ++e) d = fmaf(qv[e], kf[i][e], d);
-      d += __shfl_xor_sync(gmask, d, 4);
-      d += __shfl_xor_sync(gmask, d, 2);
-      d += __shfl_xor_sync(gmask, d, 1);
-      const float sc = __fdiv_rn(d, sdiv) + bj[i];
-      const float mn = fmaxf(m, sc);
-      const float alpha = expf(m - mn);
-      const float p = expf(sc - mn);
-      l = l * alpha + p;
-#pragma unroll
-      for (int e = 0; e < DL; ++e) o[e] = fmaf(o[e], alpha, p * vf[i][e]);
-      m = mn;
-    }
-  }
-
-  __shared__ float sm_m[16], sm_l[16];
-  __shared__ float sm_o[16][HD];
-  if (gl == 0) {
-    sm_m[g] = m;
-    sm_l[g] = l;
-  }
-#pragma unroll
-  for (int e = 0; e < DL; ++e) sm_o[g][gl * DL + e] = o[e];
-  __syncthreads();
-  float M = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) M = fmaxf(M, sm_m[i]);
-  float L = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) L += (sm_m[i] == -INFINITY) ? 0.f : expf(sm_m[i] - M) * sm_l[i];
-  for (int dd = threadIdx.x; dd < HD; dd += blockDim.x) {
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (sm_m[i] != -INFINITY) acc = fmaf(expf(sm_m[i] - M), sm_o[i][dd], acc);
-    if (ns == 1) {
-      out[((size_t)r * nh + h) * HD + dd] = acc / L;
-    } else {
-      part_o[(((size_t)sp * n + r) * nh + h) * HD + dd] = acc;
-    }
-  }
-  if (ns == 1) return;
-  if (threadIdx.x == 0) {
-    part_ml[(((size_t)sp * n + r) * nh + h) * 2 + 0] = M;
-    part_ml[(((size_t)sp * n + r) * nh + h) * 2 + 1] = L;
-  }
-  // the last split CTA of this (row, head) merges every split in split order
-  // (deterministic), then re-arms the counter for the next forward
-  __shared__ int is_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&counters[r * nh + h], 1);
-    is_last = prev == ns - 1;
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  float Mx = -INFINITY;
-  for (int s2 = 0; s2 < ns; ++s2) Mx = fmaxf(Mx, __ldcg(&part_ml[(((size_t)s2 * n + r) * nh + h) * 2]));
-  float Lx = 0.f;
-  for (int s2 = 0; s2 < ns; ++s2) {
-    const float ms = __ldcg(&part_ml[(((size_t)s2 * n + r) * nh + h) * 2]);
-    if (ms != -INFINITY) Lx += expf(ms - Mx) * __ldcg(&part_ml[(((size_t)s2 * n + r) * nh + h) * 2 + 1]);
-  }
-  for (int dd = threadIdx.x; dd < HD; dd += blockDim.x) {
-    float acc = 0.f;
-    for (int s2 = 0; s2 < ns; ++s2) {
-      const float ms = __ldcg(&part_ml[(((size_t)s2 * n + r) * nh + h) * 2]);
-      if (ms != -INFINITY) acc = fmaf(expf(ms - Mx), __ldcg(&part_o[(((size_t)s2 * n + r) * nh + h) * HD + dd]), acc);
-    }
-    out[((size_t)r * nh + h) * HD + dd] = acc / Lx;
-  }
-  if (threadIdx.x == 0) counters[r * nh + h] = 0;
-}
-
-// ---------------------------------------------------------------------------
 // fp16-weight GEMV, fp32 x / accumulate: the LM head (chat.py:388, fp16 head
 // from chat.py:140) and projections a file keeps raw. Warp per 2 rows, lanes
 // along K with 16-byte loads.
@@ -516,26 +370,6 @@ int launch_rope_append(bool fp16, const float* qkv, int nh, int nkv, int hd, con
   else
     RET_LAUNCH(launch_pdl(rope_append_kernel<float>, dim3(max_n), dim3(256), 0, s, qkv, nh, nkv, hd, cos_t, sin_t,
                           half, row_pos, P, bt, bs, (float*)kc, (float*)vc, q_out));
-  return LUMINA_OK;
-}
-
-int launch_attention(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
-                     const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
-                     float* part_o, float* part_ml, int* counters, int max_n, int max_splits, cudaStream_t s) {
-  const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
-  dim3 grid(nh, max_n, max_splits);
-#define ATT(HD_, KT_)                                                                                        \
-  RET_LAUNCH(launch_pdl(attn_kernel<HD_, KT_>, grid, dim3(128), 0, s, q, nh, nkv, (const KT_*)kc, (const KT_*)vc, \
-                        bt, bs, row_pos, bias, P, out, part_o, part_ml, sdiv, counters))
-  if (hd == 128) {
-    if (fp16) ATT(128, __half); else ATT(128, float);
-  } else if (hd == 64) {
-    if (fp16) ATT(64, __half); else ATT(64, float);
-  } else {
-    set_error("attention: head_dim %d not built (64, 128)", hd);
-    return LUMINA_E_UNSUPPORTED;
-  }
-#undef ATT
   return LUMINA_OK;
 }
 

@@ -100,6 +100,7 @@ SIGNATURES = {
     "lumina_decode_greedy": [_VP, _I, _I, _IP, _FP, _IP],
     "lumina_profile_gemv": [_VP, _I, _FP, _IP, ctypes.POINTER(ctypes.c_double)],
     "lumina_kv_attend": [_VP, _I, _FP, _FP],
+    "lumina_profile_attention": [_VP, _I, _FP, ctypes.POINTER(ctypes.c_double)],
     "lumina_fault_status": [_I, _IP, _I],
     "lumina_debug_wait_limit": [ctypes.c_longlong],
 }

@@ -444,6 +444,15 @@ class CudaChatModel:
         toks = list(out)[:int(n)]
         return (toks, ms.value, nk.value) if timed else toks
 
+    def profile_attention(self, iters: int = 4):
+        """Device time of the decode row's attention of every layer at the
+        current KV length, replayed alone in a CUDA graph: (ms per launch,
+        algorithmic bytes per launch)."""
+        ms = ctypes.c_float()
+        by = ctypes.c_double()
+        check(self.lib.lumina_profile_attention(self.h, int(iters), ctypes.byref(ms), ctypes.byref(by)), self.lib)
+        return ms.value, by.value
+
     def profile_gemv(self, iters: int = 4):
         """Device time of the decode token's packed GEMVs, replayed alone in a
         CUDA graph: (ms per launch, launches per token, algorithmic bytes per
