@@ -10,11 +10,14 @@
 // memory (double-buffered; fp16 cache rows by cp.async, fp32 cache rows
 // converted to fp16 on the way), so every K/V row is read once per 64 query
 // rows. Each warp computes its 16 x 64 score tile with mma.sync m16n8k16
-// (fp16 inputs, fp32 accumulation; q is rounded to fp16, the fp16 cache is
-// used as stored), masks it, keeps an online softmax per row in registers
-// (fp32, the running maximum subtracted), and multiplies the fp16
+// (fp16 inputs, fp32 accumulation), masks it, keeps an online softmax per
+// row in registers (fp32, the running maximum subtracted), and multiplies the
 // probabilities with the V tile on the tensor pipe (the score accumulators
-// become the A fragments directly). The output rows are divided by their
+// become the A fragments directly). The fp32 operands q and p enter the
+// tensor pipe as two fp16 parts, v = hi + lo with hi = fp16(v) and
+// lo = fp16(v - hi), each multiplied with the same K or V fragment, so they
+// keep about 22 bits; the fp16 cache is used as stored (an fp32 cache is
+// rounded to fp16 in the tile). The output rows are divided by their
 // softmax sums at the end.
 #include "model.cuh"
 
@@ -32,8 +35,8 @@ struct ArCfg {
   static constexpr int Q_BYTES = AR_BR * ROW;
   static constexpr int KV_BYTES = AR_BC * ROW;
   static constexpr int B_BYTES = AR_BR * AR_BC * 4;  // bias tile (fp32)
-  // [Q][2 x (K, V)][kpos 2 x AR_BC ints][bias 2 x tile]
-  static constexpr int SMEM_NOBIAS = Q_BYTES + 4 * KV_BYTES + 2 * AR_BC * 4;
+  // [Q hi][Q lo][2 x (K, V)][kpos 2 x AR_BC ints][bias 2 x tile]
+  static constexpr int SMEM_NOBIAS = 2 * Q_BYTES + 4 * KV_BYTES + 2 * AR_BC * 4;
   static constexpr int SMEM_BIAS = SMEM_NOBIAS + 2 * B_BYTES;
 };
 
@@ -57,6 +60,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+// (a, b) -> fp16 pair (hi) and the fp16 pair of the remainders (lo)
+__device__ __forceinline__ uint32_t pack_hl(float a, float b, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const __half2 l = __floats2half2_rn(a - __low2float(h), b - __high2float(h));
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 template <int HD, typename KT>
 __global__ void __launch_bounds__(AR_THREADS)
@@ -78,9 +88,10 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   const size_t bstride = (size_t)nkv * bs * HD;
 
   extern __shared__ __align__(16) uint8_t sm[];
-  uint8_t* Qs = sm;
-  uint8_t* KVs = sm + C::Q_BYTES;  // [buf][K | V]
-  int* kpos_s = reinterpret_cast<int*>(sm + C::Q_BYTES + 4 * C::KV_BYTES);  // [buf][AR_BC]
+  uint8_t* Qs = sm;                   // fp16(q)
+  uint8_t* Ql = sm + C::Q_BYTES;       // fp16(q - fp16(q))
+  uint8_t* KVs = sm + 2 * C::Q_BYTES;  // [buf][K | V]
+  int* kpos_s = reinterpret_cast<int*>(sm + 2 * C::Q_BYTES + 4 * C::KV_BYTES);  // [buf][AR_BC]
   float* bias_s = reinterpret_cast<float*>(kpos_s + 2 * AR_BC);             // [buf][AR_BR][AR_BC]
 
   // tile kt of K, V (and positions, bias) into buffer kt & 1
@@ -139,20 +150,26 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   };
 
   load_tile(0);
-  // q rows of the block -> fp16 (rows past n are zero)
+  // q rows of the block -> fp16 hi and lo parts (rows past n are zero)
   for (int i = tid; i < AR_BR * (HD / 4); i += AR_THREADS) {
     const int rr = i / (HD / 4), c4 = i - rr * (HD / 4), row = r0 + rr;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (row < n) v = *reinterpret_cast<const float4*>(q + ((size_t)row * nh + h) * HD + c4 * 4);
-    *reinterpret_cast<uint2*>(Qs + rr * C::ROW + c4 * 8) = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+    uint32_t l0, l1;
+    const uint32_t h0 = pack_hl(v.x, v.y, l0), h1 = pack_hl(v.z, v.w, l1);
+    *reinterpret_cast<uint2*>(Qs + rr * C::ROW + c4 * 8) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(Ql + rr * C::ROW + c4 * 8) = make_uint2(l0, l1);
   }
   const int ra = r0 + 16 * warp + g, rb = ra + 8;  // this lane's two rows
   const int pa = ra < n ? row_pos[ra] : -1, pb = rb < n ? row_pos[rb] : -1;
   __syncthreads();
-  uint32_t qa[NKK][4];
+  uint32_t qa[NKK][4], ql[NKK][4];
 #pragma unroll
-  for (int kk = 0; kk < NKK; ++kk)
-    ldsm_x4(qa[kk], Qs + (16 * warp + (lane & 15)) * C::ROW + (16 * kk + 8 * (lane >> 4)) * 2);
+  for (int kk = 0; kk < NKK; ++kk) {
+    const int off = (16 * warp + (lane & 15)) * C::ROW + (16 * kk + 8 * (lane >> 4)) * 2;
+    ldsm_x4(qa[kk], Qs + off);
+    ldsm_x4(ql[kk], Ql + off);
+  }
 
   float o[NDT][4];
 #pragma unroll
@@ -186,6 +203,8 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         ldsm_x4(kb, ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
         mma_f16(s[nt], qa[kk], kb[0], kb[1]);
         mma_f16(s[nt + 1], qa[kk], kb[2], kb[3]);
+        mma_f16(s[nt], ql[kk], kb[0], kb[1]);
+        mma_f16(s[nt + 1], ql[kk], kb[2], kb[3]);
       }
     }
     // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
@@ -242,11 +261,11 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa4[4];
-      pa4[0] = pack_h2(s[2 * kk][0], s[2 * kk][1]);
-      pa4[1] = pack_h2(s[2 * kk][2], s[2 * kk][3]);
-      pa4[2] = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa4[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      uint32_t pa4[4], pl4[4];
+      pa4[0] = pack_hl(s[2 * kk][0], s[2 * kk][1], pl4[0]);
+      pa4[1] = pack_hl(s[2 * kk][2], s[2 * kk][3], pl4[1]);
+      pa4[2] = pack_hl(s[2 * kk + 1][0], s[2 * kk + 1][1], pl4[2]);
+      pa4[3] = pack_hl(s[2 * kk + 1][2], s[2 * kk + 1][3], pl4[3]);
 #pragma unroll
       for (int nd = 0; nd < NDT; nd += 2) {
         // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then dims 8(nd+1)..
@@ -254,6 +273,8 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         ldsm_x4_t(vb, vs + (16 * kk + (lane & 15)) * C::ROW + (8 * nd + 8 * (lane >> 4)) * 2);
         mma_f16(o[nd], pa4, vb[0], vb[1]);
         mma_f16(o[nd + 1], pa4, vb[2], vb[3]);
+        mma_f16(o[nd], pl4, vb[0], vb[1]);
+        mma_f16(o[nd + 1], pl4, vb[2], vb[3]);
       }
     }
     __syncthreads();  // buffer b is free for tile kt + 2

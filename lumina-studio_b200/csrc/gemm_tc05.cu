@@ -7,11 +7,16 @@
 // int4 codes of 128 weight rows x 64 columns (the tensor-core fragment layout
 // of weights.cuh, one 16-byte load per thread) and their group scales, and
 // write fp16(s * level(c)) into shared memory in the 128-byte-swizzled
-// K-major layout that tcgen05.mma reads; the activations arrive as fp16 rows
-// (act_f16_kernel: RMSNorm fused, K padded to 64) through a TMA tensor map
-// with the same swizzle. One thread issues tcgen05.mma.kind::f16 (M = 128
-// weight rows, N = BN token rows, K = 16, four per K step) accumulating in
-// fp32 in tensor memory across the whole K; tcgen05.commit frees a stage
+// K-major layout that tcgen05.mma reads. The fp32 activations are carried as
+// two fp16 planes, x = hi + lo with hi = fp16(x) and lo = fp16(x - hi)
+// (act_f16_kernel: RMSNorm fused, K padded to 64), so the product keeps the
+// fp32 activations to about 2^-22 relative (one fp16 plane alone rounds them
+// to 2^-11, which compounds through the layers of a long prefill). Both
+// planes of BN token rows arrive by one TMA box with the same swizzle and
+// form a B operand of 2 BN rows. One thread issues tcgen05.mma.kind::f16
+// (M = 128 weight rows, N = 2 BN, K = 16, four per K step) accumulating in
+// fp32 in tensor memory across the whole K; the epilogue adds column m of
+// the hi half to column m of the lo half. tcgen05.commit frees a stage
 // when its MMAs have read it. The K loop keeps STAGES stages in flight: while
 // the tensor pipe works on step kb, the threads dequantize step kb + STAGES
 // - 1 into the stage that step kb - 1 released. After the last step the
@@ -91,11 +96,12 @@ __device__ __forceinline__ void tc05_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+// box {64 columns, BN rows, 2 planes} at (c0, c1, 0)
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
           smem_u32(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      "l"(map), "r"(c0), "r"(c1), "r"(0), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -212,10 +218,11 @@ __device__ __forceinline__ int g5_orig_row(const G5Args& a, int row) {
 template <int BN, typename ST>
 __global__ void __launch_bounds__(G5_THREADS, 1)
 gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
+  static_assert(2 * BN <= 256, "hi and lo planes form one MMA of N = 2 BN <= 256");
   constexpr int S = G5_STAGES;
-  constexpr int B_BYTES = BN * 128;
+  constexpr int B_BYTES = 2 * BN * 128;  // hi rows, then lo rows
   constexpr int STAGE = G5_A_BYTES + B_BYTES;
-  constexpr uint32_t IDESC = idesc_f16(G5_BM, BN);
+  constexpr uint32_t IDESC = idesc_f16(G5_BM, 2 * BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // activation tile landed
@@ -240,7 +247,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(BN)
+                 "r"(2 * BN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -259,7 +266,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   if (tid == 0) {
     for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
       mbar_expect_tx(&full_b[kb], B_BYTES);
-      tma_load_2d(smem + kb * STAGE + G5_A_BYTES, &tmx, kb * G5_BK, m0, &full_b[kb]);
+      tma_load_3d(smem + kb * STAGE + G5_A_BYTES, &tmx, kb * G5_BK, m0, &full_b[kb]);
       ++tma_issued;
     }
   }
@@ -300,7 +307,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
       wq.pop(a, smem + ns * STAGE, n0, tid);  // step nk (steps are dequantized in order)
       if (tid == 0) {
         mbar_expect_tx(&full_b[ns], B_BYTES);
-        tma_load_2d(smem + ns * STAGE + G5_A_BYTES, &tmx, nk * G5_BK, m0, &full_b[ns]);
+        tma_load_3d(smem + ns * STAGE + G5_A_BYTES, &tmx, nk * G5_BK, m0, &full_b[ns]);
         ++tma_issued;
       }
     }
@@ -322,14 +329,18 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   tc05_fence_after();
   if (__syncthreads_and(ok ? 1 : 0)) {
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and
-    // token columns [BN/2 (w / 4), BN/2 (w / 4 + 1))
+    // token columns [BN/2 (w / 4), BN/2 (w / 4 + 1)) of both planes
     const int quarter = warp & 3, half = warp >> 2;
     const int row = n0 + 32 * quarter + lane;
     constexpr int COLS = BN / 2;
     for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+      float v[16], lo[16];
+      const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+      tmem_ld16(ta, v);
+      tmem_ld16(ta + (uint32_t)BN, lo);
       if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += lo[j];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int m = m0 + c0 + j;
@@ -351,13 +362,15 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   }
   tc05_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
 }
 
-// fp32 rows (optionally RMS-normalized, chat.py:63-66) -> fp16 rows of Kpad
-// columns, zeros past K
+// fp32 rows (optionally RMS-normalized, chat.py:63-66) -> two planes of fp16
+// rows of Kpad columns, hi = fp16(v) at out[m], lo = fp16(v - hi) at
+// out[M + m]; zeros past K
 template <bool NORM>
-__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int ldx, int K, int Kpad,
+__global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ x, int ldx, int K, int Kpad, int M,
                                                       const float* __restrict__ nw, float eps, __half* __restrict__ out) {
   __shared__ float red[8];
   const int m = blockIdx.x, tid = threadIdx.x;
@@ -377,11 +390,14 @@ __global__ void __launch_bounds__(256) act_f16_kernel(const float* __restrict__ 
     rinv = 1.0f / sqrtf(tot / (float)K + eps);
   }
   __half* o = out + (size_t)m * Kpad;
+  __half* ol = out + (size_t)(M + m) * Kpad;
   for (int k = 2 * tid; k < Kpad; k += 512) {
     float v0 = 0.f, v1 = 0.f;
     if (k < K) v0 = NORM ? (xr[k] * rinv) * nw[k] : xr[k];
     if (k + 1 < K) v1 = NORM ? (xr[k + 1] * rinv) * nw[k + 1] : xr[k + 1];
-    *reinterpret_cast<__half2*>(o + k) = __floats2half2_rn(v0, v1);
+    const __half2 hi = __floats2half2_rn(v0, v1);
+    *reinterpret_cast<__half2*>(o + k) = hi;
+    *reinterpret_cast<__half2*>(ol + k) = __floats2half2_rn(v0 - __low2float(hi), v1 - __high2float(hi));
   }
 }
 
@@ -404,7 +420,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 template <int BN, typename ST>
 int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s) {
   auto kern = gemm_tc05_kernel<BN, ST>;
-  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + BN * 128) + (2 * G5_STAGES + 1) * 8 + 1024;
+  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + 2 * BN * 128) + (2 * G5_STAGES + 1) * 8 + 1024;
   const int rc = set_smem_limit((const void*)kern, smem, "gemm_tc05");
   if (rc) return rc;
   const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN);
@@ -421,8 +437,7 @@ int g5_bn(const CUtensorMap& map, const G5Args& a, int bn, cudaStream_t s) {
   switch (bn) {
     case 32: return g5_launch<32, ST>(map, a, s);
     case 64: return g5_launch<64, ST>(map, a, s);
-    case 128: return g5_launch<128, ST>(map, a, s);
-    default: return g5_launch<256, ST>(map, a, s);
+    default: return g5_launch<128, ST>(map, a, s);
   }
 }
 
@@ -457,7 +472,7 @@ int x16_scratch(int device, size_t elems, __half** out) {
 
 }  // namespace
 
-size_t gemm_tc05_x16_elems(int rows, int cols) { return (size_t)rows * (size_t)((cols + 63) / 64 * 64); }
+size_t gemm_tc05_x16_elems(int rows, int cols) { return 2 * (size_t)rows * (size_t)((cols + 63) / 64 * 64); }
 
 int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                      __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
@@ -484,22 +499,29 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
   // 1) activations -> fp16 rows (RMSNorm fused)
   {
     const cudaError_t e = norm_w ? launch_pdl(act_f16_kernel<true>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
-                                              norm_w, eps, x16)
+                                              M, norm_w, eps, x16)
                                  : launch_pdl(act_f16_kernel<false>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
-                                              norm_w, eps, x16);
+                                              M, norm_w, eps, x16);
     if (e != cudaSuccess) {
       set_error("act_f16 launch: %s", cudaGetErrorString(e));
       return LUMINA_E_CUDA;
     }
   }
-  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  // 2) the fp16 rows as a 2-D tensor (K innermost), 64 x BN boxes, 128-byte swizzle
+  // the token tile: the smallest that covers M (at most 128: the two planes
+  // make N = 2 BN), halved (not below 64) while the grid leaves SMs idle --
+  // weights of few 128-row tiles (o_proj, down: 32) would otherwise run on a
+  // fraction of the GPU
+  int bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const int row_tiles = (w->rows + G5_BM - 1) / G5_BM;
+  while (bn > 64 && row_tiles * ((M + bn - 1) / bn) < sm_count()) bn /= 2;
+  // 2) the fp16 planes as a 3-D tensor (K innermost, rows, plane), boxes of
+  // 64 x BN x 2, 128-byte swizzle: a stage holds BN hi rows then BN lo rows
   CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)Kpad, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)Kpad * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)G5_BK, (cuuint32_t)bn};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr,
+  const cuuint64_t dims[3] = {(cuuint64_t)Kpad, (cuuint64_t)M, 2};
+  const cuuint64_t strides[2] = {(cuuint64_t)Kpad * 2, (cuuint64_t)M * Kpad * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)G5_BK, (cuuint32_t)bn, 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x16, dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) {
