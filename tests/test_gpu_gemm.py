@@ -1,12 +1,14 @@
 """The tcgen05 multi-row projection (lumina_gemm_rows, the prefill / tree
 verification path): int4 codes turned into fp16 weights in shared memory,
-fp16 activation rows by TMA, fp32 accumulation in tensor memory.
+the fp32 activation rows as fp16 hi and lo planes by TMA, fp32 accumulation
+in tensor memory.
 
-Two bars: against the reference's math (fp32 x @ fp16-rounded dequantized
-W, chat.py:140 + 239-243) within 2e-3 relative L2, and against the same
-contraction with x rounded to fp16 (the kernel's own input rounding) within
-5e-5 (fp32 accumulation over up to 11008 terms) -- a wrong swizzle, descriptor or tile placement shows up as an O(1)
-error there, not a rounding-sized one."""
+Two bars against the reference's math (fp32 x @ fp16-rounded dequantized
+W, chat.py:140 + 239-243): the 2e-3 relative L2 of the decode path, and
+5e-5 against the float64 product (fp32 accumulation over up to 11008
+terms; a single fp16 plane of x would already miss it at about 2e-4) -- a
+wrong swizzle, descriptor, plane offset or tile placement shows up as an
+O(1) error there, not a rounding-sized one."""
 import numpy as np
 import pytest
 
@@ -54,8 +56,7 @@ def test_gemm_rows(torch_cuda, monkeypatch, group, N, K, M):
         y = yd.cpu().numpy()
         W16 = lf.dequant("int4", codes, scales, group).astype(np.float16).astype(np.float32)
         assert rel_l2(y, x @ W16.T) < REL_L2
-        x16 = x.astype(np.float16).astype(np.float64)
-        assert rel_l2(y, x16 @ W16.astype(np.float64).T) < EXACT
+        assert rel_l2(y, x.astype(np.float64) @ W16.astype(np.float64).T) < EXACT
         # a second call gives the same bits (fixed accumulation order)
         w.gemm_rows(xd.data_ptr(), M, K, yd.data_ptr(), N)
         torch.cuda.synchronize()
