@@ -19,6 +19,13 @@
 // keep about 22 bits; the fp16 cache is used as stored (an fp32 cache is
 // rounded to fp16 in the tile). The output rows are divided by their
 // softmax sums at the end.
+//
+// Few rows (tree verification: 31 rows, one row block per head) would leave
+// most SMs idle, so the key tiles also split over gridDim.z CTAs: CTA z takes
+// tiles [z nkt / ks, (z + 1) nkt / ks), writes its unnormalized output rows
+// and per-row (max, sum) to a workspace, and the CTA that draws the last
+// ticket of its (head, row block) merges the ks states in z order:
+// M = max_z m_z, out = sum_z o_z e^(m_z - M) / sum_z l_z e^(m_z - M).
 #include "model.cuh"
 
 namespace lumina {
@@ -28,6 +35,7 @@ namespace {
 constexpr int AR_BR = 64;   // query rows per CTA
 constexpr int AR_BC = 64;   // keys per tile
 constexpr int AR_THREADS = 128;
+constexpr int AR_MIN_SPLIT_TILES = 4;  // key tiles per CTA when the keys are split
 
 template <int HD>
 struct ArCfg {
@@ -73,7 +81,7 @@ __global__ void __launch_bounds__(AR_THREADS)
 attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
                  const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
                  const int* __restrict__ row_pos, const float* __restrict__ bias, const DevParams* __restrict__ P,
-                 float* __restrict__ out, float sdiv) {
+                 float* __restrict__ out, float sdiv, float* __restrict__ ws, int* __restrict__ cnt) {
   using C = ArCfg<HD>;
   constexpr int NKK = HD / 16;  // k-steps of q.K^T
   constexpr int NDT = HD / 8;   // n-tiles of P.V
@@ -94,8 +102,11 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   int* kpos_s = reinterpret_cast<int*>(sm + 2 * C::Q_BYTES + 4 * C::KV_BYTES);  // [buf][AR_BC]
   float* bias_s = reinterpret_cast<float*>(kpos_s + 2 * AR_BC);             // [buf][AR_BR][AR_BC]
 
-  // tile kt of K, V (and positions, bias) into buffer kt & 1
+  // tile kt of K, V (and positions, bias) into buffer kt & 1; this CTA's
+  // tiles are [kt0, kt1)
   const int nkt = (T + AR_BC - 1) / AR_BC;
+  const int ks = gridDim.z, z = blockIdx.z;
+  const int kt0 = (int)((long long)nkt * z / ks), kt1 = (int)((long long)nkt * (z + 1) / ks);
   auto load_tile = [&](int kt) {
     const int b = kt & 1;
     uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
@@ -149,7 +160,7 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
-  load_tile(0);
+  if (kt0 < kt1) load_tile(kt0);
   // q rows of the block -> fp16 hi and lo parts (rows past n are zero)
   for (int i = tid; i < AR_BR * (HD / 4); i += AR_THREADS) {
     const int rr = i / (HD / 4), c4 = i - rr * (HD / 4), row = r0 + rr;
@@ -176,8 +187,8 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   for (int i = 0; i < NDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
 
-  for (int kt = 0; kt < nkt; ++kt) {
-    if (kt + 1 < nkt) {
+  for (int kt = kt0; kt < kt1; ++kt) {
+    if (kt + 1 < kt1) {
       load_tile(kt + 1);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
@@ -280,28 +291,109 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     __syncthreads();  // buffer b is free for tile kt + 2
   }
   // out[row][h][d] = o / l: lane holds rows a (o[.][0..1]) and b (o[.][2..3]), dims 8nd + 2t, +1
-  const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+  if (ks == 1) {
+    const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+      const int d = 8 * nd + 2 * t;
+      if (ra < n)
+        *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(o[nd][0] * ia, o[nd][1] * ia);
+      if (rb < n)
+        *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(o[nd][2] * ib, o[nd][3] * ib);
+    }
+    return;
+  }
+  // split keys: state z of (row, head) at part_o[(z n + row) nh + h][HD] and
+  // part_ml[(z n + row) nh + h] = (m, l)
+  float* part_o = ws;
+  float2* part_ml = reinterpret_cast<float2*>(ws + (size_t)ks * n * nh * HD);
+  const size_t ia_idx = ((size_t)z * n + ra) * nh + h, ib_idx = ((size_t)z * n + rb) * nh + h;
+#pragma unroll
+  for (int nd = 0; nd < NDT; ++nd) {
+    const int d = 8 * nd + 2 * t;
+    if (ra < n) *reinterpret_cast<float2*>(part_o + ia_idx * HD + d) = make_float2(o[nd][0], o[nd][1]);
+    if (rb < n) *reinterpret_cast<float2*>(part_o + ib_idx * HD + d) = make_float2(o[nd][2], o[nd][3]);
+  }
+  if (t == 0) {
+    if (ra < n) part_ml[ia_idx] = make_float2(ma, la);
+    if (rb < n) part_ml[ib_idx] = make_float2(mb, lb);
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int last_s;
+  const int tile = blockIdx.y * nh + h;
+  if (tid == 0) last_s = atomicAdd(&cnt[tile], 1) == ks - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // merge in z order
+  float Ma = -INFINITY, Mb = -INFINITY;
+  for (int zz = 0; zz < ks; ++zz) {
+    if (ra < n) Ma = fmaxf(Ma, __ldcg(&part_ml[((size_t)zz * n + ra) * nh + h].x));
+    if (rb < n) Mb = fmaxf(Mb, __ldcg(&part_ml[((size_t)zz * n + rb) * nh + h].x));
+  }
+  float accA[NDT][2], accB[NDT][2], La = 0.f, Lb = 0.f;
+#pragma unroll
+  for (int nd = 0; nd < NDT; ++nd) accA[nd][0] = accA[nd][1] = accB[nd][0] = accB[nd][1] = 0.f;
+  for (int zz = 0; zz < ks; ++zz) {
+    const size_t ja = ((size_t)zz * n + ra) * nh + h, jb = ((size_t)zz * n + rb) * nh + h;
+    if (ra < n && Ma != -INFINITY) {
+      const float2 ml = __ldcg(&part_ml[ja]);
+      const float f = ml.x == -INFINITY ? 0.f : expf(ml.x - Ma);
+      La += ml.y * f;
+#pragma unroll
+      for (int nd = 0; nd < NDT; ++nd) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(part_o + ja * HD + 8 * nd + 2 * t));
+        accA[nd][0] += v.x * f;
+        accA[nd][1] += v.y * f;
+      }
+    }
+    if (rb < n && Mb != -INFINITY) {
+      const float2 ml = __ldcg(&part_ml[jb]);
+      const float f = ml.x == -INFINITY ? 0.f : expf(ml.x - Mb);
+      Lb += ml.y * f;
+#pragma unroll
+      for (int nd = 0; nd < NDT; ++nd) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(part_o + jb * HD + 8 * nd + 2 * t));
+        accB[nd][0] += v.x * f;
+        accB[nd][1] += v.y * f;
+      }
+    }
+  }
+  const float ia = La > 0.f ? 1.f / La : 0.f, ib = Lb > 0.f ? 1.f / Lb : 0.f;
 #pragma unroll
   for (int nd = 0; nd < NDT; ++nd) {
     const int d = 8 * nd + 2 * t;
     if (ra < n)
-      *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(o[nd][0] * ia, o[nd][1] * ia);
+      *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(accA[nd][0] * ia, accA[nd][1] * ia);
     if (rb < n)
-      *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(o[nd][2] * ib, o[nd][3] * ib);
+      *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(accB[nd][0] * ib, accB[nd][1] * ib);
   }
+  if (tid == 0) cnt[tile] = 0;
 }
 
 template <int HD, typename KT>
 int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc, const int* bt, int bs,
                 const int* row_pos, const float* bias, const DevParams* P, float* out, int max_n, float sdiv,
-                cudaStream_t s) {
+                int t_tot, const SplitWork* sw, cudaStream_t s) {
   auto kern = attn_rows_kernel<HD, KT>;
   const size_t smem = bias ? ArCfg<HD>::SMEM_BIAS : ArCfg<HD>::SMEM_NOBIAS;
   const int rc = set_smem_limit((const void*)kern, smem, "attention (rows)");
   if (rc) return rc;
-  const dim3 grid(nh, (max_n + AR_BR - 1) / AR_BR);
+  // key splits while heads x row blocks leave SMs idle: at least
+  // AR_MIN_SPLIT_TILES key tiles per CTA, the states within the workspace
+  const int rb = (max_n + AR_BR - 1) / AR_BR, tiles = nh * rb;
+  const int nkt = (t_tot + AR_BC - 1) / AR_BC;
+  int ks = 1;
+  if (sw && sw->ws && sw->cnt && tiles < sm_count() && tiles <= sw->cnt_n) {
+    ks = std::min((2 * sm_count() + tiles - 1) / tiles, nkt / AR_MIN_SPLIT_TILES);
+    while (ks > 1 && (size_t)ks * max_n * nh * (HD + 2) > sw->ws_elems) --ks;
+    ks = std::max(ks, 1);
+  }
+  const dim3 grid(nh, rb, ks);
   const cudaError_t e = launch_pdl(kern, grid, dim3(AR_THREADS), smem, s, q, nh, nkv, (const KT*)kc, (const KT*)vc,
-                                   bt, bs, row_pos, bias, P, out, sdiv);
+                                   bt, bs, row_pos, bias, P, out, sdiv, ks > 1 ? sw->ws : nullptr,
+                                   ks > 1 ? sw->cnt : nullptr);
   if (e != cudaSuccess) {
     set_error("attention (rows) launch: %s", cudaGetErrorString(e));
     return LUMINA_E_CUDA;
@@ -313,12 +405,14 @@ int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc,
 
 int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
                           const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
-                          int max_n, cudaStream_t s) {
+                          int max_n, int t_tot, const SplitWork* sw, cudaStream_t s) {
   const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
-  if (hd == 128) return fp16 ? launch_rows<128, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s)
-                             : launch_rows<128, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s);
-  if (hd == 64) return fp16 ? launch_rows<64, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s)
-                            : launch_rows<64, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, s);
+  if (hd == 128)
+    return fp16 ? launch_rows<128, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s)
+                : launch_rows<128, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+  if (hd == 64)
+    return fp16 ? launch_rows<64, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s)
+                : launch_rows<64, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
   set_error("attention: head_dim %d not built (64, 128)", hd);
   return LUMINA_E_UNSUPPORTED;
 }

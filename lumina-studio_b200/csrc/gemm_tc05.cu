@@ -25,6 +25,12 @@
 // SwiGLU over interleaved gate/up rows, or the store of q/k/v rows in their
 // original order for the RoPE + KV append kernel).
 //
+// A grid of fewer (row, token) tiles than the GPU has SMs -- few token rows
+// (tree verification) or few weight rows (o_proj, down) -- also splits K:
+// CTA z of a tile takes K steps [z P / ks, (z + 1) P / ks), writes its fp32
+// partial tile to a workspace, and the CTA that draws the tile's last ticket
+// adds the ks partials in z order and runs the epilogue.
+//
 // Waits are bounded: a wait that gives up sets bit 3 of the device fault
 // word; the CTA then stops issuing work, lets its TMA loads and MMAs in flight
 // finish (waiting with the default limit), frees its tensor memory and exits.
@@ -45,6 +51,7 @@ constexpr int G5_BK = 64;                  // K per stage: one 128-byte swizzle 
 constexpr int G5_STAGES = 4;
 constexpr int G5_THREADS = 256;            // 8 warps: all dequantize, all run the epilogue
 constexpr int G5_A_BYTES = G5_BM * G5_BK * 2;
+constexpr int G5_MIN_SPLIT_STEPS = 8;      // K steps per CTA when K is split
 
 struct G5Args {
   const uint8_t* codes;
@@ -64,6 +71,9 @@ struct G5Args {
   int hd;
   int* fault;
   long long spin;
+  int ks;       // K splits (grid z)
+  float* ws;    // ks > 1: partial tiles, [z][M][rows]
+  int* cnt;     // ks > 1: one ticket counter per (row tile, token tile)
 };
 
 // ---- tcgen05 / TMA building blocks -----------------------------------------
@@ -135,11 +145,11 @@ struct G5Frag {
 };
 
 template <typename ST>
-__device__ __forceinline__ G5Frag g5_load(const G5Args& a, int n0, int kb, int tid) {
+__device__ __forceinline__ G5Frag g5_load(const G5Args& a, int n0, int kb, int kb_end, int tid) {
   const int T = tid >> 5, L = tid & 31, g = L >> 2;
   const int gt = (n0 >> 4) + T;
   G5Frag f{make_uint4(0u, 0u, 0u, 0u), 0.f, 0.f};
-  if (gt < a.T16 && kb < a.P) {
+  if (gt < a.T16 && kb < kb_end) {
     f.q = ldg_stream(a.codes + (((size_t)gt * a.P + kb) * 32 + L) * 16);
     const uint8_t* sp = a.scales + (((size_t)gt * a.ng + (kb >> a.gsh)) * 8 + g) * 2 * sizeof(ST);
     if constexpr (sizeof(ST) == 2) {
@@ -187,22 +197,24 @@ __device__ __forceinline__ void g5_dequant(const G5Frag& fr, uint8_t* As, int ti
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor pipe
 }
 
-// the register queue: entry i holds step (next + i)
+// the register queue over K steps [begin, end): entry i holds step (next + i)
 template <typename ST>
 struct G5Queue {
   G5Frag e[G5_PD];
   int next;  // step of e[0]
-  __device__ __forceinline__ void init(const G5Args& a, int n0, int tid) {
-    next = 0;
+  int end;
+  __device__ __forceinline__ void init(const G5Args& a, int n0, int begin, int end_, int tid) {
+    next = begin;
+    end = end_;
 #pragma unroll
-    for (int i = 0; i < G5_PD; ++i) e[i] = g5_load<ST>(a, n0, i, tid);
+    for (int i = 0; i < G5_PD; ++i) e[i] = g5_load<ST>(a, n0, begin + i, end, tid);
   }
   // dequantize step `next` into As and load step next + G5_PD
   __device__ __forceinline__ void pop(const G5Args& a, uint8_t* As, int n0, int tid) {
     g5_dequant(e[0], As, tid);
 #pragma unroll
     for (int i = 0; i + 1 < G5_PD; ++i) e[i] = e[i + 1];
-    e[G5_PD - 1] = g5_load<ST>(a, n0, next + G5_PD, tid);
+    e[G5_PD - 1] = g5_load<ST>(a, n0, next + G5_PD, end, tid);
     ++next;
   }
 };
@@ -213,6 +225,28 @@ __device__ __forceinline__ int g5_orig_row(const G5Args& a, int row) {
   if (row >= a.qk_rows) return row;
   const int h = row / a.hd, rr = row - h * a.hd;
   return h * a.hd + (rr >> 1) + (rr & 1) * (a.hd >> 1);
+}
+
+// epilogue of 16 token columns mb .. mb + 15 of this thread's weight row
+// (every lane of the warp calls it: SwiGLU takes the up row from lane + 1)
+__device__ __forceinline__ void g5_emit(const G5Args& a, int row, int mb, const float (&v)[16], int lane) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = mb + j;
+    if (a.epi == G5_SWIGLU) {
+      const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
+      if (m < a.M && !(lane & 1) && row + 1 < a.rows) {
+        const float gt = v[j];
+        const float e = expf(-fminf(fmaxf(gt, -40.f), 40.f));  // chat.py:300-302
+        a.y[(size_t)m * a.ldy + (row >> 1)] = gt / (1.0f + e) * up;
+      }
+    } else if (m < a.M && row < a.rows) {
+      if (a.epi == G5_RESID)
+        a.y[(size_t)m * a.ldy + row] = a.resid[(size_t)m * a.ldr + row] + v[j];
+      else
+        a.y[(size_t)m * a.ldy + g5_orig_row(a, row)] = v[j];
+    }
+  }
 }
 
 template <int BN, typename ST>
@@ -229,11 +263,13 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   uint64_t* empty = full_b + S;                                      // stage's MMAs done
   uint64_t* accum = empty + S;                                       // every MMA done
   __shared__ uint32_t tmem_base;
-  __shared__ int abort_s;
+  __shared__ int abort_s, last_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * G5_BM, m0 = blockIdx.y * BN;
-  const int KB = a.P;
+  // this CTA's K steps: kb0 + i for i < KB
+  const int z = blockIdx.z;
+  const int kb0 = (int)((long long)a.P * z / a.ks), KB = (int)((long long)a.P * (z + 1) / a.ks) - kb0;
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
@@ -254,7 +290,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   // weights never depend on the previous kernel: the first stages' codes go
   // to shared memory before the dependency wait
   G5Queue<ST> wq;
-  wq.init(a, n0, tid);
+  wq.init(a, n0, kb0, kb0 + KB, tid);
   for (int kb = 0; kb < S - 1 && kb < KB; ++kb) wq.pop(a, smem + kb * STAGE, n0, tid);
   tc05_fence_before();
   __syncthreads();
@@ -266,7 +302,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   if (tid == 0) {
     for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
       mbar_expect_tx(&full_b[kb], B_BYTES);
-      tma_load_3d(smem + kb * STAGE + G5_A_BYTES, &tmx, kb * G5_BK, m0, &full_b[kb]);
+      tma_load_3d(smem + kb * STAGE + G5_A_BYTES, &tmx, (kb0 + kb) * G5_BK, m0, &full_b[kb]);
       ++tma_issued;
     }
   }
@@ -307,7 +343,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
       wq.pop(a, smem + ns * STAGE, n0, tid);  // step nk (steps are dequantized in order)
       if (tid == 0) {
         mbar_expect_tx(&full_b[ns], B_BYTES);
-        tma_load_3d(smem + ns * STAGE + G5_A_BYTES, &tmx, nk * G5_BK, m0, &full_b[ns]);
+        tma_load_3d(smem + ns * STAGE + G5_A_BYTES, &tmx, (kb0 + nk) * G5_BK, m0, &full_b[ns]);
         ++tma_issued;
       }
     }
@@ -327,37 +363,66 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
     ok = false;
   }
   tc05_fence_after();
-  if (__syncthreads_and(ok ? 1 : 0)) {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and
-    // token columns [BN/2 (w / 4), BN/2 (w / 4 + 1)) of both planes
-    const int quarter = warp & 3, half = warp >> 2;
-    const int row = n0 + 32 * quarter + lane;
-    constexpr int COLS = BN / 2;
-    for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
-      float v[16], lo[16];
-      const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
-      tmem_ld16(ta, v);
-      tmem_ld16(ta + (uint32_t)BN, lo);
-      if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
+  const bool all_ok = __syncthreads_and(ok ? 1 : 0);
+  // warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and token
+  // columns [BN/2 (w / 4), BN/2 (w / 4 + 1)) of both planes
+  const int quarter = warp & 3, half = warp >> 2;
+  const int row = n0 + 32 * quarter + lane;
+  constexpr int COLS = BN / 2;
+  if (a.ks == 1) {
+    if (all_ok) {
+      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+        float v[16], lo[16];
+        const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+        __syncwarp();
+        tmem_ld16(ta, v);
+        tmem_ld16(ta + (uint32_t)BN, lo);
+        if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] += lo[j];
+        for (int j = 0; j < 16; ++j) v[j] += lo[j];
+        g5_emit(a, row, m0 + c0, v, lane);
+      }
+    }
+  } else {
+    // split K: the partial tile to ws[z][m][row]; every CTA of the tile
+    // takes a ticket (an aborted CTA too, so the counter returns to zero)
+    if (all_ok) {
+      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+        float v[16], lo[16];
+        const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+        __syncwarp();
+        tmem_ld16(ta, v);
+        tmem_ld16(ta + (uint32_t)BN, lo);
+        if (row < a.rows) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + c0 + j;
-        if (a.epi == G5_SWIGLU) {
-          const float up = __shfl_down_sync(0xffffffffu, v[j], 1);
-          if (m < a.M && !(lane & 1) && row + 1 < a.rows) {
-            const float gt = v[j];
-            const float e = expf(-fminf(fmaxf(gt, -40.f), 40.f));  // chat.py:300-302
-            a.y[(size_t)m * a.ldy + (row >> 1)] = gt / (1.0f + e) * up;
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < a.M) a.ws[((size_t)z * a.M + m) * a.rows + row] = v[j] + lo[j];
           }
-        } else if (m < a.M && row < a.rows) {
-          if (a.epi == G5_RESID)
-            a.y[(size_t)m * a.ldy + row] = a.resid[(size_t)m * a.ldr + row] + v[j];
-          else
-            a.y[(size_t)m * a.ldy + g5_orig_row(a, row)] = v[j];
         }
       }
+    }
+    __threadfence();
+    __syncthreads();
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) last_s = atomicAdd(&a.cnt[tile], 1) == a.ks - 1;
+    __syncthreads();
+    if (last_s) {
+      __threadfence();
+      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+        if (m0 + c0 >= a.M) break;  // warp-uniform
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + c0 + j;
+          float acc = 0.f;
+          if (m < a.M && row < a.rows)
+            for (int zz = 0; zz < a.ks; ++zz) acc += __ldcg(a.ws + ((size_t)zz * a.M + m) * a.rows + row);
+          v[j] = acc;
+        }
+        g5_emit(a, row, m0 + c0, v, lane);
+      }
+      if (tid == 0) a.cnt[tile] = 0;
     }
   }
   tc05_fence_before();
@@ -423,7 +488,7 @@ int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s) {
   const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + 2 * BN * 128) + (2 * G5_STAGES + 1) * 8 + 1024;
   const int rc = set_smem_limit((const void*)kern, smem, "gemm_tc05");
   if (rc) return rc;
-  const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN);
+  const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN, a.ks);
   const cudaError_t e = launch_pdl(kern, grid, dim3(G5_THREADS), smem, s, map, a);
   if (e != cudaSuccess) {
     set_error("gemm_tc05 launch: %s", cudaGetErrorString(e));
@@ -472,11 +537,42 @@ int x16_scratch(int device, size_t elems, __half** out) {
 
 }  // namespace
 
+int split_scratch(int device, SplitWork* out) {
+  static std::mutex mu;
+  static SplitWork work[64];
+  if (device < 0 || device >= 64) {
+    set_error("split workspace: bad device %d", device);
+    return LUMINA_E_ARG;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  SplitWork& sw = work[device];
+  if (!sw.ws) {
+    float* ws = nullptr;
+    int* cnt = nullptr;
+    if (cudaMalloc(&ws, SPLIT_WS_ELEMS * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&cnt, SPLIT_COUNTERS * sizeof(int)) != cudaSuccess ||
+        cudaMemset(cnt, 0, SPLIT_COUNTERS * sizeof(int)) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {  // zeroed before any stream uses it
+      cudaGetLastError();
+      if (ws) cudaFree(ws);
+      if (cnt) cudaFree(cnt);
+      set_error("split workspace: cudaMalloc failed");
+      return LUMINA_E_OOM;
+    }
+    sw.ws = ws;
+    sw.ws_elems = SPLIT_WS_ELEMS;
+    sw.cnt = cnt;
+    sw.cnt_n = SPLIT_COUNTERS;
+  }
+  *out = sw;
+  return LUMINA_OK;
+}
+
 size_t gemm_tc05_x16_elems(int rows, int cols) { return 2 * (size_t)rows * (size_t)((cols + 63) / 64 * 64); }
 
 int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                      __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
-                     cudaStream_t s) {
+                     cudaStream_t s, const SplitWork* sw) {
   if (!w->mma || w->bits != 4 || (w->group % 64) || M < 1) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;
@@ -514,6 +610,17 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
   int bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
   const int row_tiles = (w->rows + G5_BM - 1) / G5_BM;
   while (bn > 64 && row_tiles * ((M + bn - 1) / bn) < sm_count()) bn /= 2;
+  // K splits while the tiles still leave SMs idle (two CTAs fit on an SM at
+  // BN = 32): at least G5_MIN_SPLIT_STEPS K steps per CTA, partials within
+  // the workspace
+  const int tiles = row_tiles * ((M + bn - 1) / bn);
+  const int target = sm_count() * (bn <= 32 ? 2 : 1);
+  int ks = 1;
+  if (sw && sw->ws && sw->cnt && tiles < target && tiles <= sw->cnt_n) {
+    ks = std::min((target + tiles - 1) / tiles, P / G5_MIN_SPLIT_STEPS);
+    while (ks > 1 && (size_t)ks * M * w->rows > sw->ws_elems) --ks;
+    ks = std::max(ks, 1);
+  }
   // 2) the fp16 planes as a 3-D tensor (K innermost, rows, plane), boxes of
   // 64 x BN x 2, 128-byte swizzle: a stage holds BN hi rows then BN lo rows
   CUtensorMap map;
@@ -546,6 +653,9 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
   a.hd = hd > 0 ? hd : 1;
   a.fault = fault;
   a.spin = wait_spin_limit();
+  a.ks = ks;
+  a.ws = ks > 1 ? sw->ws : nullptr;
+  a.cnt = ks > 1 ? sw->cnt : nullptr;
   return w->fp16_scales ? g5_bn<__half>(map, a, bn, s) : g5_bn<float>(map, a, bn, s);
 }
 
@@ -566,10 +676,12 @@ extern "C" int lumina_gemm_rows(const lumina_weight* w, const float* x_dev, int 
   cudaGetDevice(&prev);
   if (prev != w->device) cudaSetDevice(w->device);
   __half* x16 = nullptr;
+  SplitWork sw;
   int rc = x16_scratch(w->device, gemm_tc05_x16_elems(rows, w->cols), &x16);
+  if (!rc) rc = split_scratch(w->device, &sw);
   if (!rc)
     rc = gemm_tc05_launch(w, x_dev, ldx, rows, nullptr, 0.f, x16, y_dev, ldy, G5_STORE, nullptr, 0, 0, 0,
-                          (cudaStream_t)stream);
+                          (cudaStream_t)stream, &sw);
   if (prev >= 0 && prev != w->device) cudaSetDevice(prev);
   return rc;
 }

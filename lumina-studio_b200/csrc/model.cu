@@ -59,6 +59,7 @@ struct lumina_model {
   float *x = nullptr, *qkv_buf = nullptr, *q_buf = nullptr, *attn = nullptr, *ffn_buf = nullptr;
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
   __half* x16 = nullptr;  // fp16 activation rows of the tcgen05 projections
+  SplitWork split;        // partials of split-K projections and split-key attention
   ActQ aq{};
   void* kv_tmp = nullptr;
   float* bias_dev = nullptr;
@@ -364,7 +365,8 @@ int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, i
       const int g5 = epi == EPI_RESID ? G5_RESID : epi == EPI_SWIGLU ? G5_SWIGLU : G5_STORE;
       const int width = rk ? (rk->nh + 2 * rk->nkv) * rk->hd : 0;
       int rc = gemm_tc05_launch(w, x, ldx, n, norm, m->c.eps, m->x16, qkv ? m->qkv_buf : y, qkv ? width : ldy, g5,
-                                resid, ldr, qkv ? (rk->nh + rk->nkv) * rk->hd : 0, rk ? rk->hd : 0, m->stream);
+                                resid, ldr, qkv ? (rk->nh + rk->nkv) * rk->hd : 0, rk ? rk->hd : 0, m->stream,
+                                &m->split);
       if (rc == LUMINA_OK && qkv)
         rc = launch_rope_append(rk->kv_fp16, m->qkv_buf, rk->nh, rk->nkv, rk->hd, rk->cos_t, rk->sin_t, rk->row_pos,
                                 m->P_dev, rk->block_table, rk->bs, rk->kcache, rk->vcache, rk->q_out, n, m->stream);
@@ -453,7 +455,8 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
                                  m->c.block_size, m->P_dev, m->attn, s, &pf_o));
   } else {
     TRY(launch_attention_rows(m->c.kv_fp16, hd, m->q_buf, nh, nkv, layer_k(m, l), layer_v(m, l), m->bt_dev,
-                              m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, n, s));
+                              m->c.block_size, m->rowpos_dev, bias, m->P_dev, m->attn, n, m->P_host->t_tot,
+                              &m->split, s));
   }
   // 3) o_proj + residual (chat.py:282-283)
   if (tp) {
@@ -1013,7 +1016,15 @@ int lumina_model_finalize(lumina_model* m) {
   TRY(dalloc(m, (void**)&m->logits, (size_t)R * V * 4));
   const int kmax = std::max(std::max(m->d, qw), m->ffn);
   const int nblk_pad = ((kmax + 31) / 32 + 4) / 4 * 4;  // whole chunks for every kind
-  if (R >= TC05_MIN_ROWS) TRY(dalloc(m, (void**)&m->x16, gemm_tc05_x16_elems(R, kmax) * 2));
+  if (R >= TC05_MIN_ROWS) {
+    TRY(dalloc(m, (void**)&m->x16, gemm_tc05_x16_elems(R, kmax) * 2));
+    TRY(dalloc(m, (void**)&m->split.ws, SPLIT_WS_ELEMS * sizeof(float)));
+    TRY(dalloc(m, (void**)&m->split.cnt, SPLIT_COUNTERS * sizeof(int)));
+    LUMINA_CUDA_TRY(cudaMemset(m->split.cnt, 0, SPLIT_COUNTERS * sizeof(int)));
+    LUMINA_CUDA_TRY(cudaDeviceSynchronize());  // zero before the model's non-blocking stream starts
+    m->split.ws_elems = SPLIT_WS_ELEMS;
+    m->split.cnt_n = SPLIT_COUNTERS;
+  }
   void* aqb = nullptr;
   TRY(dalloc(m, &aqb, actq_scratch_bytes(R, nblk_pad)));
   actq_carve(aqb, R, nblk_pad, &m->aq);

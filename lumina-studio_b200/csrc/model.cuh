@@ -63,10 +63,12 @@ int launch_rope_append(bool fp16, const float* qkv, int nh, int nkv, int hd, con
                        const int* row_pos, const DevParams* P, const int* bt, int bs, void* kc, void* vc,
                        float* q_out, int max_n, cudaStream_t s);
 // attention of several query rows (prefill, tree verification) on the tensor
-// pipe: one CTA per (head, 64 rows), K/V tiles of 64 keys (attn_rows.cu)
+// pipe: one CTA per (head, 64 rows), K/V tiles of 64 keys (attn_rows.cu);
+// when heads x row blocks leave SMs idle, the keys (t_tot of them, the host's
+// copy of P->t_tot) split over CTAs whose partial softmax states `sw` holds
 int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
                           const int* bt, int bs, const int* row_pos, const float* bias, const DevParams* P, float* out,
-                          int max_n, cudaStream_t s);
+                          int max_n, int t_tot, const SplitWork* sw, cudaStream_t s);
 // single-query decode attention (one new row, no bias): one cluster of
 // ATTNC_CLUSTER CTAs per head, keys streamed in chunks of ATTNC_CHUNK
 constexpr int ATTNC_CLUSTER = 8;

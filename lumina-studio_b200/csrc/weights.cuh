@@ -176,18 +176,36 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
                    const L2Prefetch* pf = nullptr);
 
+// Workspace of a kernel whose grid splits its reduction (K of a projection,
+// the keys of an attention row block) over several CTAs: partial results go
+// to `ws`, and the CTA that takes the last ticket of its tile's counter
+// combines them in split order (deterministic, no CTA waits on another).
+// Counters start at zero and the combining CTA resets its own, so kernels of
+// one stream can share the workspace; kernels on different streams cannot.
+struct SplitWork {
+  float* ws = nullptr;
+  size_t ws_elems = 0;
+  int* cnt = nullptr;
+  int cnt_n = 0;
+};
+// per-device workspace for the library's own entry points (lumina_gemm_rows)
+int split_scratch(int device, SplitWork* out);
+constexpr size_t SPLIT_WS_ELEMS = (size_t)8 << 20;  // 32 MiB of fp32 partials
+constexpr int SPLIT_COUNTERS = 8192;
+
 // Multi-row int4 projection on tcgen05 (gemm_tc05.cu): x (M rows, stride
-// ldx, fp32) -> fp16 rows in x16 (gemm_tc05_x16_elems(M, cols) halves;
-// RMSNorm fused when norm_w is given) -> y (M rows, stride ldy). Epilogues:
-// G5_STORE (rows < qk_rows of a fused q/k/v weight are stored at their
-// un-permuted index, head size hd), G5_RESID (y = resid + W x), G5_SWIGLU
-// (interleaved gate/up rows -> silu(gate) * up at row / 2).
+// ldx, fp32) -> fp16 hi and lo planes in x16 (gemm_tc05_x16_elems(M, cols)
+// halves; RMSNorm fused when norm_w is given) -> y (M rows, stride ldy).
+// Epilogues: G5_STORE (rows < qk_rows of a fused q/k/v weight are stored at
+// their un-permuted index, head size hd), G5_RESID (y = resid + W x),
+// G5_SWIGLU (interleaved gate/up rows -> silu(gate) * up at row / 2). With
+// `sw`, a grid of fewer tiles than SMs splits K over CTAs.
 // LUMINA_E_UNSUPPORTED when the weight is not int4 in the fragment layout.
 enum { G5_STORE = 0, G5_RESID = 1, G5_SWIGLU = 2 };
 size_t gemm_tc05_x16_elems(int rows, int cols);
 int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                      __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
-                     cudaStream_t s);
+                     cudaStream_t s, const SplitWork* sw = nullptr);
 
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);

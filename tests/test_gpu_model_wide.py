@@ -162,6 +162,58 @@ def test_wide_decode_step_at_4096(wide, wide_oracle, long_context):
     wide.kv_truncate(T)
 
 
+def _tree_4x2():
+    """A depth-5, 32-node draft tree: the root's 4 children, 2 children
+    each, then single chains, plus 3 nodes at depth 5."""
+    parents, depths, frontier = [-1], [0], [0]
+    for b in (4, 2, 1, 1):
+        nxt = []
+        for p in frontier:
+            for _ in range(b):
+                parents.append(p)
+                depths.append(depths[p] + 1)
+                nxt.append(len(parents) - 1)
+        frontier = nxt
+    for p in frontier[:32 - len(parents)]:
+        parents.append(p)
+        depths.append(depths[p] + 1)
+    return parents, depths
+
+
+def test_wide_tree_verify_at_4096(wide, wide_oracle, long_context):
+    """The tree verification forward of the tree-speculation workload (31
+    child rows, ancestry bias, positions Lp - 1 + depth) over a 4096-token
+    context: the projections split K over CTAs (31 rows fill too few tiles)
+    and the attention splits its 65 key tiles; logits of every row and the
+    children's K/V rows against the oracle's verify_tree on the device's own
+    cached rows."""
+    from lumina_b200.engine import verify_tree
+    from oracle.decode import verify_tree as overify
+    T = _prefill(wide, long_context)
+    cache = {}
+    for lyr in range(wide.n_layer):
+        cache[lyr] = wide.kv_read(lyr, 0, T)
+    parents, depths = _tree_4x2()
+    rng = np.random.default_rng(8)
+    ids = [long_context[-1]] + [int(t) for t in rng.integers(0, CFG["vocab_size"], len(parents) - 1)]
+    try:
+        lg, order = verify_tree(wide, T, ids, parents, depths)
+        want, tc, _ = overify(wide_oracle, cache, T, ids, parents, depths)
+        assert lg.shape == want.shape == (31, CFG["vocab_size"])
+        for r in range(31):
+            assert rel_l2(lg[r], want[r]) < REL_L2, r
+        for lyr in range(wide.n_layer):
+            k, v = wide.kv_read(lyr, T, 31)
+            assert rel_l2(k, tc[lyr][0][T:].astype(np.float16)) < REL_L2, lyr
+            assert rel_l2(v, tc[lyr][1][T:].astype(np.float16)) < REL_L2, lyr
+        # a second verification gives the same bits (fixed split order)
+        wide.kv_truncate(T)
+        lg2, _ = verify_tree(wide, T, ids, parents, depths)
+        assert np.array_equal(lg2.view(np.uint32), lg.view(np.uint32))
+    finally:
+        wide.kv_truncate(T)
+
+
 @pytest.mark.parametrize("T", [4096, 4000, 512, 17, 1])
 def test_wide_attention_kernel(wide, long_context, T):
     """attnc_kernel<128, half> alone (lumina_kv_attend) against numpy
