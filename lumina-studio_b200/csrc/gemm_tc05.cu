@@ -106,6 +106,15 @@ __device__ __forceinline__ void tc05_commit(uint64_t* bar) {
                : "memory");
 }
 
+// box {64 columns, 128 rows} at (c0, c1): a dense fp16 weight tile
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // box {64 columns, BN rows, 2 planes} at (c0, c1, 0)
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
@@ -133,11 +142,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // tile T at each K step: rows 16T + g (low nibbles) and 16T + g + 8 (high
 // nibbles), columns 32(j >> 1) + 16(j & 1) + 4t + q of byte q of word j.
 // The word and the two rows' group scales are loaded G5_PD steps before they
-// are dequantized (a register queue), so no step waits on its own load.
+// are dequantized (a register queue), so no step waits on its own load. Step
+// p lives in slot p mod G5_PD for its whole time in the queue: every slot is
+// named by a constant, so no queue entry is ever moved -- moving a register
+// whose load is still in flight would wait for that load.
 // Each run of four columns becomes one 8-byte store of four fp16 values at
 // the 128-byte-swizzled position: row r at r * 128, 16-byte chunk
 // (col / 8) XOR (r mod 8).
-constexpr int G5_PD = 4;  // K steps between a code load and its use
+constexpr int G5_PD = 8;  // K steps between a code load and its use
 
 struct G5Frag {
   uint4 q;
@@ -197,25 +209,36 @@ __device__ __forceinline__ void g5_dequant(const G5Frag& fr, uint8_t* As, int ti
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor pipe
 }
 
-// the register queue over K steps [begin, end): entry i holds step (next + i)
+// the register queue over K steps [begin, end): local step p in slot p % G5_PD
 template <typename ST>
 struct G5Queue {
   G5Frag e[G5_PD];
-  int next;  // step of e[0]
-  int end;
-  __device__ __forceinline__ void init(const G5Args& a, int n0, int begin, int end_, int tid) {
-    next = begin;
+  int begin, end;
+  __device__ __forceinline__ void init(const G5Args& a, int n0, int begin_, int end_, int tid) {
+    begin = begin_;
     end = end_;
 #pragma unroll
     for (int i = 0; i < G5_PD; ++i) e[i] = g5_load<ST>(a, n0, begin + i, end, tid);
   }
-  // dequantize step `next` into As and load step next + G5_PD
-  __device__ __forceinline__ void pop(const G5Args& a, uint8_t* As, int n0, int tid) {
-    g5_dequant(e[0], As, tid);
-#pragma unroll
-    for (int i = 0; i + 1 < G5_PD; ++i) e[i] = e[i + 1];
-    e[G5_PD - 1] = g5_load<ST>(a, n0, next + G5_PD, end, tid);
-    ++next;
+  template <int SLOT>
+  __device__ __forceinline__ void pop_at(const G5Args& a, uint8_t* As, int n0, int tid, int p) {
+    g5_dequant(e[SLOT], As, tid);
+    e[SLOT] = g5_load<ST>(a, n0, begin + p + G5_PD, end, tid);
+  }
+  // dequantize local step p (steps are popped in order) into As and load
+  // step p + G5_PD into its slot
+  __device__ __forceinline__ void pop(const G5Args& a, uint8_t* As, int n0, int tid, int p) {
+    static_assert(G5_PD == 8, "one case per slot");
+    switch (p & (G5_PD - 1)) {
+      case 0: pop_at<0>(a, As, n0, tid, p); break;
+      case 1: pop_at<1>(a, As, n0, tid, p); break;
+      case 2: pop_at<2>(a, As, n0, tid, p); break;
+      case 3: pop_at<3>(a, As, n0, tid, p); break;
+      case 4: pop_at<4>(a, As, n0, tid, p); break;
+      case 5: pop_at<5>(a, As, n0, tid, p); break;
+      case 6: pop_at<6>(a, As, n0, tid, p); break;
+      default: pop_at<7>(a, As, n0, tid, p); break;
+    }
   }
 };
 
@@ -249,9 +272,12 @@ __device__ __forceinline__ void g5_emit(const G5Args& a, int row, int mb, const 
   }
 }
 
-template <int BN, typename ST>
+// DENSE: the weight is an fp16 matrix (the LM head) whose 128 x 64 tiles
+// arrive by TMA (tensor map tmw, same swizzle) instead of being rebuilt from
+// codes; ST is then unused.
+template <int BN, typename ST, bool DENSE>
 __global__ void __launch_bounds__(G5_THREADS, 1)
-gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
+gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, G5Args a) {
   static_assert(2 * BN <= 256, "hi and lo planes form one MMA of N = 2 BN <= 256");
   constexpr int S = G5_STAGES;
   constexpr int B_BYTES = 2 * BN * 128;  // hi rows, then lo rows
@@ -262,6 +288,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // activation tile landed
   uint64_t* empty = full_b + S;                                      // stage's MMAs done
   uint64_t* accum = empty + S;                                       // every MMA done
+  uint64_t* full_a = accum + 1;                                      // DENSE: weight tile landed
   __shared__ uint32_t tmem_base;
   __shared__ int abort_s, last_s;
 
@@ -275,10 +302,12 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_b[i], 1);
       mbar_init(&empty[i], 1);
+      if (DENSE) mbar_init(&full_a[i], 1);
     }
     mbar_init(accum, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+    if (DENSE) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
     abort_s = 0;
   }
   if (warp == 0) {
@@ -290,8 +319,19 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
   // weights never depend on the previous kernel: the first stages' codes go
   // to shared memory before the dependency wait
   G5Queue<ST> wq;
-  wq.init(a, n0, kb0, kb0 + KB, tid);
-  for (int kb = 0; kb < S - 1 && kb < KB; ++kb) wq.pop(a, smem + kb * STAGE, n0, tid);
+  int a_issued = 0, a_waited = 0;  // DENSE, thread 0: weight tiles requested / landed
+  if constexpr (DENSE) {
+    __syncthreads();  // barriers initialized
+    if (tid == 0)
+      for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
+        mbar_expect_tx(&full_a[kb], G5_A_BYTES);
+        tma_load_2d(smem + kb * STAGE, &tmw, (kb0 + kb) * G5_BK, n0, &full_a[kb]);
+        ++a_issued;
+      }
+  } else {
+    wq.init(a, n0, kb0, kb0 + KB, tid);
+    for (int kb = 0; kb < S - 1 && kb < KB; ++kb) wq.pop(a, smem + kb * STAGE, n0, tid, kb);
+  }
   tc05_fence_before();
   __syncthreads();
   tc05_fence_after();
@@ -312,7 +352,12 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
     __syncthreads();  // stage kb's weight tile is written (and fenced) by every thread
     if (abort_s) break;
     if (tid == 0) {
-      const bool landed = mbar_wait_bounded(&full_b[s], (uint32_t)((kb / S) & 1), a.spin);
+      bool landed = true;
+      if constexpr (DENSE) {
+        landed = mbar_wait_bounded(&full_a[s], (uint32_t)((kb / S) & 1), a.spin);
+        a_waited += landed ? 1 : 0;
+      }
+      landed = landed && mbar_wait_bounded(&full_b[s], (uint32_t)((kb / S) & 1), a.spin);
       if (!landed) {
         atomicOr(a.fault, 8);
         abort_s = 1;
@@ -340,8 +385,13 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
           continue;  // the next barrier sees the abort
         }
       }
-      wq.pop(a, smem + ns * STAGE, n0, tid);  // step nk (steps are dequantized in order)
+      if constexpr (!DENSE) wq.pop(a, smem + ns * STAGE, n0, tid, nk);  // steps are dequantized in order
       if (tid == 0) {
+        if constexpr (DENSE) {
+          mbar_expect_tx(&full_a[ns], G5_A_BYTES);
+          tma_load_2d(smem + ns * STAGE, &tmw, (kb0 + nk) * G5_BK, n0, &full_a[ns]);
+          ++a_issued;
+        }
         mbar_expect_tx(&full_b[ns], B_BYTES);
         tma_load_3d(smem + ns * STAGE + G5_A_BYTES, &tmx, (kb0 + nk) * G5_BK, m0, &full_b[ns]);
         ++tma_issued;
@@ -354,6 +404,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, G5Args a) {
     if (!ok) {
       // let every activation load in flight land before the stages go away
       for (int i = tma_waited; i < tma_issued; ++i) mbar_wait_bounded(&full_b[i % S], (uint32_t)((i / S) & 1));
+      for (int i = a_waited; i < a_issued; ++i) mbar_wait_bounded(&full_a[i % S], (uint32_t)((i / S) & 1));
     }
     tc05_commit(accum);  // completes once every MMA issued above is done
   }
@@ -482,14 +533,14 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-template <int BN, typename ST>
-int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s) {
-  auto kern = gemm_tc05_kernel<BN, ST>;
-  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + 2 * BN * 128) + (2 * G5_STAGES + 1) * 8 + 1024;
+template <int BN, typename ST, bool DENSE = false>
+int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s, const CUtensorMap* wmap = nullptr) {
+  auto kern = gemm_tc05_kernel<BN, ST, DENSE>;
+  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + 2 * BN * 128) + (3 * G5_STAGES + 1) * 8 + 1024;
   const int rc = set_smem_limit((const void*)kern, smem, "gemm_tc05");
   if (rc) return rc;
   const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN, a.ks);
-  const cudaError_t e = launch_pdl(kern, grid, dim3(G5_THREADS), smem, s, map, a);
+  const cudaError_t e = launch_pdl(kern, grid, dim3(G5_THREADS), smem, s, map, wmap ? *wmap : map, a);
   if (e != cudaSuccess) {
     set_error("gemm_tc05 launch: %s", cudaGetErrorString(e));
     return LUMINA_E_CUDA;
@@ -532,6 +583,62 @@ int x16_scratch(int device, size_t elems, __half** out) {
     cap[device] = want;
   }
   *out = buf[device];
+  return LUMINA_OK;
+}
+
+// 1) the activation rows -> fp16 hi and lo planes (RMSNorm fused when
+// norm_w is given); 2) the token tile and K splits; 3) the planes' tensor map
+int g5_prepare(const float* x, int ldx, int M, int K, int P, const float* norm_w, float eps, __half* x16, int rows,
+               const SplitWork* sw, cudaStream_t s, int* bn_out, int* ks_out, CUtensorMap* map) {
+  auto encode = tensor_map_encoder();
+  if (!encode) {
+    set_error("gemm_tc05: cuTensorMapEncodeTiled unavailable");
+    return LUMINA_E_CUDA;
+  }
+  const int Kpad = P * 64;
+  {
+    const cudaError_t e = norm_w ? launch_pdl(act_f16_kernel<true>, dim3(M), dim3(256), 0, s, x, ldx, K, Kpad, M,
+                                              norm_w, eps, x16)
+                                 : launch_pdl(act_f16_kernel<false>, dim3(M), dim3(256), 0, s, x, ldx, K, Kpad, M,
+                                              norm_w, eps, x16);
+    if (e != cudaSuccess) {
+      set_error("act_f16 launch: %s", cudaGetErrorString(e));
+      return LUMINA_E_CUDA;
+    }
+  }
+  // the token tile: the smallest that covers M (at most 128: the two planes
+  // make N = 2 BN), halved (not below 64) while the grid leaves SMs idle --
+  // weights of few 128-row tiles (o_proj, down: 32) would otherwise run on a
+  // fraction of the GPU
+  int bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const int row_tiles = (rows + G5_BM - 1) / G5_BM;
+  while (bn > 64 && row_tiles * ((M + bn - 1) / bn) < sm_count()) bn /= 2;
+  // K splits while the tiles still leave SMs idle (two CTAs fit on an SM at
+  // BN = 32): at least G5_MIN_SPLIT_STEPS K steps per CTA, partials within
+  // the workspace
+  const int tiles = row_tiles * ((M + bn - 1) / bn);
+  const int target = sm_count() * (bn <= 32 ? 2 : 1);
+  int ks = 1;
+  if (sw && sw->ws && sw->cnt && tiles < target && tiles <= sw->cnt_n) {
+    ks = std::min((target + tiles - 1) / tiles, P / G5_MIN_SPLIT_STEPS);
+    while (ks > 1 && (size_t)ks * M * rows > sw->ws_elems) --ks;
+    ks = std::max(ks, 1);
+  }
+  // the fp16 planes as a 3-D tensor (K innermost, rows, plane), boxes of
+  // 64 x BN x 2, 128-byte swizzle: a stage holds BN hi rows then BN lo rows
+  const cuuint64_t dims[3] = {(cuuint64_t)Kpad, (cuuint64_t)M, 2};
+  const cuuint64_t strides[2] = {(cuuint64_t)Kpad * 2, (cuuint64_t)M * Kpad * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)G5_BK, (cuuint32_t)bn, 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x16, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) {
+    set_error("gemm_tc05: tensor map encode failed (%d)", (int)cr);
+    return LUMINA_E_CUDA;
+  }
+  *bn_out = bn;
+  *ks_out = ks;
   return LUMINA_OK;
 }
 
@@ -581,60 +688,15 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
     set_error("gemm_tc05: SwiGLU needs an even row count");
     return LUMINA_E_ARG;
   }
-  auto encode = tensor_map_encoder();
-  if (!encode) {
-    set_error("gemm_tc05: cuTensorMapEncodeTiled unavailable");
-    return LUMINA_E_CUDA;
-  }
   int* fault = fault_flag_ptr();
   if (!fault) {
     set_error("gemm_tc05: fault flag unavailable");
     return LUMINA_E_CUDA;
   }
-  const int P = w->n_chunks / 2, Kpad = P * 64;
-  // 1) activations -> fp16 rows (RMSNorm fused)
-  {
-    const cudaError_t e = norm_w ? launch_pdl(act_f16_kernel<true>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
-                                              M, norm_w, eps, x16)
-                                 : launch_pdl(act_f16_kernel<false>, dim3(M), dim3(256), 0, s, x, ldx, w->cols, Kpad,
-                                              M, norm_w, eps, x16);
-    if (e != cudaSuccess) {
-      set_error("act_f16 launch: %s", cudaGetErrorString(e));
-      return LUMINA_E_CUDA;
-    }
-  }
-  // the token tile: the smallest that covers M (at most 128: the two planes
-  // make N = 2 BN), halved (not below 64) while the grid leaves SMs idle --
-  // weights of few 128-row tiles (o_proj, down: 32) would otherwise run on a
-  // fraction of the GPU
-  int bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
-  const int row_tiles = (w->rows + G5_BM - 1) / G5_BM;
-  while (bn > 64 && row_tiles * ((M + bn - 1) / bn) < sm_count()) bn /= 2;
-  // K splits while the tiles still leave SMs idle (two CTAs fit on an SM at
-  // BN = 32): at least G5_MIN_SPLIT_STEPS K steps per CTA, partials within
-  // the workspace
-  const int tiles = row_tiles * ((M + bn - 1) / bn);
-  const int target = sm_count() * (bn <= 32 ? 2 : 1);
-  int ks = 1;
-  if (sw && sw->ws && sw->cnt && tiles < target && tiles <= sw->cnt_n) {
-    ks = std::min((target + tiles - 1) / tiles, P / G5_MIN_SPLIT_STEPS);
-    while (ks > 1 && (size_t)ks * M * w->rows > sw->ws_elems) --ks;
-    ks = std::max(ks, 1);
-  }
-  // 2) the fp16 planes as a 3-D tensor (K innermost, rows, plane), boxes of
-  // 64 x BN x 2, 128-byte swizzle: a stage holds BN hi rows then BN lo rows
+  const int P = w->n_chunks / 2;
+  int bn = 0, ks = 1;
   CUtensorMap map;
-  const cuuint64_t dims[3] = {(cuuint64_t)Kpad, (cuuint64_t)M, 2};
-  const cuuint64_t strides[2] = {(cuuint64_t)Kpad * 2, (cuuint64_t)M * Kpad * 2};
-  const cuuint32_t box[3] = {(cuuint32_t)G5_BK, (cuuint32_t)bn, 2};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x16, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) {
-    set_error("gemm_tc05: tensor map encode failed (%d)", (int)cr);
-    return LUMINA_E_CUDA;
-  }
+  if (const int rc = g5_prepare(x, ldx, M, w->cols, P, norm_w, eps, x16, w->rows, sw, s, &bn, &ks, &map)) return rc;
   G5Args a{};
   a.codes = w->codes;
   a.scales = w->scales;
@@ -657,6 +719,52 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
   a.ws = ks > 1 ? sw->ws : nullptr;
   a.cnt = ks > 1 ? sw->cnt : nullptr;
   return w->fp16_scales ? g5_bn<__half>(map, a, bn, s) : g5_bn<float>(map, a, bn, s);
+}
+
+int dense_tc05_launch(const __half* W, int rows, int K, const float* x, int ldx, int M, __half* x16, float* y,
+                      int ldy, cudaStream_t s, const SplitWork* sw) {
+  if (M < 1 || rows < 1 || K < 1 || (K % 8)) return LUMINA_E_UNSUPPORTED;
+  auto encode = tensor_map_encoder();
+  int* fault = fault_flag_ptr();
+  if (!encode || !fault) {
+    set_error("gemm_tc05 (dense): tensor map encoder or fault flag unavailable");
+    return LUMINA_E_CUDA;
+  }
+  const int P = (K + G5_BK - 1) / G5_BK;
+  int bn = 0, ks = 1;
+  CUtensorMap map, wmap;
+  if (const int rc = g5_prepare(x, ldx, M, K, P, nullptr, 0.f, x16, rows, sw, s, &bn, &ks, &map)) return rc;
+  // the weight rows as a 2-D tensor (K innermost), 64 x 128 boxes; columns
+  // past K and rows past `rows` read as zeros
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)G5_BK, (cuuint32_t)G5_BM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(W), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) {
+    set_error("gemm_tc05 (dense): tensor map encode failed (%d)", (int)cr);
+    return LUMINA_E_CUDA;
+  }
+  G5Args a{};
+  a.rows = rows;
+  a.P = P;
+  a.M = M;
+  a.y = y;
+  a.ldy = ldy;
+  a.epi = G5_STORE;
+  a.hd = 1;
+  a.fault = fault;
+  a.spin = wait_spin_limit();
+  a.ks = ks;
+  a.ws = ks > 1 ? sw->ws : nullptr;
+  a.cnt = ks > 1 ? sw->cnt : nullptr;
+  switch (bn) {
+    case 32: return g5_launch<32, float, true>(map, a, s, &wmap);
+    case 64: return g5_launch<64, float, true>(map, a, s, &wmap);
+    default: return g5_launch<128, float, true>(map, a, s, &wmap);
+  }
 }
 
 }  // namespace lumina

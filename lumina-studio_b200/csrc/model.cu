@@ -498,6 +498,13 @@ int run_head(lumina_model* m, int first, int rows, unsigned long long* amax = nu
   // the next token's first GEMV (layer 0 q/k/v) into L2 meanwhile
   const L2Prefetch pf = prefetch_of(qkv_weight(m, 0));
   if (m->c.tp_size <= 1) {
+    if (rows >= TC05_MIN_ROWS && m->x16 && !amax) {
+      // several rows (tree verification, all-row logits): the fp16 head on
+      // the tensor pipe, read once for all rows
+      const int rc = dense_tc05_launch(m->head, V, m->d, m->x + (size_t)first * m->d, m->d, rows, m->x16, m->logits,
+                                       V, m->stream, &m->split);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    }
     return launch_dense_gemv(m->head, V, m->d, m->x + (size_t)first * m->d, m->d, rows, m->logits, V, nullptr, 0,
                              m->stream, amax, &pf);
   }

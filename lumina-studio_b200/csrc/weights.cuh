@@ -206,6 +206,10 @@ size_t gemm_tc05_x16_elems(int rows, int cols);
 int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                      __half* x16, float* y, int ldy, int epi, const float* resid, int ldr, int qk_rows, int hd,
                      cudaStream_t s, const SplitWork* sw = nullptr);
+// The same contraction with a dense fp16 weight W (rows x K, row-major, K a
+// multiple of 8; the LM head): y[m, r] = sum_k x[m, k] W[r, k], stored.
+int dense_tc05_launch(const __half* W, int rows, int K, const float* x, int ldx, int M, __half* x16, float* y,
+                      int ldy, cudaStream_t s, const SplitWork* sw = nullptr);
 
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);
