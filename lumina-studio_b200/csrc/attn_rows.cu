@@ -68,6 +68,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+// 4-byte asynchronous copy global -> shared; src_bytes 0 writes a zero and
+// reads nothing
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
 // (a, b) -> fp16 pair (hi) and the fp16 pair of the remainders (lo)
 __device__ __forceinline__ uint32_t pack_hl(float a, float b, uint32_t& lo) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -146,15 +153,23 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         *reinterpret_cast<uint2*>(vs + j * C::ROW + ch * 8) = vh;
       }
     }
+    // key positions and the bias tile also arrive by cp.async (4-byte copies:
+    // bias rows of bias_ld floats need not be 16-byte aligned), so no thread
+    // waits on a load here; out-of-range bias entries are zero-filled
     for (int j = tid; j < AR_BC; j += AR_THREADS) {
       const int key = j0 + j;
-      kpos_s[b * AR_BC + j] = key >= T ? 0x7fffffff : (key < t_prev ? key : row_pos[key - t_prev]);
+      int* dst = &kpos_s[b * AR_BC + j];
+      if (key >= T || key < t_prev)
+        *dst = key >= T ? 0x7fffffff : key;
+      else
+        cp_async4(dst, row_pos + (key - t_prev), 4);
     }
     if (bias) {
       float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
       for (int i = tid; i < AR_BR * AR_BC; i += AR_THREADS) {
         const int rr = i / AR_BC, j = i - rr * AR_BC, row = r0 + rr, key = j0 + j;
-        bt[i] = (row < n && key < T) ? bias[(size_t)row * bias_ld + key] : 0.f;
+        const bool in = row < n && key < T;
+        cp_async4(bt + i, in ? bias + (size_t)row * bias_ld + key : bias, in ? 4 : 0);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -195,97 +210,101 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    const int b = kt & 1;
-    const uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
-    const uint8_t* vs = ks + C::KV_BYTES;
-    const int* kp = kpos_s + b * AR_BC;
-    const float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
-    // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7
-    float s[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; nt += 2) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      s[nt + 1][0] = s[nt + 1][1] = s[nt + 1][2] = s[nt + 1][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < NKK; ++kk) {
-        // matrices: keys 8nt.. x dims lo / hi, keys 8(nt+1).. x dims lo / hi
-        uint32_t kb[4];
-        const int key = 8 * nt + (lane & 7) + 8 * (lane >> 4);
-        ldsm_x4(kb, ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
-        mma_f16(s[nt], qa[kk], kb[0], kb[1]);
-        mma_f16(s[nt + 1], qa[kk], kb[2], kb[3]);
-        mma_f16(s[nt], ql[kk], kb[0], kb[1]);
-        mma_f16(s[nt + 1], ql[kk], kb[2], kb[3]);
-      }
-    }
-    // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
-    float mxa = -INFINITY, mxb = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = 8 * nt + 2 * t + (e & 1);
-        const bool rowb = e >= 2;
-        const int rp = rowb ? pb : pa;
-        float v = -INFINITY;
-        if (rp >= 0 && kp[j] <= rp) {
-          v = __fdiv_rn(s[nt][e], sdiv);
-          if (bias) v += fminf(0.f, bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j]);
+    // a warp whose 16 rows are all past n (tree verification: 31 rows in a
+    // 64-row block) only helps load the tiles
+    if (r0 + 16 * warp < n) {
+      const int b = kt & 1;
+      const uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
+      const uint8_t* vs = ks + C::KV_BYTES;
+      const int* kp = kpos_s + b * AR_BC;
+      const float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
+      // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7
+      float s[8][4];
+  #pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        s[nt + 1][0] = s[nt + 1][1] = s[nt + 1][2] = s[nt + 1][3] = 0.f;
+  #pragma unroll
+        for (int kk = 0; kk < NKK; ++kk) {
+          // matrices: keys 8nt.. x dims lo / hi, keys 8(nt+1).. x dims lo / hi
+          uint32_t kb[4];
+          const int key = 8 * nt + (lane & 7) + 8 * (lane >> 4);
+          ldsm_x4(kb, ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
+          mma_f16(s[nt], qa[kk], kb[0], kb[1]);
+          mma_f16(s[nt + 1], qa[kk], kb[2], kb[3]);
+          mma_f16(s[nt], ql[kk], kb[0], kb[1]);
+          mma_f16(s[nt + 1], ql[kk], kb[2], kb[3]);
         }
-        s[nt][e] = v;
-        if (rowb) mxb = fmaxf(mxb, v); else mxa = fmaxf(mxa, v);
       }
-    }
-    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
-    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
-    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-    const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
-    const float aa = na == -INFINITY ? 1.f : expf(ma - na), ab = nb == -INFINITY ? 1.f : expf(mb - nb);
-    float sa = 0.f, sb = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const bool rowb = e >= 2;
-        const float m = rowb ? nb : na;
-        const float p = s[nt][e] == -INFINITY ? 0.f : expf(s[nt][e] - m);
-        s[nt][e] = p;
-        if (rowb) sb += p; else sa += p;
+      // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
+      float mxa = -INFINITY, mxb = -INFINITY;
+  #pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 8 * nt + 2 * t + (e & 1);
+          const bool rowb = e >= 2;
+          const int rp = rowb ? pb : pa;
+          float v = -INFINITY;
+          if (rp >= 0 && kp[j] <= rp) {
+            v = __fdiv_rn(s[nt][e], sdiv);
+            if (bias) v += fminf(0.f, bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j]);
+          }
+          s[nt][e] = v;
+          if (rowb) mxb = fmaxf(mxb, v); else mxa = fmaxf(mxa, v);
+        }
       }
-    }
-    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
-    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
-    sb += __shfl_xor_sync(0xffffffffu, sb, 1);
-    sb += __shfl_xor_sync(0xffffffffu, sb, 2);
-    la = la * aa + sa;
-    lb = lb * ab + sb;
-    ma = na;
-    mb = nb;
-#pragma unroll
-    for (int i = 0; i < NDT; ++i) {
-      o[i][0] *= aa;
-      o[i][1] *= aa;
-      o[i][2] *= ab;
-      o[i][3] *= ab;
-    }
-    // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa4[4], pl4[4];
-      pa4[0] = pack_hl(s[2 * kk][0], s[2 * kk][1], pl4[0]);
-      pa4[1] = pack_hl(s[2 * kk][2], s[2 * kk][3], pl4[1]);
-      pa4[2] = pack_hl(s[2 * kk + 1][0], s[2 * kk + 1][1], pl4[2]);
-      pa4[3] = pack_hl(s[2 * kk + 1][2], s[2 * kk + 1][3], pl4[3]);
-#pragma unroll
-      for (int nd = 0; nd < NDT; nd += 2) {
-        // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then dims 8(nd+1)..
-        uint32_t vb[4];
-        ldsm_x4_t(vb, vs + (16 * kk + (lane & 15)) * C::ROW + (8 * nd + 8 * (lane >> 4)) * 2);
-        mma_f16(o[nd], pa4, vb[0], vb[1]);
-        mma_f16(o[nd + 1], pa4, vb[2], vb[3]);
-        mma_f16(o[nd], pl4, vb[0], vb[1]);
-        mma_f16(o[nd + 1], pl4, vb[2], vb[3]);
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
+      const float aa = na == -INFINITY ? 1.f : expf(ma - na), ab = nb == -INFINITY ? 1.f : expf(mb - nb);
+      float sa = 0.f, sb = 0.f;
+  #pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool rowb = e >= 2;
+          const float m = rowb ? nb : na;
+          const float p = s[nt][e] == -INFINITY ? 0.f : expf(s[nt][e] - m);
+          s[nt][e] = p;
+          if (rowb) sb += p; else sa += p;
+        }
+      }
+      sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+      sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+      sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+      sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+      la = la * aa + sa;
+      lb = lb * ab + sb;
+      ma = na;
+      mb = nb;
+  #pragma unroll
+      for (int i = 0; i < NDT; ++i) {
+        o[i][0] *= aa;
+        o[i][1] *= aa;
+        o[i][2] *= ab;
+        o[i][3] *= ab;
+      }
+      // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
+  #pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t pa4[4], pl4[4];
+        pa4[0] = pack_hl(s[2 * kk][0], s[2 * kk][1], pl4[0]);
+        pa4[1] = pack_hl(s[2 * kk][2], s[2 * kk][3], pl4[1]);
+        pa4[2] = pack_hl(s[2 * kk + 1][0], s[2 * kk + 1][1], pl4[2]);
+        pa4[3] = pack_hl(s[2 * kk + 1][2], s[2 * kk + 1][3], pl4[3]);
+  #pragma unroll
+        for (int nd = 0; nd < NDT; nd += 2) {
+          // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then dims 8(nd+1)..
+          uint32_t vb[4];
+          ldsm_x4_t(vb, vs + (16 * kk + (lane & 15)) * C::ROW + (8 * nd + 8 * (lane >> 4)) * 2);
+          mma_f16(o[nd], pa4, vb[0], vb[1]);
+          mma_f16(o[nd + 1], pa4, vb[2], vb[3]);
+          mma_f16(o[nd], pl4, vb[0], vb[1]);
+          mma_f16(o[nd + 1], pl4, vb[2], vb[3]);
+        }
       }
     }
     __syncthreads();  // buffer b is free for tile kt + 2
