@@ -48,10 +48,36 @@ namespace {
 
 constexpr int G5_BM = 128;                 // weight rows per CTA (the MMA's M)
 constexpr int G5_BK = 64;                  // K per stage: one 128-byte swizzle row of fp16
-constexpr int G5_STAGES = 4;
-constexpr int G5_THREADS = 256;            // 8 warps: all dequantize, all run the epilogue
+constexpr int G5_SA = 4;                   // weight stages
+constexpr int G5_DEQ_WARPS = 8;            // dequantize (one 16-row tile each), then run the epilogue
+constexpr int G5_THREADS = 32 * (G5_DEQ_WARPS + 1);  // + the control warp (TMA, MMA, TMEM)
 constexpr int G5_A_BYTES = G5_BM * G5_BK * 2;
 constexpr int G5_MIN_SPLIT_STEPS = 8;      // K steps per CTA when K is split
+constexpr double G5_CTA_OVERHEAD = 4.0;    // a CTA's fixed cost, in K steps
+
+// activation stages (a deeper ring for narrow token tiles, whose stages are
+// small) and the shared memory of one CTA
+template <int BN>
+struct G5Cfg {
+  static constexpr int SB = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
+  static constexpr int B_BYTES = 2 * BN * 128;  // hi rows, then lo rows
+  static constexpr size_t SMEM = (size_t)G5_SA * G5_A_BYTES + (size_t)SB * B_BYTES + (2 * G5_SA + 2 * SB + 1) * 8 + 1024;
+};
+
+// named barrier 1 over the 8 dequantizing warps (the control warp is elsewhere)
+__device__ __forceinline__ void g5_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * G5_DEQ_WARPS) : "memory"); }
+__device__ __forceinline__ bool g5_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(32 * G5_DEQ_WARPS)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 struct G5Args {
   const uint8_t* codes;
@@ -272,214 +298,241 @@ __device__ __forceinline__ void g5_emit(const G5Args& a, int row, int mb, const 
   }
 }
 
+// One CTA: 8 dequantizing warps (warp T rebuilds 16-row tile T of each K
+// step into the weight stage, then runs the epilogue) and a control warp
+// whose lane 0 moves the activation tiles by TMA and issues the MMAs. The
+// two sides meet only at mbarriers: full_a (the 8 warps wrote a weight
+// stage), full_b (an activation stage landed), empty_a / empty_b (the MMAs
+// of a step finished reading its stages, tcgen05.commit), accum (every MMA
+// done). No CTA-wide barrier sits in the K loop, so every warp runs ahead
+// as far as its stages allow.
+//
 // DENSE: the weight is an fp16 matrix (the LM head) whose 128 x 64 tiles
 // arrive by TMA (tensor map tmw, same swizzle) instead of being rebuilt from
-// codes; ST is then unused.
+// codes; ST is then unused and the 8 warps only run the epilogue.
 template <int BN, typename ST, bool DENSE>
 __global__ void __launch_bounds__(G5_THREADS, 1)
 gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, G5Args a) {
   static_assert(2 * BN <= 256, "hi and lo planes form one MMA of N = 2 BN <= 256");
-  constexpr int S = G5_STAGES;
-  constexpr int B_BYTES = 2 * BN * 128;  // hi rows, then lo rows
-  constexpr int STAGE = G5_A_BYTES + B_BYTES;
+  using C = G5Cfg<BN>;
+  constexpr int SA = G5_SA, SB = C::SB;
   constexpr uint32_t IDESC = idesc_f16(G5_BM, 2 * BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // activation tile landed
-  uint64_t* empty = full_b + S;                                      // stage's MMAs done
-  uint64_t* accum = empty + S;                                       // every MMA done
-  uint64_t* full_a = accum + 1;                                      // DENSE: weight tile landed
+  uint8_t* Bst = smem + SA * G5_A_BYTES;                                  // activation stages
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(Bst + SB * C::B_BYTES);  // weight stage written / landed
+  uint64_t* empty_a = full_a + SA;                                        // weight stage read by its MMAs
+  uint64_t* full_b = empty_a + SA;                                        // activation stage landed
+  uint64_t* empty_b = full_b + SB;                                        // activation stage read
+  uint64_t* accum = empty_b + SB;                                         // every MMA done
   __shared__ uint32_t tmem_base;
   __shared__ int abort_s, last_s;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * G5_BM, m0 = blockIdx.y * BN;
-  // this CTA's K steps: kb0 + i for i < KB
+  // this CTA's K steps: kb0 + p for p < KB
   const int z = blockIdx.z;
   const int kb0 = (int)((long long)a.P * z / a.ks), KB = (int)((long long)a.P * (z + 1) / a.ks) - kb0;
 
   if (tid == 0) {
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&full_a[i], DENSE ? 1 : G5_DEQ_WARPS);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < SB; ++i) {
       mbar_init(&full_b[i], 1);
-      mbar_init(&empty[i], 1);
-      if (DENSE) mbar_init(&full_a[i], 1);
+      mbar_init(&empty_b[i], 1);
     }
     mbar_init(accum, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
-    if (DENSE) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
     abort_s = 0;
   }
-  if (warp == 0) {
+  if (warp == G5_DEQ_WARPS) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                  "r"(2 * BN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  // weights never depend on the previous kernel: the first stages' codes go
-  // to shared memory before the dependency wait
-  G5Queue<ST> wq;
-  int a_issued = 0, a_waited = 0;  // DENSE, thread 0: weight tiles requested / landed
-  if constexpr (DENSE) {
-    __syncthreads();  // barriers initialized
-    if (tid == 0)
-      for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
-        mbar_expect_tx(&full_a[kb], G5_A_BYTES);
-        tma_load_2d(smem + kb * STAGE, &tmw, (kb0 + kb) * G5_BK, n0, &full_a[kb]);
-        ++a_issued;
-      }
-  } else {
-    wq.init(a, n0, kb0, kb0 + KB, tid);
-    for (int kb = 0; kb < S - 1 && kb < KB; ++kb) wq.pop(a, smem + kb * STAGE, n0, tid, kb);
   }
   tc05_fence_before();
   __syncthreads();
   tc05_fence_after();
   const uint32_t tmem = tmem_base;
   pdl_launch_dependents();
-  pdl_wait();
-  int tma_issued = 0;  // thread 0: activation tiles requested
-  if (tid == 0) {
-    for (int kb = 0; kb < S - 1 && kb < KB; ++kb) {
-      mbar_expect_tx(&full_b[kb], B_BYTES);
-      tma_load_3d(smem + kb * STAGE + G5_A_BYTES, &tmx, (kb0 + kb) * G5_BK, m0, &full_b[kb]);
-      ++tma_issued;
-    }
-  }
-  int tma_waited = 0;  // thread 0: activation tiles that landed and were consumed
-  for (int kb = 0; kb < KB; ++kb) {
-    const int s = kb % S;
-    __syncthreads();  // stage kb's weight tile is written (and fenced) by every thread
-    if (abort_s) break;
-    if (tid == 0) {
-      bool landed = true;
-      if constexpr (DENSE) {
-        landed = mbar_wait_bounded(&full_a[s], (uint32_t)((kb / S) & 1), a.spin);
-        a_waited += landed ? 1 : 0;
-      }
-      landed = landed && mbar_wait_bounded(&full_b[s], (uint32_t)((kb / S) & 1), a.spin);
-      if (!landed) {
-        atomicOr(a.fault, 8);
-        abort_s = 1;
-      } else {
-        ++tma_waited;
-        tc05_fence_after();
-        const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + G5_A_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < G5_BK / 16; ++kk)
-          tc05_mma(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), IDESC, (kb | kk) != 0);
-        tc05_commit(&empty[s]);
-      }
-    }
-    // stage kb + S - 1 into the stage step kb - 1 used, once its MMAs are done
-    const int nk = kb + S - 1;
-    if (nk < KB) {
-      const int ns = nk % S;
-      if (kb >= 1) {
-        const bool freed = mbar_wait_bounded(&empty[ns], (uint32_t)(((kb - 1) / S) & 1), a.spin);
-        if (!__all_sync(0xffffffffu, freed)) {
-          if (lane == 0) {
-            atomicOr(a.fault, 8);
-            abort_s = 1;
+  volatile int* abort_v = &abort_s;
+
+  if (warp < G5_DEQ_WARPS) {
+    // ---- dequantizing warps: weights never depend on the previous kernel,
+    // so they stream from the first instruction
+    if constexpr (!DENSE) {
+      G5Queue<ST> wq;
+      wq.init(a, n0, kb0, kb0 + KB, tid);
+      for (int p = 0; p < KB; ++p) {
+        const int s = p % SA;
+        if (p >= SA) {
+          // the stage's previous step (p - SA) must have been read by its MMAs
+          const bool freed = mbar_wait_bounded(&empty_a[s], (uint32_t)((p / SA - 1) & 1), a.spin);
+          if (!__all_sync(0xffffffffu, freed)) {
+            if (lane == 0) {
+              atomicOr(a.fault, 8);
+              *abort_v = 1;
+            }
+            break;
           }
-          continue;  // the next barrier sees the abort
         }
-      }
-      if constexpr (!DENSE) wq.pop(a, smem + ns * STAGE, n0, tid, nk);  // steps are dequantized in order
-      if (tid == 0) {
-        if constexpr (DENSE) {
-          mbar_expect_tx(&full_a[ns], G5_A_BYTES);
-          tma_load_2d(smem + ns * STAGE, &tmw, (kb0 + nk) * G5_BK, n0, &full_a[ns]);
-          ++a_issued;
-        }
-        mbar_expect_tx(&full_b[ns], B_BYTES);
-        tma_load_3d(smem + ns * STAGE + G5_A_BYTES, &tmx, (kb0 + nk) * G5_BK, m0, &full_b[ns]);
-        ++tma_issued;
+        if (*abort_v) break;
+        wq.pop(a, smem + s * G5_A_BYTES, n0, tid, p);  // ends with the async-proxy fence
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
       }
     }
-  }
-  __syncthreads();
-  bool ok = !abort_s;
-  if (tid == 0) {
-    if (!ok) {
-      // let every activation load in flight land before the stages go away
-      for (int i = tma_waited; i < tma_issued; ++i) mbar_wait_bounded(&full_b[i % S], (uint32_t)((i / S) & 1));
-      for (int i = a_waited; i < a_issued; ++i) mbar_wait_bounded(&full_a[i % S], (uint32_t)((i / S) & 1));
+  } else if (lane == 0) {
+    // ---- control thread: activation (and, DENSE, weight) tiles by TMA, MMAs
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+    int a_issued = 0, a_landed = 0, b_issued = 0, b_landed = 0;
+    if constexpr (DENSE) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
+      for (int p = 0; p < SA && p < KB; ++p, ++a_issued) {
+        mbar_expect_tx(&full_a[p], G5_A_BYTES);
+        tma_load_2d(smem + p * G5_A_BYTES, &tmw, (kb0 + p) * G5_BK, n0, &full_a[p]);
+      }
+    }
+    pdl_wait();  // the activation rows come from the previous kernel
+    for (int p = 0; p < SB && p < KB; ++p, ++b_issued) {
+      mbar_expect_tx(&full_b[p], C::B_BYTES);
+      tma_load_3d(Bst + p * C::B_BYTES, &tmx, (kb0 + p) * G5_BK, m0, &full_b[p]);
+    }
+    for (int p = 0; p < KB; ++p) {
+      const int sa = p % SA, sb = p % SB;
+      bool ok = mbar_wait_bounded(&full_a[sa], (uint32_t)((p / SA) & 1), a.spin);
+      if (ok && DENSE) ++a_landed;
+      ok = ok && mbar_wait_bounded(&full_b[sb], (uint32_t)((p / SB) & 1), a.spin);
+      if (ok) ++b_landed;
+      if (!ok || *abort_v) {
+        if (!ok) atomicOr(a.fault, 8);
+        *abort_v = 1;
+        break;
+      }
+      tc05_fence_after();
+      const uint32_t sa_addr = smem_u32(smem + sa * G5_A_BYTES), sb_addr = smem_u32(Bst + sb * C::B_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < G5_BK / 16; ++kk)
+        tc05_mma(tmem, smem_desc_sw128(sa_addr + kk * 32), smem_desc_sw128(sb_addr + kk * 32), IDESC, (p | kk) != 0);
+      tc05_commit(&empty_a[sa]);
+      tc05_commit(&empty_b[sb]);
+      // refill the stages of step p - 1 (its MMAs were issued one step ago)
+      // with step p - 1 + SB (activations) and, DENSE, p - 1 + SA (weights)
+      if (p >= 1) {
+        const int q = p - 1;
+        const bool nb = q + SB < KB, na = DENSE && q + SA < KB;
+        if (nb || na) {
+          bool freed = true;
+          if (nb) freed = mbar_wait_bounded(&empty_b[q % SB], (uint32_t)((q / SB) & 1), a.spin);
+          if (freed && na) freed = mbar_wait_bounded(&empty_a[q % SA], (uint32_t)((q / SA) & 1), a.spin);
+          if (!freed) {
+            atomicOr(a.fault, 8);
+            *abort_v = 1;
+            break;
+          }
+          if (nb) {
+            mbar_expect_tx(&full_b[q % SB], C::B_BYTES);
+            tma_load_3d(Bst + (q % SB) * C::B_BYTES, &tmx, (kb0 + q + SB) * G5_BK, m0, &full_b[q % SB]);
+            ++b_issued;
+          }
+          if (na) {
+            mbar_expect_tx(&full_a[q % SA], G5_A_BYTES);
+            tma_load_2d(smem + (q % SA) * G5_A_BYTES, &tmw, (kb0 + q + SA) * G5_BK, n0, &full_a[q % SA]);
+            ++a_issued;
+          }
+        }
+      }
+    }
+    if (*abort_v) {
+      // let every tile load in flight land before the stages go away
+      for (int i = b_landed; i < b_issued; ++i) mbar_wait_bounded(&full_b[i % SB], (uint32_t)((i / SB) & 1));
+      for (int i = a_landed; i < a_issued; ++i) mbar_wait_bounded(&full_a[i % SA], (uint32_t)((i / SA) & 1));
     }
     tc05_commit(accum);  // completes once every MMA issued above is done
   }
-  const bool done = mbar_wait_bounded(accum, 0u, ok ? a.spin : MBAR_SPIN_LIMIT);
-  if (!done) {
-    if (lane == 0) atomicOr(a.fault, 8);
-    ok = false;
-  }
-  tc05_fence_after();
-  const bool all_ok = __syncthreads_and(ok ? 1 : 0);
-  // warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and token
-  // columns [BN/2 (w / 4), BN/2 (w / 4 + 1)) of both planes
-  const int quarter = warp & 3, half = warp >> 2;
-  const int row = n0 + 32 * quarter + lane;
-  constexpr int COLS = BN / 2;
-  if (a.ks == 1) {
-    if (all_ok) {
-      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
-        float v[16], lo[16];
-        const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
-        __syncwarp();
-        tmem_ld16(ta, v);
-        tmem_ld16(ta + (uint32_t)BN, lo);
-        if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
+
+  if (warp < G5_DEQ_WARPS) {
+    // ---- epilogue (the 8 warps; named barrier 1 spans them only)
+    const bool done = mbar_wait_bounded(accum, 0u, MBAR_SPIN_LIMIT);
+    tc05_fence_after();
+    pdl_wait();  // outputs and residual rows may belong to earlier kernels
+    if (!done && lane == 0) atomicOr(a.fault, 8);
+    const bool all_ok = g5_bar_and(done && !*abort_v);
+    // warp w reads TMEM lanes 32 (w % 4) .. + 31 (weight rows) and token
+    // columns [BN/2 (w / 4), BN/2 (w / 4 + 1)) of both planes
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = n0 + 32 * quarter + lane;
+    constexpr int COLS = BN / 2;
+    if (a.ks == 1) {
+      if (all_ok) {
+        for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+          float v[16], lo[16];
+          const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+          __syncwarp();
+          tmem_ld16(ta, v);
+          tmem_ld16(ta + (uint32_t)BN, lo);
+          if (m0 + c0 >= a.M) continue;  // warp-uniform: the loads above are collective
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] += lo[j];
-        g5_emit(a, row, m0 + c0, v, lane);
+          for (int j = 0; j < 16; ++j) v[j] += lo[j];
+          g5_emit(a, row, m0 + c0, v, lane);
+        }
       }
-    }
-  } else {
-    // split K: the partial tile to ws[z][m][row]; every CTA of the tile
-    // takes a ticket (an aborted CTA too, so the counter returns to zero)
-    if (all_ok) {
-      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
-        float v[16], lo[16];
-        const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
-        __syncwarp();
-        tmem_ld16(ta, v);
-        tmem_ld16(ta + (uint32_t)BN, lo);
-        if (row < a.rows) {
+    } else {
+      // split K: the partial tile to ws[z][m][row]; every CTA of the tile
+      // takes a ticket (an aborted CTA too, so the counter returns to zero)
+      if (all_ok) {
+        for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+          float v[16], lo[16];
+          const uint32_t ta = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+          __syncwarp();
+          tmem_ld16(ta, v);
+          tmem_ld16(ta + (uint32_t)BN, lo);
+          if (row < a.rows) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < a.M) a.ws[((size_t)z * a.M + m) * a.rows + row] = v[j] + lo[j];
+            for (int j = 0; j < 16; ++j) {
+              const int m = m0 + c0 + j;
+              if (m < a.M) a.ws[((size_t)z * a.M + m) * a.rows + row] = v[j] + lo[j];
+            }
           }
         }
       }
-    }
-    __threadfence();
-    __syncthreads();
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-    if (tid == 0) last_s = atomicAdd(&a.cnt[tile], 1) == a.ks - 1;
-    __syncthreads();
-    if (last_s) {
       __threadfence();
-      for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
-        if (m0 + c0 >= a.M) break;  // warp-uniform
-        float v[16];
+      g5_bar();
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      if (tid == 0) last_s = atomicAdd(&a.cnt[tile], 1) == a.ks - 1;
+      g5_bar();
+      if (last_s) {
+        __threadfence();
+        for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 16) {
+          if (m0 + c0 >= a.M) break;  // warp-uniform
+          float v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          float acc = 0.f;
-          if (m < a.M && row < a.rows)
-            for (int zz = 0; zz < a.ks; ++zz) acc += __ldcg(a.ws + ((size_t)zz * a.M + m) * a.rows + row);
-          v[j] = acc;
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            float acc = 0.f;
+            if (m < a.M && row < a.rows)
+              for (int zz = 0; zz < a.ks; ++zz) acc += __ldcg(a.ws + ((size_t)zz * a.M + m) * a.rows + row);
+            v[j] = acc;
+          }
+          g5_emit(a, row, m0 + c0, v, lane);
         }
-        g5_emit(a, row, m0 + c0, v, lane);
+        if (tid == 0) a.cnt[tile] = 0;
       }
-      if (tid == 0) a.cnt[tile] = 0;
     }
   }
   tc05_fence_before();
   __syncthreads();
-  if (warp == 0)
+  if (warp == G5_DEQ_WARPS) {
+    // no MMA may still write the accumulator when it is freed (the epilogue's
+    // wait can only have given up on a failed CTA)
+    if (lane == 0) mbar_wait_bounded(accum, 0u, MBAR_SPIN_LIMIT);
+    __syncwarp();
+    tc05_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+  }
 }
 
 // fp32 rows (optionally RMS-normalized, chat.py:63-66) -> two planes of fp16
@@ -536,7 +589,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 template <int BN, typename ST, bool DENSE = false>
 int g5_launch(const CUtensorMap& map, const G5Args& a, cudaStream_t s, const CUtensorMap* wmap = nullptr) {
   auto kern = gemm_tc05_kernel<BN, ST, DENSE>;
-  const size_t smem = (size_t)G5_STAGES * (G5_A_BYTES + 2 * BN * 128) + (3 * G5_STAGES + 1) * 8 + 1024;
+  const size_t smem = G5Cfg<BN>::SMEM;
   const int rc = set_smem_limit((const void*)kern, smem, "gemm_tc05");
   if (rc) return rc;
   const dim3 grid((a.rows + G5_BM - 1) / G5_BM, (a.M + BN - 1) / BN, a.ks);
@@ -613,16 +666,24 @@ int g5_prepare(const float* x, int ldx, int M, int K, int P, const float* norm_w
   int bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
   const int row_tiles = (rows + G5_BM - 1) / G5_BM;
   while (bn > 64 && row_tiles * ((M + bn - 1) / bn) < sm_count()) bn /= 2;
-  // K splits while the tiles still leave SMs idle (two CTAs fit on an SM at
-  // BN = 32): at least G5_MIN_SPLIT_STEPS K steps per CTA, partials within
-  // the workspace
+  // K splits: one CTA per SM, so a grid of `tiles` x ks CTAs runs in
+  // ceil(tiles ks / SMs) waves of P / ks steps (plus about G5_CTA_OVERHEAD
+  // steps of pipeline fill and epilogue each); take the ks with the fewest
+  // step-times, at least G5_MIN_SPLIT_STEPS K steps per CTA, partials
+  // within the workspace
   const int tiles = row_tiles * ((M + bn - 1) / bn);
-  const int target = sm_count() * (bn <= 32 ? 2 : 1);
   int ks = 1;
-  if (sw && sw->ws && sw->cnt && tiles < target && tiles <= sw->cnt_n) {
-    ks = std::min((target + tiles - 1) / tiles, P / G5_MIN_SPLIT_STEPS);
-    while (ks > 1 && (size_t)ks * M * rows > sw->ws_elems) --ks;
-    ks = std::max(ks, 1);
+  if (sw && sw->ws && sw->cnt && tiles <= sw->cnt_n) {
+    const int sms = sm_count();
+    double best = 1e30;
+    for (int k = 1; k <= std::max(1, P / G5_MIN_SPLIT_STEPS); ++k) {
+      if (k > 1 && (size_t)k * M * rows > sw->ws_elems) break;
+      const double t = (double)((tiles * k + sms - 1) / sms) * ((double)P / k + G5_CTA_OVERHEAD);
+      if (t < best - 1e-9) {
+        best = t;
+        ks = k;
+      }
+    }
   }
   // the fp16 planes as a 3-D tensor (K innermost, rows, plane), boxes of
   // 64 x BN x 2, 128-byte swizzle: a stage holds BN hi rows then BN lo rows
