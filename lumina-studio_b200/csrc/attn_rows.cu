@@ -40,11 +40,11 @@ constexpr int AR_MIN_SPLIT_TILES = 4;  // key tiles per CTA when the keys are sp
 template <int HD>
 struct ArCfg {
   static constexpr int ROW = HD * 2 + 16;  // padded fp16 row (bytes): ldmatrix phases hit distinct banks
-  static constexpr int Q_BYTES = AR_BR * ROW;
+  static constexpr int Q_BYTES = AR_BR * ROW;  // q hi + lo staged in one K/V buffer (2 KV_BYTES)
   static constexpr int KV_BYTES = AR_BC * ROW;
   static constexpr int B_BYTES = AR_BR * AR_BC * 4;  // bias tile (fp32)
-  // [Q hi][Q lo][2 x (K, V)][kpos 2 x AR_BC ints][bias 2 x tile]
-  static constexpr int SMEM_NOBIAS = 2 * Q_BYTES + 4 * KV_BYTES + 2 * AR_BC * 4;
+  // [2 x (K, V)][kpos 2 x AR_BC ints][bias 2 x tile]; two CTAs fit on an SM
+  static constexpr int SMEM_NOBIAS = 4 * KV_BYTES + 2 * AR_BC * 4;
   static constexpr int SMEM_BIAS = SMEM_NOBIAS + 2 * B_BYTES;
 };
 
@@ -103,10 +103,8 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   const size_t bstride = (size_t)nkv * bs * HD;
 
   extern __shared__ __align__(16) uint8_t sm[];
-  uint8_t* Qs = sm;                   // fp16(q)
-  uint8_t* Ql = sm + C::Q_BYTES;       // fp16(q - fp16(q))
-  uint8_t* KVs = sm + 2 * C::Q_BYTES;  // [buf][K | V]
-  int* kpos_s = reinterpret_cast<int*>(sm + 2 * C::Q_BYTES + 4 * C::KV_BYTES);  // [buf][AR_BC]
+  uint8_t* KVs = sm;  // [buf][K | V]
+  int* kpos_s = reinterpret_cast<int*>(sm + 4 * C::KV_BYTES);  // [buf][AR_BC]
   float* bias_s = reinterpret_cast<float*>(kpos_s + 2 * AR_BC);             // [buf][AR_BR][AR_BC]
 
   // tile kt of K, V (and positions, bias) into buffer kt & 1; this CTA's
@@ -120,13 +118,26 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     uint8_t* vs = ks + C::KV_BYTES;
     const int j0 = kt * AR_BC;
     if constexpr (sizeof(KT) == 2) {
-      constexpr int CH = HD * 2 / 16;
-      for (int i = tid; i < AR_BC * CH; i += AR_THREADS) {
-        const int j = i / CH, ch = i - j * CH, key = j0 + j;
+      // thread tid copies 16-byte chunk tid % CH of keys tid / CH + it * KSTEP;
+      // the page numbers of those keys are read first, all at once (each
+      // cp.async below is a memory-clobbering asm that would otherwise make
+      // every page-table read wait for the previous copy's issue)
+      constexpr int CH = HD * 2 / 16, IT = AR_BC * CH / AR_THREADS, KSTEP = AR_THREADS / CH;
+      static_assert(AR_BC * CH % AR_THREADS == 0 && AR_THREADS % CH == 0, "whole chunks per thread");
+      const int ch = tid % CH, jt = tid / CH;
+      int page[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int key = j0 + jt + it * KSTEP;
+        page[it] = key < T ? block_table[key / bs] : 0;
+      }
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int j = jt + it * KSTEP, key = j0 + j;
         uint8_t* kd = ks + j * C::ROW + ch * 16;
         uint8_t* vd = vs + j * C::ROW + ch * 16;
         if (key < T) {
-          const size_t base = (size_t)block_table[key / bs] * bstride + ((size_t)kvh * bs + key % bs) * HD;
+          const size_t base = (size_t)page[it] * bstride + ((size_t)kvh * bs + key % bs) * HD;
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(kd)),
                        "l"(reinterpret_cast<const uint8_t*>(kcache + base) + ch * 16) : "memory");
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(vd)),
@@ -176,7 +187,12 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   };
 
   if (kt0 < kt1) load_tile(kt0);
-  // q rows of the block -> fp16 hi and lo parts (rows past n are zero)
+  // q rows of the block -> fp16 hi and lo parts (rows past n are zero),
+  // staged in the K/V buffer that tile kt0 does not use, then held in
+  // registers for the whole key loop
+  static_assert(2 * C::Q_BYTES <= 2 * C::KV_BYTES, "q hi and lo fit in one K/V buffer");
+  uint8_t* Qs = KVs + (size_t)((kt0 + 1) & 1) * 2 * C::KV_BYTES;  // fp16(q)
+  uint8_t* Ql = Qs + C::Q_BYTES;                                    // fp16(q - fp16(q))
   for (int i = tid; i < AR_BR * (HD / 4); i += AR_THREADS) {
     const int rr = i / (HD / 4), c4 = i - rr * (HD / 4), row = r0 + rr;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -196,6 +212,7 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     ldsm_x4(qa[kk], Qs + off);
     ldsm_x4(ql[kk], Ql + off);
   }
+  __syncthreads();  // the staging buffer is free for tile kt0 + 1
 
   float o[NDT][4];
 #pragma unroll
@@ -218,29 +235,37 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       const uint8_t* vs = ks + C::KV_BYTES;
       const int* kp = kpos_s + b * AR_BC;
       const float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
-      // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7
+      // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7; the
+      // k-step loop is outside so that consecutive MMAs feed 8 different
+      // accumulators (a chain of dependent mma.sync would stall on each)
       float s[8][4];
-  #pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-        s[nt + 1][0] = s[nt + 1][1] = s[nt + 1][2] = s[nt + 1][3] = 0.f;
-  #pragma unroll
-        for (int kk = 0; kk < NKK; ++kk) {
-          // matrices: keys 8nt.. x dims lo / hi, keys 8(nt+1).. x dims lo / hi
-          uint32_t kb[4];
-          const int key = 8 * nt + (lane & 7) + 8 * (lane >> 4);
-          ldsm_x4(kb, ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
-          mma_f16(s[nt], qa[kk], kb[0], kb[1]);
-          mma_f16(s[nt + 1], qa[kk], kb[2], kb[3]);
-          mma_f16(s[nt], ql[kk], kb[0], kb[1]);
-          mma_f16(s[nt + 1], ql[kk], kb[2], kb[3]);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < NKK; ++kk) {
+        // matrices of pair np: keys 16np.. x dims lo / hi, keys 16np+8.. x dims lo / hi
+        uint32_t kb[4][4];
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          const int key = 16 * np + (lane & 7) + 8 * (lane >> 4);
+          ldsm_x4(kb[np], ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
+        }
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          mma_f16(s[2 * np], qa[kk], kb[np][0], kb[np][1]);
+          mma_f16(s[2 * np + 1], qa[kk], kb[np][2], kb[np][3]);
+        }
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          mma_f16(s[2 * np], ql[kk], kb[np][0], kb[np][1]);
+          mma_f16(s[2 * np + 1], ql[kk], kb[np][2], kb[np][3]);
         }
       }
       // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
       float mxa = -INFINITY, mxb = -INFINITY;
-  #pragma unroll
+#pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-  #pragma unroll
+#pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int j = 8 * nt + 2 * t + (e & 1);
           const bool rowb = e >= 2;
@@ -261,9 +286,9 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
       const float aa = na == -INFINITY ? 1.f : expf(ma - na), ab = nb == -INFINITY ? 1.f : expf(mb - nb);
       float sa = 0.f, sb = 0.f;
-  #pragma unroll
+#pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-  #pragma unroll
+#pragma unroll
         for (int e = 0; e < 4; ++e) {
           const bool rowb = e >= 2;
           const float m = rowb ? nb : na;
@@ -280,7 +305,7 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       lb = lb * ab + sb;
       ma = na;
       mb = nb;
-  #pragma unroll
+#pragma unroll
       for (int i = 0; i < NDT; ++i) {
         o[i][0] *= aa;
         o[i][1] *= aa;
@@ -288,22 +313,32 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         o[i][3] *= ab;
       }
       // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
-  #pragma unroll
+#pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t pa4[4], pl4[4];
         pa4[0] = pack_hl(s[2 * kk][0], s[2 * kk][1], pl4[0]);
         pa4[1] = pack_hl(s[2 * kk][2], s[2 * kk][3], pl4[1]);
         pa4[2] = pack_hl(s[2 * kk + 1][0], s[2 * kk + 1][1], pl4[2]);
         pa4[3] = pack_hl(s[2 * kk + 1][2], s[2 * kk + 1][3], pl4[3]);
-  #pragma unroll
-        for (int nd = 0; nd < NDT; nd += 2) {
-          // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then dims 8(nd+1)..
-          uint32_t vb[4];
-          ldsm_x4_t(vb, vs + (16 * kk + (lane & 15)) * C::ROW + (8 * nd + 8 * (lane >> 4)) * 2);
-          mma_f16(o[nd], pa4, vb[0], vb[1]);
-          mma_f16(o[nd + 1], pa4, vb[2], vb[3]);
-          mma_f16(o[nd], pl4, vb[0], vb[1]);
-          mma_f16(o[nd + 1], pl4, vb[2], vb[3]);
+#pragma unroll
+        for (int nd = 0; nd < NDT; nd += 4) {
+          // matrices (transposed): keys 16kk.. / 16kk+8.. x dims 8nd.., then
+          // dims 8(nd+1)..; two such pairs, so that an accumulator's hi and lo
+          // products are four MMAs apart
+          uint32_t vb[2][4];
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            ldsm_x4_t(vb[u], vs + (16 * kk + (lane & 15)) * C::ROW + (8 * (nd + 2 * u) + 8 * (lane >> 4)) * 2);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            mma_f16(o[nd + 2 * u], pa4, vb[u][0], vb[u][1]);
+            mma_f16(o[nd + 2 * u + 1], pa4, vb[u][2], vb[u][3]);
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            mma_f16(o[nd + 2 * u], pl4, vb[u][0], vb[u][1]);
+            mma_f16(o[nd + 2 * u + 1], pl4, vb[u][2], vb[u][3]);
+          }
         }
       }
     }

@@ -48,20 +48,29 @@ namespace {
 
 constexpr int G5_BM = 128;                 // weight rows per CTA (the MMA's M)
 constexpr int G5_BK = 64;                  // K per stage: one 128-byte swizzle row of fp16
-constexpr int G5_SA = 4;                   // weight stages
 constexpr int G5_DEQ_WARPS = 8;            // dequantize (one 16-row tile each), then run the epilogue
-constexpr int G5_THREADS = 32 * (G5_DEQ_WARPS + 1);  // + the control warp (TMA, MMA, TMEM)
+constexpr int G5_MMA_WARP = G5_DEQ_WARPS;  // tensor memory and the MMAs
+constexpr int G5_THREADS = 32 * (G5_DEQ_WARPS + 2);  // + the MMA warp + the TMA warp
 constexpr int G5_A_BYTES = G5_BM * G5_BK * 2;
 constexpr int G5_MIN_SPLIT_STEPS = 8;      // K steps per CTA when K is split
 constexpr double G5_CTA_OVERHEAD = 4.0;    // a CTA's fixed cost, in K steps
 
-// activation stages (a deeper ring for narrow token tiles, whose stages are
-// small) and the shared memory of one CTA
+// A stage holds G5_KS K steps: [weight tiles | activation tiles], G5_KS of
+// each. S stages, code chunks of CK steps, RC chunk slots per dequantizing
+// warp; shared memory of one CTA: [stages][code rings][mbarriers]
+constexpr int G5_KS = 2;
 template <int BN>
 struct G5Cfg {
-  static constexpr int SB = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
-  static constexpr int B_BYTES = 2 * BN * 128;  // hi rows, then lo rows
-  static constexpr size_t SMEM = (size_t)G5_SA * G5_A_BYTES + (size_t)SB * B_BYTES + (2 * G5_SA + 2 * SB + 1) * 8 + 1024;
+  static constexpr int B_BYTES = 2 * BN * 128;  // one step's activations: hi rows, then lo rows
+  static constexpr int STAGE = G5_KS * (G5_A_BYTES + B_BYTES);
+  static constexpr int S = BN <= 32 ? 3 : 2;
+  static constexpr int CK = BN <= 64 ? 4 : 2;
+  static constexpr int RC = BN <= 64 ? 4 : 3;
+  static constexpr int RING_SLOT = CK * 512 + CK * 16 * 4;  // G5Ring<CK>::SLOT
+  static constexpr int RING_BYTES = 8 * RC * RING_SLOT;
+  static constexpr int N_BARS = 3 * S + 1 + 8 * RC;
+  static constexpr size_t SMEM = (size_t)S * STAGE + RING_BYTES + N_BARS * 8 + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory of one CTA");
 };
 
 // named barrier 1 over the 8 dequantizing warps (the control warp is elsewhere)
@@ -167,38 +176,62 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // Thread (warp T, lane L = 4g + t) owns the 16-byte fragment word of 16-row
 // tile T at each K step: rows 16T + g (low nibbles) and 16T + g + 8 (high
 // nibbles), columns 32(j >> 1) + 16(j & 1) + 4t + q of byte q of word j.
-// The word and the two rows' group scales are loaded G5_PD steps before they
-// are dequantized (a register queue), so no step waits on its own load. Step
-// p lives in slot p mod G5_PD for its whole time in the queue: every slot is
-// named by a constant, so no queue entry is ever moved -- moving a register
-// whose load is still in flight would wait for that load.
 // Each run of four columns becomes one 8-byte store of four fp16 values at
 // the 128-byte-swizzled position: row r at r * 128, 16-byte chunk
 // (col / 8) XOR (r mod 8).
-constexpr int G5_PD = 8;  // K steps between a code load and its use
-
+//
+// The codes and scales reach shared memory by bulk asynchronous copies, not
+// by loads of the dequantizing threads: every step ends with a release (the
+// async-proxy fence and the mbarrier arrive that hand the stage to the MMA),
+// and a release waits for the thread's own loads still in flight -- with
+// the weights loaded by the threads themselves, every step would wait one
+// HBM latency. Lane 0 of warp T streams tile T's codes through a ring of
+// RC chunks of CK steps (tile T's codes of consecutive K steps are
+// contiguous, 512 bytes a step, and so are its scale groups), each chunk
+// completing an mbarrier; the warp reads a step's word and scales with
+// shared loads.
 struct G5Frag {
   uint4 q;
   float s0, s1;
 };
 
-template <typename ST>
-__device__ __forceinline__ G5Frag g5_load(const G5Args& a, int n0, int kb, int kb_end, int tid) {
-  const int T = tid >> 5, L = tid & 31, g = L >> 2;
-  const int gt = (n0 >> 4) + T;
-  G5Frag f{make_uint4(0u, 0u, 0u, 0u), 0.f, 0.f};
-  if (gt < a.T16 && kb < kb_end) {
-    f.q = ldg_stream(a.codes + (((size_t)gt * a.P + kb) * 32 + L) * 16);
-    const uint8_t* sp = a.scales + (((size_t)gt * a.ng + (kb >> a.gsh)) * 8 + g) * 2 * sizeof(ST);
-    if constexpr (sizeof(ST) == 2) {
-      const __half2 h = *reinterpret_cast<const __half2*>(sp);
-      f.s0 = __low2float(h);
-      f.s1 = __high2float(h);
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(sp);
-      f.s0 = v.x;
-      f.s1 = v.y;
-    }
+// a chunk slot of CK steps: codes, then up to CK scale groups of 16 rows
+template <int CK>
+struct G5Ring {
+  static constexpr int CODE_BYTES = CK * 512;
+  static constexpr int SLOT = CODE_BYTES + CK * 16 * 4;
+};
+
+// chunk c (local) of this warp's tile: steps [c CK, min((c + 1) CK, KB)) of
+// the CTA's range starting at kb0, and the scale groups they use
+template <typename ST, int CK>
+__device__ __forceinline__ void g5_fetch(const G5Args& a, int gt, int kb0, int KB, int c, uint8_t* slot,
+                                         uint64_t* bar) {
+  const int p0 = c * CK, ns = min(CK, KB - p0);
+  const int g0 = (kb0 + p0) >> a.gsh, g1 = (kb0 + p0 + ns - 1) >> a.gsh;
+  const uint32_t cb = (uint32_t)ns * 512u, sb = (uint32_t)(g1 - g0 + 1) * 16u * (uint32_t)sizeof(ST);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the warp's reads of the slot come first
+  mbar_expect_tx(bar, cb + sb);
+  bulk_g2s(slot, a.codes + ((size_t)gt * a.P + kb0 + p0) * 512, cb, bar);
+  bulk_g2s(slot + G5Ring<CK>::CODE_BYTES, a.scales + ((size_t)gt * a.ng + g0) * 16 * sizeof(ST), sb, bar);
+}
+
+// local step p's fragment from its chunk slot
+template <typename ST, int CK>
+__device__ __forceinline__ G5Frag g5_read(const G5Args& a, const uint8_t* slot, int kb0, int p, int lane) {
+  const int g = lane >> 2, i = p % CK;
+  const int grp = ((kb0 + p) >> a.gsh) - ((kb0 + p - i) >> a.gsh);
+  G5Frag f;
+  f.q = *reinterpret_cast<const uint4*>(slot + i * 512 + lane * 16);
+  const uint8_t* sp = slot + G5Ring<CK>::CODE_BYTES + (grp * 8 + g) * 2 * sizeof(ST);
+  if constexpr (sizeof(ST) == 2) {
+    const __half2 h = *reinterpret_cast<const __half2*>(sp);
+    f.s0 = __low2float(h);
+    f.s1 = __high2float(h);
+  } else {
+    const float2 v = *reinterpret_cast<const float2*>(sp);
+    f.s0 = v.x;
+    f.s1 = v.y;
   }
   return f;
 }
@@ -232,41 +265,7 @@ __device__ __forceinline__ void g5_dequant(const G5Frag& fr, uint8_t* As, int ti
                    : "memory");
     }
   }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor pipe
 }
-
-// the register queue over K steps [begin, end): local step p in slot p % G5_PD
-template <typename ST>
-struct G5Queue {
-  G5Frag e[G5_PD];
-  int begin, end;
-  __device__ __forceinline__ void init(const G5Args& a, int n0, int begin_, int end_, int tid) {
-    begin = begin_;
-    end = end_;
-#pragma unroll
-    for (int i = 0; i < G5_PD; ++i) e[i] = g5_load<ST>(a, n0, begin + i, end, tid);
-  }
-  template <int SLOT>
-  __device__ __forceinline__ void pop_at(const G5Args& a, uint8_t* As, int n0, int tid, int p) {
-    g5_dequant(e[SLOT], As, tid);
-    e[SLOT] = g5_load<ST>(a, n0, begin + p + G5_PD, end, tid);
-  }
-  // dequantize local step p (steps are popped in order) into As and load
-  // step p + G5_PD into its slot
-  __device__ __forceinline__ void pop(const G5Args& a, uint8_t* As, int n0, int tid, int p) {
-    static_assert(G5_PD == 8, "one case per slot");
-    switch (p & (G5_PD - 1)) {
-      case 0: pop_at<0>(a, As, n0, tid, p); break;
-      case 1: pop_at<1>(a, As, n0, tid, p); break;
-      case 2: pop_at<2>(a, As, n0, tid, p); break;
-      case 3: pop_at<3>(a, As, n0, tid, p); break;
-      case 4: pop_at<4>(a, As, n0, tid, p); break;
-      case 5: pop_at<5>(a, As, n0, tid, p); break;
-      case 6: pop_at<6>(a, As, n0, tid, p); break;
-      default: pop_at<7>(a, As, n0, tid, p); break;
-    }
-  }
-};
 
 // RoPE pair permutation of the fused q/k/v weight: row 2p + e of a head is
 // the original row p + e * hd / 2
@@ -298,14 +297,21 @@ __device__ __forceinline__ void g5_emit(const G5Args& a, int row, int mb, const 
   }
 }
 
-// One CTA: 8 dequantizing warps (warp T rebuilds 16-row tile T of each K
-// step into the weight stage, then runs the epilogue) and a control warp
-// whose lane 0 moves the activation tiles by TMA and issues the MMAs. The
-// two sides meet only at mbarriers: full_a (the 8 warps wrote a weight
-// stage), full_b (an activation stage landed), empty_a / empty_b (the MMAs
-// of a step finished reading its stages, tcgen05.commit), accum (every MMA
-// done). No CTA-wide barrier sits in the K loop, so every warp runs ahead
-// as far as its stages allow.
+// One CTA, three roles that meet only at mbarriers (no CTA-wide barrier in
+// the K loop, so every warp runs ahead as far as the stages allow):
+//  * warps 0-7 dequantize (warp T rebuilds 16-row tile T of each K step into
+//    the stage's weight tile) and later run the epilogue;
+//  * warp 8 owns the tensor memory, and its lane 0 issues the MMAs: one wait
+//    on the stage's `full` barrier, four tcgen05.mma, one tcgen05.commit to
+//    the stage's `empty` barrier per K step;
+//  * warp 9's lane 0 moves the activation tiles (and, DENSE, the weight
+//    tiles) by TMA, counting their bytes on the same `full` barrier.
+// A stage is [weight tile | activation tile]. `tiles` completes when the
+// stage's TMA bytes landed; warp 0 waits for it before it arrives on `full`,
+// which completes when the 8 dequantizing warps arrived; `empty` completes
+// when the step's MMAs have read the stage. Each mbarrier wait costs a couple
+// of hundred cycles even when its phase is already complete, so the MMA
+// thread, which sets the pace, waits once per step (DENSE: on `tiles`).
 //
 // DENSE: the weight is an fp16 matrix (the LM head) whose 128 x 64 tiles
 // arrive by TMA (tensor map tmw, same swizzle) instead of being rebuilt from
@@ -315,16 +321,16 @@ __global__ void __launch_bounds__(G5_THREADS, 1)
 gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, G5Args a) {
   static_assert(2 * BN <= 256, "hi and lo planes form one MMA of N = 2 BN <= 256");
   using C = G5Cfg<BN>;
-  constexpr int SA = G5_SA, SB = C::SB;
+  constexpr int S = C::S;
   constexpr uint32_t IDESC = idesc_f16(G5_BM, 2 * BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* Bst = smem + SA * G5_A_BYTES;                                  // activation stages
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(Bst + SB * C::B_BYTES);  // weight stage written / landed
-  uint64_t* empty_a = full_a + SA;                                        // weight stage read by its MMAs
-  uint64_t* full_b = empty_a + SA;                                        // activation stage landed
-  uint64_t* empty_b = full_b + SB;                                        // activation stage read
-  uint64_t* accum = empty_b + SB;                                         // every MMA done
+  uint8_t* Ring = smem + S * C::STAGE;                                  // code rings, RC slots per warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(Ring + C::RING_BYTES);   // weight tile written (8 warps)
+  uint64_t* tiles = full + S;                                           // the stage's TMA bytes landed
+  uint64_t* empty = tiles + S;                                          // stage read by its MMAs
+  uint64_t* accum = empty + S;                                          // every MMA done
+  uint64_t* chunk = accum + 1;                                          // code chunk landed, RC per warp
   __shared__ uint32_t tmem_base;
   __shared__ int abort_s, last_s;
 
@@ -335,19 +341,17 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   const int kb0 = (int)((long long)a.P * z / a.ks), KB = (int)((long long)a.P * (z + 1) / a.ks) - kb0;
 
   if (tid == 0) {
-    for (int i = 0; i < SA; ++i) {
-      mbar_init(&full_a[i], DENSE ? 1 : G5_DEQ_WARPS);
-      mbar_init(&empty_a[i], 1);
-    }
-    for (int i = 0; i < SB; ++i) {
-      mbar_init(&full_b[i], 1);
-      mbar_init(&empty_b[i], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], G5_DEQ_WARPS);
+      mbar_init(&tiles[i], 1);
+      mbar_init(&empty[i], 1);
     }
     mbar_init(accum, 1);
+    for (int i = 0; i < G5_DEQ_WARPS * C::RC; ++i) mbar_init(&chunk[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_s = 0;
   }
-  if (warp == G5_DEQ_WARPS) {
+  if (warp == G5_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                  "r"(2 * BN)
                  : "memory");
@@ -360,18 +364,58 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   pdl_launch_dependents();
   volatile int* abort_v = &abort_s;
 
+  const int NS = (KB + G5_KS - 1) / G5_KS;  // stages (the last may hold one step)
   if (warp < G5_DEQ_WARPS) {
     // ---- dequantizing warps: weights never depend on the previous kernel,
     // so they stream from the first instruction
     if constexpr (!DENSE) {
-      G5Queue<ST> wq;
-      wq.init(a, n0, kb0, kb0 + KB, tid);
+      constexpr int RC = C::RC, CK = C::CK;
+      uint8_t* ring = Ring + warp * RC * C::RING_SLOT;
+      uint64_t* cbar = chunk + warp * RC;
+      const int gt = (n0 >> 4) + warp;  // this warp's 16-row tile
+      const bool have = gt < a.T16;     // tiles past the weight dequantize zeros
+      const int NC = (KB + CK - 1) / CK;
+      int issued = 0, landed = 0;  // chunks requested (lane 0) / seen complete
+      if (have && lane == 0)
+        for (; issued < RC && issued < NC; ++issued)
+          g5_fetch<ST, CK>(a, gt, kb0, KB, issued, ring + issued * C::RING_SLOT, &cbar[issued]);
       for (int p = 0; p < KB; ++p) {
-        const int s = p % SA;
-        if (p >= SA) {
-          // the stage's previous step (p - SA) must have been read by its MMAs
-          const bool freed = mbar_wait_bounded(&empty_a[s], (uint32_t)((p / SA - 1) & 1), a.spin);
-          if (!__all_sync(0xffffffffu, freed)) {
+        const int q = p / G5_KS, sub = p % G5_KS, s = q % S, c = p / CK, i = p % CK;
+        const uint8_t* slot = ring + (c % RC) * C::RING_SLOT;
+        if (sub == 0 && q >= S) {
+          // the stage's previous occupant (stage q - S) must have been read by its MMAs
+          if (!mbar_wait_warp(&empty[s], (uint32_t)((q / S - 1) & 1), a.spin, lane)) {
+            if (lane == 0) {
+              atomicOr(a.fault, 8);
+              *abort_v = 1;
+            }
+            break;
+          }
+          if (*abort_v) break;
+        }
+        G5Frag fr{make_uint4(0u, 0u, 0u, 0u), 0.f, 0.f};
+        if (have) {
+          if (i == 0) {
+            if (!mbar_wait_warp(&cbar[c % RC], (uint32_t)((c / RC) & 1), a.spin, lane)) {
+              if (lane == 0) {
+                atomicOr(a.fault, 8);
+                *abort_v = 1;
+              }
+              break;
+            }
+            landed = c + 1;
+          }
+          fr = g5_read<ST, CK>(a, slot, kb0, p, lane);
+        }
+        g5_dequant(fr, smem + s * C::STAGE + sub * G5_A_BYTES, tid);
+        const bool stage_done = sub == G5_KS - 1 || p == KB - 1;
+        const bool chunk_end = have && (i == CK - 1 || p == KB - 1);
+        if (!stage_done && !chunk_end) continue;  // nothing to hand over after this step
+        // the stage's weight tiles become visible to the tensor pipe
+        if (stage_done) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (stage_done && warp == 0) {
+          // the stage's activation tiles must have landed before `full`
+          if (!mbar_wait_warp(&tiles[s], (uint32_t)((q / S) & 1), a.spin, lane)) {
             if (lane == 0) {
               atomicOr(a.fault, 8);
               *abort_v = 1;
@@ -379,84 +423,78 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
             break;
           }
         }
-        if (*abort_v) break;
-        wq.pop(a, smem + s * G5_A_BYTES, n0, tid, p);  // ends with the async-proxy fence
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
-      }
-    }
-  } else if (lane == 0) {
-    // ---- control thread: activation (and, DENSE, weight) tiles by TMA, MMAs
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
-    int a_issued = 0, a_landed = 0, b_issued = 0, b_landed = 0;
-    if constexpr (DENSE) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
-      for (int p = 0; p < SA && p < KB; ++p, ++a_issued) {
-        mbar_expect_tx(&full_a[p], G5_A_BYTES);
-        tma_load_2d(smem + p * G5_A_BYTES, &tmw, (kb0 + p) * G5_BK, n0, &full_a[p]);
-      }
-    }
-    pdl_wait();  // the activation rows come from the previous kernel
-    for (int p = 0; p < SB && p < KB; ++p, ++b_issued) {
-      mbar_expect_tx(&full_b[p], C::B_BYTES);
-      tma_load_3d(Bst + p * C::B_BYTES, &tmx, (kb0 + p) * G5_BK, m0, &full_b[p]);
-    }
-    for (int p = 0; p < KB; ++p) {
-      const int sa = p % SA, sb = p % SB;
-      bool ok = mbar_wait_bounded(&full_a[sa], (uint32_t)((p / SA) & 1), a.spin);
-      if (ok && DENSE) ++a_landed;
-      ok = ok && mbar_wait_bounded(&full_b[sb], (uint32_t)((p / SB) & 1), a.spin);
-      if (ok) ++b_landed;
-      if (!ok || *abort_v) {
-        if (!ok) atomicOr(a.fault, 8);
-        *abort_v = 1;
-        break;
-      }
-      tc05_fence_after();
-      const uint32_t sa_addr = smem_u32(smem + sa * G5_A_BYTES), sb_addr = smem_u32(Bst + sb * C::B_BYTES);
-#pragma unroll
-      for (int kk = 0; kk < G5_BK / 16; ++kk)
-        tc05_mma(tmem, smem_desc_sw128(sa_addr + kk * 32), smem_desc_sw128(sb_addr + kk * 32), IDESC, (p | kk) != 0);
-      tc05_commit(&empty_a[sa]);
-      tc05_commit(&empty_b[sb]);
-      // refill the stages of step p - 1 (its MMAs were issued one step ago)
-      // with step p - 1 + SB (activations) and, DENSE, p - 1 + SA (weights)
-      if (p >= 1) {
-        const int q = p - 1;
-        const bool nb = q + SB < KB, na = DENSE && q + SA < KB;
-        if (nb || na) {
-          bool freed = true;
-          if (nb) freed = mbar_wait_bounded(&empty_b[q % SB], (uint32_t)((q / SB) & 1), a.spin);
-          if (freed && na) freed = mbar_wait_bounded(&empty_a[q % SA], (uint32_t)((q / SA) & 1), a.spin);
-          if (!freed) {
-            atomicOr(a.fault, 8);
-            *abort_v = 1;
-            break;
-          }
-          if (nb) {
-            mbar_expect_tx(&full_b[q % SB], C::B_BYTES);
-            tma_load_3d(Bst + (q % SB) * C::B_BYTES, &tmx, (kb0 + q + SB) * G5_BK, m0, &full_b[q % SB]);
-            ++b_issued;
-          }
-          if (na) {
-            mbar_expect_tx(&full_a[q % SA], G5_A_BYTES);
-            tma_load_2d(smem + (q % SA) * G5_A_BYTES, &tmw, (kb0 + q + SA) * G5_BK, n0, &full_a[q % SA]);
-            ++a_issued;
+        if (lane == 0) {
+          if (stage_done) mbar_arrive(&full[s]);
+          // the chunk's last step is read: its slot takes chunk c + RC
+          if (chunk_end && issued < NC) {
+            g5_fetch<ST, CK>(a, gt, kb0, KB, issued, ring + (issued % RC) * C::RING_SLOT, &cbar[issued % RC]);
+            ++issued;
           }
         }
       }
+      // a warp that stopped early lets its chunk copies in flight land first
+      if (have && lane == 0)
+        for (int c = landed; c < issued; ++c) mbar_wait_bounded(&cbar[c % RC], (uint32_t)((c / RC) & 1));
     }
-    if (*abort_v) {
-      // let every tile load in flight land before the stages go away
-      for (int i = b_landed; i < b_issued; ++i) mbar_wait_bounded(&full_b[i % SB], (uint32_t)((i / SB) & 1));
-      for (int i = a_landed; i < a_issued; ++i) mbar_wait_bounded(&full_a[i % SA], (uint32_t)((i / SA) & 1));
+  } else if (warp == G5_MMA_WARP) {
+    // ---- MMA thread: one wait and one commit per stage of G5_KS steps
+    if (lane == 0) {
+      for (int q = 0; q < NS; ++q) {
+        const int s = q % S;
+        if (!mbar_wait_bounded(DENSE ? &tiles[s] : &full[s], (uint32_t)((q / S) & 1), a.spin) || *abort_v) {
+          if (!*abort_v) atomicOr(a.fault, 8);
+          *abort_v = 1;
+          break;
+        }
+        tc05_fence_after();
+        const uint32_t st = smem_u32(smem + s * C::STAGE);
+        const int nsub = min(G5_KS, KB - q * G5_KS);
+        for (int sub = 0; sub < nsub; ++sub) {
+          const uint32_t sa = st + sub * G5_A_BYTES, sb = st + G5_KS * G5_A_BYTES + sub * C::B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < G5_BK / 16; ++kk)
+            tc05_mma(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), IDESC,
+                     (q | sub | kk) != 0);
+        }
+        tc05_commit(&empty[s]);
+      }
+      tc05_commit(accum);  // completes once every MMA issued above is done
     }
-    tc05_commit(accum);  // completes once every MMA issued above is done
+  } else if (lane == 0) {
+    // ---- TMA thread: a stage is refilled once the MMAs of its previous
+    // occupant are done; the bytes count on the stage's `tiles` barrier
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+    if (DENSE) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
+    pdl_wait();  // the activation rows come from the previous kernel
+    int issued = 0;
+    for (; issued < NS; ++issued) {
+      const int s = issued % S;
+      if (issued >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((issued / S - 1) & 1), a.spin)) {
+        atomicOr(a.fault, 8);
+        *abort_v = 1;
+        break;
+      }
+      if (*abort_v) break;
+      uint8_t* st = smem + s * C::STAGE;
+      const int k0 = kb0 + issued * G5_KS, nsub = min(G5_KS, KB - issued * G5_KS);
+      mbar_expect_tx(&tiles[s], (uint32_t)nsub * (C::B_BYTES + (DENSE ? G5_A_BYTES : 0)));
+      for (int sub = 0; sub < nsub; ++sub) {
+        tma_load_3d(st + G5_KS * G5_A_BYTES + sub * C::B_BYTES, &tmx, (k0 + sub) * G5_BK, m0, &tiles[s]);
+        if (DENSE) tma_load_2d(st + sub * G5_A_BYTES, &tmw, (k0 + sub) * G5_BK, n0, &tiles[s]);
+      }
+    }
+    // an aborted CTA lets the loads in flight land before the stages go away
+    // (`tiles` phases complete on the bytes alone; older phases completed
+    // before their stage was refilled)
+    if (*abort_v)
+      for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+        mbar_wait_bounded(&tiles[i % S], (uint32_t)((i / S) & 1));
   }
 
   if (warp < G5_DEQ_WARPS) {
     // ---- epilogue (the 8 warps; named barrier 1 spans them only)
-    const bool done = mbar_wait_bounded(accum, 0u, MBAR_SPIN_LIMIT);
+    const bool done = mbar_wait_warp(accum, 0u, MBAR_SPIN_LIMIT, lane);
     tc05_fence_after();
     pdl_wait();  // outputs and residual rows may belong to earlier kernels
     if (!done && lane == 0) atomicOr(a.fault, 8);
@@ -525,7 +563,7 @@ gemm_tc05_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   }
   tc05_fence_before();
   __syncthreads();
-  if (warp == G5_DEQ_WARPS) {
+  if (warp == G5_MMA_WARP) {
     // no MMA may still write the accumulator when it is freed (the epilogue's
     // wait can only have given up on a failed CTA)
     if (lane == 0) mbar_wait_bounded(accum, 0u, MBAR_SPIN_LIMIT);

@@ -369,6 +369,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+// a whole warp waits for a phase: lane 0 polls and the others wait at the
+// shuffle (32 lanes polling one mbarrier word serialize in the shared-memory
+// pipe and take issue slots from the warps that have work)
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, long long limit, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait_bounded(bar, parity, limit) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
 // global -> shared bulk copy (bytes % 16 == 0, both addresses 16-byte aligned)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -685,8 +693,7 @@ gemv_fused_kernel(FusedArgs fa) {
     cx.issue(st + S - 1);  // refill the stage consumed last step
     if (it == 0) {
       if (lane == 0 && k + 1 < my_tasks) cx.issue_scales(k + 1);
-      const bool landed = mbar_wait_bounded(&bars[k & 1], (uint32_t)((k >> 1) & 1), fa.spin);
-      if (!__all_sync(0xffffffffu, landed)) {
+      if (!mbar_wait_warp(&bars[k & 1], (uint32_t)((k >> 1) & 1), fa.spin, lane)) {
         failed = k;
         break;
       }

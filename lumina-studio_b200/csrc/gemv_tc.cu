@@ -297,8 +297,7 @@ gemv_tc_kernel(TcArgs a) {
   }
   for (int j = 0; j < n_mine; ++j) {
     const int p0 = ku * KS, np = min(P - p0, KS);
-    const bool landed = mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1), a.spin);
-    if (!__all_sync(0xffffffffu, landed)) {
+    if (!mbar_wait_warp(&bars[j % TS], (uint32_t)((j / TS) & 1), a.spin, lane)) {
       failed = j;
       break;
     }
