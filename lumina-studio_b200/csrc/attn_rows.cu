@@ -36,6 +36,7 @@ constexpr int AR_BR = 64;   // query rows per CTA
 constexpr int AR_BC = 64;   // keys per tile
 constexpr int AR_THREADS = 128;
 constexpr int AR_MIN_SPLIT_TILES = 4;  // key tiles per CTA when the keys are split
+constexpr int AR_CTAS_PER_SM = 2;      // resident CTAs per SM (registers, shared memory)
 
 template <int HD>
 struct ArCfg {
@@ -84,7 +85,7 @@ __device__ __forceinline__ uint32_t pack_hl(float a, float b, uint32_t& lo) {
 }
 
 template <int HD, typename KT>
-__global__ void __launch_bounds__(AR_THREADS)
+__global__ void __launch_bounds__(AR_THREADS, AR_CTAS_PER_SM)
 attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
                  const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
                  const int* __restrict__ row_pos, const float* __restrict__ bias, const DevParams* __restrict__ P,
@@ -434,13 +435,14 @@ int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc,
   const size_t smem = bias ? ArCfg<HD>::SMEM_BIAS : ArCfg<HD>::SMEM_NOBIAS;
   const int rc = set_smem_limit((const void*)kern, smem, "attention (rows)");
   if (rc) return rc;
-  // key splits while heads x row blocks leave SMs idle: at least
-  // AR_MIN_SPLIT_TILES key tiles per CTA, the states within the workspace
+  // key splits while heads x row blocks leave SMs idle: as many as one wave
+  // of CTAs holds (AR_CTAS_PER_SM per SM), at least AR_MIN_SPLIT_TILES key
+  // tiles per CTA, the states within the workspace
   const int rb = (max_n + AR_BR - 1) / AR_BR, tiles = nh * rb;
   const int nkt = (t_tot + AR_BC - 1) / AR_BC;
   int ks = 1;
   if (sw && sw->ws && sw->cnt && tiles < sm_count() && tiles <= sw->cnt_n) {
-    ks = std::min((2 * sm_count() + tiles - 1) / tiles, nkt / AR_MIN_SPLIT_TILES);
+    ks = std::min(AR_CTAS_PER_SM * sm_count() / tiles, nkt / AR_MIN_SPLIT_TILES);
     while (ks > 1 && (size_t)ks * max_n * nh * (HD + 2) > sw->ws_elems) --ks;
     ks = std::max(ks, 1);
   }

@@ -82,7 +82,22 @@ struct TcArgs {
   int* fault;
   long long spin;  // polls before a wait on a ring stage gives up (wait_spin_limit())
   L2Prefetch pf;   // the next kernel's bytes, pulled into L2 while this one runs
+  TcTp tp;         // a fused tensor-parallel exchange (tp.tp == 0: none)
 };
+
+__device__ __forceinline__ unsigned long long tc_global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned tc_ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void tc_st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 template <typename ST>
 __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, float& s1) {
@@ -116,7 +131,12 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0,
       if (row < a.rows) {
         float v = h ? v1 : v0;
         if constexpr (EPI == EPI_RESID) v = ep_s[t * (a.MT * 16) + (row - res0)] + v;
-        a.y[(size_t)t * a.ldy + row] = v;
+        if (EPI == EPI_STORE && a.tp.push[0]) {
+          // every rank's receive slot for this rank (peer stores over NVLink)
+          for (int r = 0; r < a.tp.tp; ++r) a.tp.push[r][(size_t)t * a.tp.ld + row] = v;
+        } else {
+          a.y[(size_t)t * a.ldy + row] = v;
+        }
       }
     }
   } else {
@@ -281,7 +301,32 @@ gemv_tc_kernel(TcArgs a) {
     }
     cp_async_commit();
   }
-  tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red);
+  TqSum sum;
+  if (a.tp.in_flags) {
+    // every rank's rows of this exchange have landed once its flag holds the
+    // epoch this rank's own producer (the kernel waited for above) set
+    __shared__ int tp_ok;
+    if (threadIdx.x == 0) {
+      const unsigned ep = *reinterpret_cast<volatile const unsigned*>(a.tp.epoch);
+      const unsigned long long t0 = tc_global_ns();
+      int ok = 1;
+      for (int r = 0; r < a.tp.tp && ok; ++r)
+        while ((int)(tc_ld_acquire_sys(a.tp.in_flags + r) - ep) < 0)
+          if (tc_global_ns() - t0 >= a.tp.timeout_ns) {
+            atomicOr(a.fault, 4);
+            ok = 0;
+            break;
+          }
+      tp_ok = ok;
+    }
+    __syncthreads();
+    if (tp_ok) {
+      sum.add = a.tp.add;
+      sum.n_add = a.tp.tp;
+      sum.xout = a.tp.xout;
+    }
+  }
+  tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, sum);
   if constexpr (EPI == EPI_RESID) cp_async_wait<0>();
   __syncthreads();
 
@@ -391,6 +436,23 @@ gemv_tc_kernel(TcArgs a) {
     }
     __syncwarp();
   }
+  if (EPI == EPI_STORE && a.tp.push[0]) {
+    // the exchange is published once every CTA's rows are out: the last CTA
+    // to take a ticket (every CTA takes one, a failed one too, so the
+    // counter returns to zero) advances the epoch and flags every rank
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int tk = atomicAdd(a.tp.ticket, 1);
+      if (tk == (int)gridDim.x - 1) {
+        *a.tp.ticket = 0;
+        __threadfence_system();
+        const unsigned ep = *a.tp.epoch + 1u;
+        *a.tp.epoch = ep;
+        for (int r = 0; r < a.tp.tp; ++r) tc_st_release_sys(a.tp.flags[r], ep);
+      }
+    }
+  }
 }
 
 template <int NB, typename ST, int EPI, bool NORM, int KS>
@@ -438,7 +500,7 @@ int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bo
 
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
-                   const L2Prefetch* pf) {
+                   const L2Prefetch* pf, const TcTp* tp) {
   if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
@@ -474,6 +536,14 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   a.fault = fault;
   a.spin = wait_spin_limit();
   if (pf) a.pf = *pf;
+  if (tp && tp->tp > 1) {
+    const bool producer = tp->push[0] != nullptr, consumer = tp->in_flags != nullptr;
+    if (producer == consumer || (producer && epi != EPI_STORE) || (consumer && !norm_w) || tp->tp > TCTP_MAX) {
+      set_error("gemv_tc: a fused exchange needs a storing producer or a normalizing consumer");
+      return LUMINA_E_ARG;
+    }
+    a.tp = *tp;
+  }
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
   const int per = (a.T16 + sm_count() - 1) / sm_count();

@@ -89,6 +89,17 @@ struct lumina_model {
   char* peer_exch[PEER_MAX] = {};
   unsigned* peer_epoch = nullptr;  // PEER_CTAS exchange counters
   bool peers_ready = false;
+  // the decode step's exchanges fused into its GEMVs (TcTp): per kind (0:
+  // o_proj, 1: down_proj) every rank owns receive slots [kind][source rank]
+  // of TP_PUSH_ROWS rows behind the three exchange slots and flags
+  // [kind][source rank] at TP_PUSH_FLAGS in the flag page; the residual
+  // alternates between xa (after the attention sum) and xb (after the MLP
+  // sum) because a consumer's CTAs read one while CTA 0 writes the other
+  bool tp_fusable = false;   // every layer's projections run on gemv_tc
+  bool tp_fuse_now = false;  // set while the decode graphs are captured
+  unsigned* tp_epoch = nullptr;  // [2] exchanges published, per kind
+  int* tp_ticket = nullptr;      // [2] producer CTA tickets
+  float *xa = nullptr, *xb = nullptr;
   std::vector<void*> allocs;
 };
 
@@ -307,6 +318,49 @@ float* exch_slot_ptr(lumina_model* m, int slot) {
   return reinterpret_cast<float*>(m->exch + PEER_FLAG_BYTES) + (size_t)slot * m->exch_slot;
 }
 
+constexpr int TP_PUSH_ROWS = 4;        // decode rows of a fused exchange (gemv_tc batch)
+constexpr size_t TP_PUSH_FLAGS = 2048;  // byte offset of the push flags in the flag page
+static_assert(TCTP_MAX == PEER_MAX, "one receive slot per rank");
+static_assert(PEER_CTAS * PEER_MAX * 4 <= TP_PUSH_FLAGS && TP_PUSH_FLAGS + 2 * PEER_MAX * 4 <= PEER_FLAG_BYTES,
+              "flag page layout");
+
+// receive slot (kind, source rank src) in rank r's region, and its flag
+float* tp_push_slot(const lumina_model* m, int r, int kind, int src) {
+  float* base = reinterpret_cast<float*>(m->peer_exch[r] + PEER_FLAG_BYTES) + 3 * m->exch_slot;
+  return base + ((size_t)kind * PEER_MAX + src) * TP_PUSH_ROWS * m->d;
+}
+unsigned* tp_push_flag(const lumina_model* m, int r, int kind, int src) {
+  return reinterpret_cast<unsigned*>(m->peer_exch[r] + TP_PUSH_FLAGS) + kind * PEER_MAX + src;
+}
+unsigned long long tp_timeout_ns() { return wait_spin_limit() == 0 ? 0ull : 10000000000ull; }
+
+// this rank's producing side of exchange `kind`: rows to every rank's slot
+TcTp tp_producer(const lumina_model* m, int kind) {
+  TcTp t;
+  t.tp = m->c.tp_size;
+  t.ld = m->d;
+  for (int r = 0; r < t.tp; ++r) {
+    t.push[r] = tp_push_slot(m, r, kind, m->c.tp_rank);
+    t.flags[r] = tp_push_flag(m, r, kind, m->c.tp_rank);
+  }
+  t.ticket = m->tp_ticket + kind;
+  t.epoch = m->tp_epoch + kind;
+  t.timeout_ns = tp_timeout_ns();
+  return t;
+}
+// the consuming side: x + every rank's rows, the sum kept in xout
+TcTp tp_consumer(const lumina_model* m, int kind, float* xout) {
+  TcTp t;
+  t.tp = m->c.tp_size;
+  t.ld = m->d;
+  for (int r = 0; r < t.tp; ++r) t.add[r] = tp_push_slot(m, m->c.tp_rank, kind, r);
+  t.in_flags = tp_push_flag(m, m->c.tp_rank, kind, 0);
+  t.xout = xout;
+  t.epoch = m->tp_epoch + kind;
+  t.timeout_ns = tp_timeout_ns();
+  return t;
+}
+
 // Exchange slot `slot` (n floats, written by the previous kernel) with every
 // rank: PEER_SUM adds the ranks' sum into out, PEER_GATHER writes the ranks'
 // slots side by side to out.
@@ -351,7 +405,15 @@ constexpr int TC05_MIN_ROWS = 8;
 // flips at score gaps of 1e-4 .. 1e-3.
 int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, int n, const float* norm, float* y,
              int ldy, int epi, const float* resid, int ldr, const RopeKV* rk, const L2Prefetch* pf = nullptr,
-             bool exact_rows = false) {
+             bool exact_rows = false, const TcTp* tpx = nullptr) {
+  if (tpx) {
+    // a fused exchange has no other kernel to fall back to
+    const int rc = w->mma && n <= 4
+                       ? gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf, tpx)
+                       : LUMINA_E_UNSUPPORTED;
+    if (rc == LUMINA_E_UNSUPPORTED) set_error("fused exchange: projection not on the tensor-pipe GEMV");
+    return rc;
+  }
   if (w->mma) {
     if (n <= 4) {
       const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf);
@@ -408,6 +470,20 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   const int qw = nh * hd, kw = nkv * hd, width = qw + 2 * kw;
   cudaStream_t s = m->stream;
   const bool tp = m->c.tp_size > 1;
+  // decode rows with the exchanges fused into the GEMVs: the layer's input
+  // residual is x (layer 0) or xa plus every rank's down_proj rows of the
+  // layer before, and the attention sum builds on that in xb
+  const bool fused = tp && m->tp_fuse_now && n <= TP_PUSH_ROWS;
+  const bool last = l + 1 == m->c.n_layer;
+  const float* x_in = fused && l > 0 ? m->xa : m->x;  // the residual before this layer's sums
+  const float* x_mid = fused ? (l > 0 ? m->xb : m->x) : m->x;  // the residual gate/up adds the o_proj sum to
+  TcTp tp_qkv, tp_o, tp_gu, tp_down;
+  if (fused) {
+    if (l > 0) tp_qkv = tp_consumer(m, 1, m->xb);
+    tp_o = tp_producer(m, 0);
+    tp_gu = tp_consumer(m, 0, m->xa);
+    if (!last) tp_down = tp_producer(m, 1);
+  }
   L2Prefetch pf_kv;
   const unsigned kv_block_bytes = (unsigned)((size_t)nkv * m->c.block_size * hd * kv_es(m));
   if (kv_block_bytes % 16 == 0) {
@@ -439,9 +515,13 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
     rk.kv_fp16 = m->c.kv_fp16;
     rk.q_out = m->q_buf;
     rk.row_base = 0;
-    TRY(gemv_any(m, Ly.qkv, m->x, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, &pf_kv,
-                 Ly.moe_e > 0));
+    TRY(gemv_any(m, Ly.qkv, x_in, d, n, Ly.in_norm, nullptr, 0, EPI_ROPE_KV, nullptr, 0, &rk, &pf_kv,
+                 Ly.moe_e > 0, fused && l > 0 ? &tp_qkv : nullptr));
   } else {
+    if (fused) {
+      set_error("fused exchange: the layer has separate q/k/v projections");
+      return LUMINA_E_STATE;
+    }
     lumina_weight* ws[3] = {Ly.q, Ly.k, Ly.v};
     const int off[3] = {0, qw, qw + kw};
     for (int i = 0; i < 3; ++i)
@@ -459,7 +539,10 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
                               &m->split, s));
   }
   // 3) o_proj + residual (chat.py:282-283)
-  if (tp) {
+  if (fused) {
+    TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, exch_slot_ptr(m, 0), d, EPI_STORE, nullptr, 0, nullptr, &pf_mlp,
+                 false, &tp_o));
+  } else if (tp) {
     TRY(gemv_any(m, Ly.o, m->attn, qw, n, nullptr, exch_slot_ptr(m, 0), d, EPI_STORE, nullptr, 0, nullptr, &pf_mlp));
     TRY(peer_exchange(m, 0, PEER_SUM, (size_t)n * d, m->x));
   } else {
@@ -473,17 +556,26 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
-    TRY(gemv_any(m, Ly.gu, m->x, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr,
-                 &pf_down));
+    TRY(gemv_any(m, Ly.gu, x_mid, d, n, Ly.post_norm, m->ffn_buf, m->ffn, EPI_SWIGLU, nullptr, 0, nullptr,
+                 &pf_down, false, fused ? &tp_gu : nullptr));
   } else {
+    if (fused) {
+      set_error("fused exchange: the layer has separate gate/up projections");
+      return LUMINA_E_STATE;
+    }
     TRY(gemv_any(m, Ly.gate, m->x, d, n, Ly.post_norm, m->g_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(gemv_any(m, Ly.up, m->x, d, n, Ly.post_norm, m->u_buf, m->ffn, EPI_STORE, nullptr, 0, nullptr));
     TRY(launch_swiglu(m->g_buf, m->u_buf, m->ffn_buf, n, m->ffn, m->ffn, s));
   }
-  if (tp) {
+  if (fused && !last) {
+    TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, exch_slot_ptr(m, 1), d, EPI_STORE, nullptr, 0, nullptr,
+                 &pf_next, false, &tp_down));
+  } else if (tp) {
+    // (a fused step's last layer: the exchange kernel adds the sum into xa,
+    // which the head reads)
     TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, exch_slot_ptr(m, 1), d, EPI_STORE, nullptr, 0, nullptr,
                  &pf_next));
-    TRY(peer_exchange(m, 1, PEER_SUM, (size_t)n * d, m->x));
+    TRY(peer_exchange(m, 1, PEER_SUM, (size_t)n * d, fused ? m->xa : m->x));
   } else {
     TRY(gemv_any(m, Ly.down, m->ffn_buf, m->ffn, n, nullptr, m->x, d, EPI_RESID, m->x, d, nullptr, &pf_next));
   }
@@ -495,6 +587,8 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
 // gather assembles [rank0 | rank1 | ...].
 int run_head(lumina_model* m, int first, int rows, unsigned long long* amax = nullptr) {
   const int V = m->head_rows;
+  // a fused decode step leaves its residual in xa
+  const float* xin = m->c.tp_size > 1 && m->tp_fuse_now && rows <= TP_PUSH_ROWS ? m->xa : m->x;
   // the next token's first GEMV (layer 0 q/k/v) into L2 meanwhile
   const L2Prefetch pf = prefetch_of(qkv_weight(m, 0));
   if (m->c.tp_size <= 1) {
@@ -510,7 +604,7 @@ int run_head(lumina_model* m, int first, int rows, unsigned long long* amax = nu
   }
   const int tp = m->c.tp_size;
   for (int r = 0; r < rows; ++r) {
-    TRY(launch_dense_gemv(m->head, V, m->d, m->x + (size_t)(first + r) * m->d, m->d, 1, exch_slot_ptr(m, 2), V,
+    TRY(launch_dense_gemv(m->head, V, m->d, xin + (size_t)(first + r) * m->d, m->d, 1, exch_slot_ptr(m, 2), V,
                           nullptr, 0, m->stream, nullptr, r == 0 ? &pf : nullptr));
     TRY(peer_exchange(m, 2, PEER_GATHER, (size_t)V, m->logits + (size_t)r * V * tp));
   }
@@ -630,9 +724,18 @@ int forward_rows(lumina_model* m, const int* tokens, int n, int pos0, const int*
   return finish_checked(m, "forward");
 }
 
+// while a decode graph is captured, its tensor-parallel exchanges are fused
+// into the GEMVs (when every projection allows it)
+struct FuseExchanges {
+  lumina_model* m;
+  explicit FuseExchanges(lumina_model* mm) : m(mm) { m->tp_fuse_now = m->c.tp_size > 1 && m->tp_fusable; }
+  ~FuseExchanges() { m->tp_fuse_now = false; }
+};
+
 int capture_step(lumina_model* m) {
   cudaStream_t s = m->stream;
   cudaGraph_t g = nullptr;
+  FuseExchanges fuse(m);
   LUMINA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = LUMINA_OK;
   const int V = m->head_rows * std::max(1, m->c.tp_size);
@@ -699,6 +802,7 @@ __global__ void greedy_commit_kernel(const unsigned long long* key, const int* a
 int capture_chain(lumina_model* m) {
   cudaStream_t s = m->stream;
   cudaGraph_t g = nullptr;
+  FuseExchanges fuse(m);
   LUMINA_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = LUMINA_OK;
   const int V = m->head_rows * std::max(1, m->c.tp_size);
@@ -1051,10 +1155,18 @@ int lumina_model_finalize(lumina_model* m) {
     static_assert(PEER_CTAS * PEER_MAX * 4 <= PEER_FLAG_BYTES, "exchange flags");
     LUMINA_CHECK_ARG(c.tp_size <= PEER_MAX, "model_finalize: tp_size %d > %d", c.tp_size, PEER_MAX);
     m->exch_slot = (std::max((size_t)R * m->d, (size_t)m->head_rows) + 63) / 64 * 64;
-    TRY(dalloc(m, (void**)&m->exch, PEER_FLAG_BYTES + 3 * m->exch_slot * 4));
+    // [flags][slot 0..2][receive slots: 2 kinds x PEER_MAX ranks x TP_PUSH_ROWS rows]
+    const size_t push_floats = 2 * (size_t)PEER_MAX * TP_PUSH_ROWS * m->d;
+    TRY(dalloc(m, (void**)&m->exch, PEER_FLAG_BYTES + (3 * m->exch_slot + push_floats) * 4));
     LUMINA_CUDA_TRY(cudaMemset(m->exch, 0, PEER_FLAG_BYTES));
     TRY(dalloc(m, (void**)&m->peer_epoch, PEER_CTAS * 4));
     LUMINA_CUDA_TRY(cudaMemset(m->peer_epoch, 0, PEER_CTAS * 4));
+    TRY(dalloc(m, (void**)&m->tp_epoch, 2 * sizeof(unsigned)));
+    TRY(dalloc(m, (void**)&m->tp_ticket, 2 * sizeof(int)));
+    LUMINA_CUDA_TRY(cudaMemset(m->tp_epoch, 0, 2 * sizeof(unsigned)));
+    LUMINA_CUDA_TRY(cudaMemset(m->tp_ticket, 0, 2 * sizeof(int)));
+    TRY(dalloc(m, (void**)&m->xa, (size_t)TP_PUSH_ROWS * m->d * 4));
+    TRY(dalloc(m, (void**)&m->xb, (size_t)TP_PUSH_ROWS * m->d * 4));
   }
   if (any_moe) {
     TRY(moe_prepare(m->d));
@@ -1164,6 +1276,15 @@ int lumina_model_init_peers(lumina_model* m, const uint8_t* handles) {
     m->peer_exch[r] = static_cast<char*>(p);
   }
   m->peers_ready = true;
+  // the decode step fuses its exchanges when every projection it needs runs
+  // on the tensor-pipe GEMV (int4 fragment layout, fused q/k/v and gate/up)
+  m->tp_fusable = getenv("LUMINA_TP_EXCHANGE_KERNELS") == nullptr;
+  for (const Layer& Ly : m->L) {
+    const lumina_weight* ws[4] = {Ly.qkv, Ly.o, Ly.gu, Ly.down};
+    for (const lumina_weight* w : ws)
+      if (!w || !w->mma || w->bits != 4 || w->group % 64) m->tp_fusable = false;
+    if (Ly.moe_e) m->tp_fusable = false;
+  }
   return LUMINA_OK;
 }
 

@@ -23,6 +23,7 @@ namespace lumina {
 
 constexpr int TQ_QMAX = 32639;  // 256 * 127 + 127
 constexpr int TQ_CH = 4;        // items per thread per pass
+constexpr int TQ_MAX_ADD = 8;   // addend rows (tensor-parallel ranks)
 
 __device__ __forceinline__ void tq_load8(float (&v)[8], const float* p, int k0, int K, bool vec) {
   if (vec && k0 + 8 <= K) {
@@ -82,11 +83,35 @@ __device__ __forceinline__ void tq_rinv(float (&ss)[NB], float (&rinv)[NB], floa
   }
 }
 
+// the rows other GPUs wrote (a tensor-parallel sum): read through L2, never
+// from a stale L1 line
+__device__ __forceinline__ void tq_add8(float (&v)[8], const float* p, int k0, int K, bool vec) {
+  if (vec && k0 + 8 <= K) {
+    const float4 f0 = __ldcg(reinterpret_cast<const float4*>(p + k0));
+    const float4 f1 = __ldcg(reinterpret_cast<const float4*>(p + k0 + 4));
+    v[0] += f0.x; v[1] += f0.y; v[2] += f0.z; v[3] += f0.w;
+    v[4] += f1.x; v[5] += f1.y; v[6] += f1.z; v[7] += f1.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k0 + j < K) v[j] += __ldcg(p + k0 + j);
+  }
+}
+
+// the input rows: x, plus (n_add > 0) the rank-ordered sum of the add[]
+// rows; `xout` (may be null) receives them before any normalization
+struct TqSum {
+  const float* const* add = nullptr;
+  int n_add = 0;
+  float* xout = nullptr;
+};
+
 // NB rows (nb live, row stride ldx) -> xb [P][2 NB][4 lanes] uint4 and
 // fq [P][NB]; NW warps; the caller syncs the CTA before reading xb / fq
 template <int NB, int NW, bool NORM>
 __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, int P, const float* nw, float eps,
-                                       const float (&w)[TQ_CH][8], uint4* xb, int2* fq, float* red) {
+                                       const float (&w)[TQ_CH][8], uint4* xb, int2* fq, float* red,
+                                       const TqSum& sum = TqSum{}) {
   constexpr int NC = 2 * NB;
   const int n_items = NB * P * 8, per_pass = TQ_CH * (int)blockDim.x;
   const bool vec_x = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
@@ -102,7 +127,10 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
       ss[b] = 0.f;
       if (b < nb)
         for (int k = threadIdx.x; k < K; k += blockDim.x) {
-          const float v = x[(size_t)b * ldx + k];
+          float v = x[(size_t)b * ldx + k];
+#pragma unroll
+          for (int r = 0; r < TQ_MAX_ADD; ++r)
+            if (r < sum.n_add) v += __ldcg(sum.add[r] + (size_t)b * ldx + k);
           ss[b] = fmaf(v, v, ss[b]);
         }
     }
@@ -120,6 +148,29 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
       if (i < n_items && b < nb) tq_load8(v[u], x + (size_t)b * ldx, k0, K, vec_x);
+    }
+    if (sum.n_add > 0) {
+      // x + rank 0 + rank 1 + ... (the same order on every rank)
+#pragma unroll
+      for (int r = 0; r < TQ_MAX_ADD; ++r) {
+        if (r >= sum.n_add) break;
+#pragma unroll
+        for (int u = 0; u < TQ_CH; ++u) {
+          const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+          if (i < n_items && row[u] < nb) tq_add8(v[u], sum.add[r] + (size_t)row[u] * ldx, (i % (P * 8)) * 8, K, vec_x);
+        }
+      }
+      if (sum.xout && blockIdx.x == 0) {
+#pragma unroll
+        for (int u = 0; u < TQ_CH; ++u) {
+          const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+          const int k0 = (i % (P * 8)) * 8;
+          if (i < n_items && row[u] < nb)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (k0 + j < K) sum.xout[(size_t)row[u] * ldx + k0 + j] = v[u][j];
+        }
+      }
     }
     if constexpr (NORM) {
       if (one_pass) {

@@ -168,13 +168,38 @@ int gemv_mma_launch(const lumina_weight* w, const float* x, int ldx, int batch, 
                     float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s,
                     const RopeKV* rk = nullptr);
 
+// The tensor-parallel sum of a row-parallel projection fused into the decode
+// GEMVs on both sides of it (no exchange kernel in between). The producer
+// (EPI_STORE) writes its rows into every rank's receive slot for this rank
+// (push[r], peer memory over NVLink), and its last CTA (ticket) advances
+// this rank's epoch of the exchange and release-stores it into every rank's
+// flag for this rank (flags[r]). The consumer (a NORM prologue) reads the
+// epoch its own producer set, waits until in_flags[r] holds it for every
+// rank r (bounded by timeout_ns), reads x + sum over r of add[r] (rank
+// order: every rank computes the same bits), and CTA 0 stores that sum in
+// xout, the residual the next exchange builds on.
+constexpr int TCTP_MAX = 8;
+struct TcTp {
+  int tp = 0;  // ranks; 0: not part of an exchange
+  int ld = 0;  // floats per row in the slots
+  float* push[TCTP_MAX] = {};
+  unsigned* flags[TCTP_MAX] = {};
+  int* ticket = nullptr;
+  const float* add[TCTP_MAX] = {};
+  const unsigned* in_flags = nullptr;
+  float* xout = nullptr;
+  unsigned* epoch = nullptr;
+  unsigned long long timeout_ns = 0;
+};
+
 // int4 decode GEMV on the tensor pipe (gemv_tc.cu), batch 1, 2 or 4 (3 runs
 // as 4), weights in the fragment layout with group = 64 * 2^k.
 // LUMINA_E_UNSUPPORTED when the shape does not fit.
 // `pf` (may be null): the next kernel's bytes to pull into L2 meanwhile.
+// `tp` (may be null): this GEMV's side of a fused tensor-parallel exchange.
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
-                   const L2Prefetch* pf = nullptr);
+                   const L2Prefetch* pf = nullptr, const TcTp* tp = nullptr);
 
 // Workspace of a kernel whose grid splits its reduction (K of a projection,
 // the keys of an attention row block) over several CTAs: partial results go

@@ -2,7 +2,10 @@
 model sharded over two ranks (heads, group-aligned FFN slices, vocab), the
 peer-memory sums after o_proj / down_proj and the logits gather, must
 reproduce the reference's recorded logits (2e-3 relative L2), the TP=1
-model's greedy tokens, and each rank's KV heads."""
+model's greedy tokens, and each rank's KV heads. The decode graphs fuse the
+exchanges into the GEMVs on either side (the producer pushes its rows into
+every rank's receive slot, the consumer sums them in its prologue); the same
+run with the exchanges as separate kernels must agree with them."""
 import os
 import socket
 import subprocess
@@ -91,3 +94,19 @@ def test_tp2_matches_reference_and_tp1(tiny_file, tmp_path):
         a, b = np.load(f"{out}.rank{k}.npz"), np.load(f"{out2}.rank{k}.npz")
         for key in a.files:
             assert np.array_equal(a[key], b[key]), (k, key)
+    # the decode steps' exchanges as separate peer-exchange kernels (the path
+    # prefill takes) give the same logits within the bar and the same tokens
+    # as the fused exchanges of the default decode graphs
+    out3 = str(tmp_path / "tp_kern")
+    env3 = dict(env, LUMINA_TP_EXCHANGE_KERNELS="1")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", f"--master-port={port + 2}",
+                        os.path.join(REPO, "tests", "tp_worker.py"), tiny_file, golden, out3],
+                       env=env3, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    for k in range(2):
+        a, c = np.load(f"{out}.rank{k}.npz"), np.load(f"{out3}.rank{k}.npz")
+        assert np.array_equal(a["prefill"], c["prefill"]), k
+        for s in range(4):
+            assert rel_l2(a[f"step{s}"], c[f"step{s}"]) < 1e-5, (k, s)
+        assert np.array_equal(a["greedy"], c["greedy"]), k
