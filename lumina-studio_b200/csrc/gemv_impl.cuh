@@ -1,6 +1,8 @@
 // Kernel templates of the packed GEMV, instantiated per bit width in
 // gemv_b1.cu .. gemv_b4.cu (see gemv.cu for the design notes).
 #pragma once
+#include <atomic>
+
 #include "weights.cuh"
 
 namespace lumina {
@@ -750,11 +752,20 @@ gemv_fused_kernel(FusedArgs fa) {
 template <int BITS, int R, int U, int NB, typename ST, int EPI>
 inline int launch_one(const GemvArgs& a, cudaStream_t s) {
   auto kern = gemv_kernel<BITS, R, U, NB, ST, EPI>;
-  static int per_sm = -1;
-  if (per_sm < 0) {
-    int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, GEMV_WARPS * 32, 0) != cudaSuccess || v < 1) v = 1;
-    per_sm = v;
+  // resident CTAs per SM, per device (atomics: racing host threads store
+  // the same value)
+  static std::atomic<int> per_sm_dev[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>& slot = per_sm_dev[dev >= 0 && dev < 64 ? dev : 0];
+  int per_sm = slot.load(std::memory_order_relaxed);
+  if (per_sm < 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_WARPS * 32, 0) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    slot.store(per_sm, std::memory_order_relaxed);
   }
   const int n_tasks = (a.w.rows + R - 1) / R;
   int grid = (n_tasks + GEMV_WARPS - 1) / GEMV_WARPS;

@@ -82,8 +82,17 @@ struct TcArgs {
   int* fault;
   long long spin;  // polls before a wait on a ring stage gives up (wait_spin_limit())
   L2Prefetch pf;   // the next kernel's bytes, pulled into L2 while this one runs
-  TcTp tp;         // a fused tensor-parallel exchange (tp.tp == 0: none)
 };
+
+// The fused tensor-parallel exchange of a launch, a kernel parameter of its
+// own so that the kernels outside an exchange (TPX false, every one-GPU
+// launch) carry neither its bytes nor its code.
+template <bool TPX>
+struct TpParam {
+  TcTp v;
+};
+template <>
+struct TpParam<false> {};
 
 __device__ __forceinline__ unsigned long long tc_global_ns() {
   unsigned long long t;
@@ -118,9 +127,10 @@ __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, flo
 // ep_s: the operands staged in shared memory by the prologue -- residual
 // rows [res0, res0 + MT*16) of each batch row (EPI_RESID), or the RoPE
 // cos / sin rows of each batch row's position (EPI_ROPE_KV).
-template <int NB, int EPI>
-__device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0, float v1, int lane,
-                                            const int* kv_blk, const int* kv_off, const float* ep_s, int res0) {
+template <int NB, int EPI, bool TPX>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, const TpParam<TPX>& tp, int row0, float v0, float v1,
+                                            int lane, const int* kv_blk, const int* kv_off, const float* ep_s,
+                                            int res0) {
   const int g = lane >> 2, t = lane & 3;
   const bool live = t < NB && t < a.nb;
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
@@ -131,9 +141,9 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0,
       if (row < a.rows) {
         float v = h ? v1 : v0;
         if constexpr (EPI == EPI_RESID) v = ep_s[t * (a.MT * 16) + (row - res0)] + v;
-        if (EPI == EPI_STORE && a.tp.push[0]) {
+        if constexpr (TPX && EPI == EPI_STORE) {
           // every rank's receive slot for this rank (peer stores over NVLink)
-          for (int r = 0; r < a.tp.tp; ++r) a.tp.push[r][(size_t)t * a.tp.ld + row] = v;
+          for (int r = 0; r < tp.v.tp; ++r) tp.v.push[r][(size_t)t * tp.v.ld + row] = v;
         } else {
           a.y[(size_t)t * a.ldy + row] = v;
         }
@@ -197,9 +207,9 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int row0, float v0,
   }
 }
 
-template <int NB, typename ST, int EPI, bool NORM, int KS>
+template <int NB, typename ST, int EPI, bool NORM, int KS, bool TPX>
 __global__ void __launch_bounds__(TW * 32, 1)
-gemv_tc_kernel(TcArgs a) {
+gemv_tc_kernel(TcArgs a, TpParam<TPX> tp) {
   constexpr int ES = sizeof(ST);
   constexpr int NC = 2 * NB;   // B columns: (high, low) bytes per batch row
   constexpr int SG = 16 * ES;  // scale bytes of one group of a tile: 8 x (row g, row g+8)
@@ -301,18 +311,17 @@ gemv_tc_kernel(TcArgs a) {
     }
     cp_async_commit();
   }
-  TqSum sum;
-  if (a.tp.in_flags) {
+  if constexpr (TPX && NORM) {
     // every rank's rows of this exchange have landed once its flag holds the
     // epoch this rank's own producer (the kernel waited for above) set
     __shared__ int tp_ok;
     if (threadIdx.x == 0) {
-      const unsigned ep = *reinterpret_cast<volatile const unsigned*>(a.tp.epoch);
+      const unsigned ep = *reinterpret_cast<volatile const unsigned*>(tp.v.epoch);
       const unsigned long long t0 = tc_global_ns();
       int ok = 1;
-      for (int r = 0; r < a.tp.tp && ok; ++r)
-        while ((int)(tc_ld_acquire_sys(a.tp.in_flags + r) - ep) < 0)
-          if (tc_global_ns() - t0 >= a.tp.timeout_ns) {
+      for (int r = 0; r < tp.v.tp && ok; ++r)
+        while ((int)(tc_ld_acquire_sys(tp.v.in_flags + r) - ep) < 0)
+          if (tc_global_ns() - t0 >= tp.v.timeout_ns) {
             atomicOr(a.fault, 4);
             ok = 0;
             break;
@@ -320,13 +329,17 @@ gemv_tc_kernel(TcArgs a) {
       tp_ok = ok;
     }
     __syncthreads();
+    TqSum sum;
     if (tp_ok) {
-      sum.add = a.tp.add;
-      sum.n_add = a.tp.tp;
-      sum.xout = a.tp.xout;
+#pragma unroll
+      for (int r = 0; r < TQ_MAX_ADD; ++r) sum.add[r] = r < tp.v.tp ? tp.v.add[r] : nullptr;
+      sum.n_add = tp.v.tp;
+      sum.xout = tp.v.xout;
     }
+    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, &sum);
+  } else {
+    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red);
   }
-  tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, sum);
   if constexpr (EPI == EPI_RESID) cp_async_wait<0>();
   __syncthreads();
 
@@ -342,7 +355,9 @@ gemv_tc_kernel(TcArgs a) {
   }
   for (int j = 0; j < n_mine; ++j) {
     const int p0 = ku * KS, np = min(P - p0, KS);
-    if (!mbar_wait_warp(&bars[j % TS], (uint32_t)((j / TS) & 1), a.spin, lane)) {
+    // every lane polls the stage's mbarrier (lane-0 polling plus a shuffle
+    // measured 2% slower per token here)
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[j % TS], (uint32_t)((j / TS) & 1), a.spin))) {
       failed = j;
       break;
     }
@@ -420,7 +435,7 @@ gemv_tc_kernel(TcArgs a) {
         }
       }
     }
-    if (have) tc_epilogue<NB, EPI>(a, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_s, ctile0 * 16);
+    if (have) tc_epilogue<NB, EPI, TPX>(a, tp, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_s, ctile0 * 16);
     acc0 = acc1 = 0.f;
     ++tile;
   }
@@ -436,31 +451,33 @@ gemv_tc_kernel(TcArgs a) {
     }
     __syncwarp();
   }
-  if (EPI == EPI_STORE && a.tp.push[0]) {
+  if constexpr (TPX && EPI == EPI_STORE) {
     // the exchange is published once every CTA's rows are out: the last CTA
     // to take a ticket (every CTA takes one, a failed one too, so the
     // counter returns to zero) advances the epoch and flags every rank
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-      const int tk = atomicAdd(a.tp.ticket, 1);
+      const int tk = atomicAdd(tp.v.ticket, 1);
       if (tk == (int)gridDim.x - 1) {
-        *a.tp.ticket = 0;
+        *tp.v.ticket = 0;
         __threadfence_system();
-        const unsigned ep = *a.tp.epoch + 1u;
-        *a.tp.epoch = ep;
-        for (int r = 0; r < a.tp.tp; ++r) tc_st_release_sys(a.tp.flags[r], ep);
+        const unsigned ep = *tp.v.epoch + 1u;
+        *tp.v.epoch = ep;
+        for (int r = 0; r < tp.v.tp; ++r) tc_st_release_sys(tp.v.flags[r], ep);
       }
     }
   }
 }
 
-template <int NB, typename ST, int EPI, bool NORM, int KS>
-int launch_tc(const TcArgs& a, size_t smem, int grid, cudaStream_t s) {
-  auto kern = gemv_tc_kernel<NB, ST, EPI, NORM, KS>;
+template <int NB, typename ST, int EPI, bool NORM, int KS, bool TPX>
+int launch_tc(const TcArgs& a, const TcTp* tpx, size_t smem, int grid, cudaStream_t s) {
+  auto kern = gemv_tc_kernel<NB, ST, EPI, NORM, KS, TPX>;
   const int rc = set_smem_limit((const void*)kern, smem, "gemv_tc");
   if (rc) return rc;
-  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(TW * 32), smem, s, a);
+  TpParam<TPX> tp{};
+  if constexpr (TPX) tp.v = *tpx;
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(TW * 32), smem, s, a, tp);
   if (e != cudaSuccess) {
     set_error("gemv_tc launch: %s", cudaGetErrorString(e));
     return LUMINA_E_CUDA;
@@ -468,31 +485,43 @@ int launch_tc(const TcArgs& a, size_t smem, int grid, cudaStream_t s) {
   return LUMINA_OK;
 }
 
+// a fused exchange (tpx non-null) has a producing side (o_proj, down_proj:
+// EPI_STORE without a norm) and consuming sides (normalizing q/k/v and
+// gate/up); the one-GPU kernels are the TPX = false instances
 template <int NB, typename ST, int KS>
-int tc_epi(const TcArgs& a, size_t smem, int grid, int epi, bool norm, cudaStream_t s) {
+int tc_epi(const TcArgs& a, const TcTp* tpx, size_t smem, int grid, int epi, bool norm, cudaStream_t s) {
   switch (epi) {
     case EPI_STORE:
-      return norm ? launch_tc<NB, ST, EPI_STORE, true, KS>(a, smem, grid, s)
-                  : launch_tc<NB, ST, EPI_STORE, false, KS>(a, smem, grid, s);
-    case EPI_RESID: return norm ? LUMINA_E_UNSUPPORTED : launch_tc<NB, ST, EPI_RESID, false, KS>(a, smem, grid, s);
-    case EPI_SWIGLU: return norm ? launch_tc<NB, ST, EPI_SWIGLU, true, KS>(a, smem, grid, s) : LUMINA_E_UNSUPPORTED;
-    default: return norm ? launch_tc<NB, ST, EPI_ROPE_KV, true, KS>(a, smem, grid, s) : LUMINA_E_UNSUPPORTED;
+      if (norm) return tpx ? LUMINA_E_UNSUPPORTED : launch_tc<NB, ST, EPI_STORE, true, KS, false>(a, tpx, smem, grid, s);
+      return tpx ? launch_tc<NB, ST, EPI_STORE, false, KS, true>(a, tpx, smem, grid, s)
+                 : launch_tc<NB, ST, EPI_STORE, false, KS, false>(a, tpx, smem, grid, s);
+    case EPI_RESID:
+      return norm || tpx ? LUMINA_E_UNSUPPORTED : launch_tc<NB, ST, EPI_RESID, false, KS, false>(a, tpx, smem, grid, s);
+    case EPI_SWIGLU:
+      if (!norm) return LUMINA_E_UNSUPPORTED;
+      return tpx ? launch_tc<NB, ST, EPI_SWIGLU, true, KS, true>(a, tpx, smem, grid, s)
+                 : launch_tc<NB, ST, EPI_SWIGLU, true, KS, false>(a, tpx, smem, grid, s);
+    default:
+      if (!norm) return LUMINA_E_UNSUPPORTED;
+      return tpx ? launch_tc<NB, ST, EPI_ROPE_KV, true, KS, true>(a, tpx, smem, grid, s)
+                 : launch_tc<NB, ST, EPI_ROPE_KV, true, KS, false>(a, tpx, smem, grid, s);
   }
 }
 
 template <int KS>
-int tc_nb(const TcArgs& a, size_t smem, int grid, int nb, bool fp16, int epi, bool norm, cudaStream_t s) {
+int tc_nb(const TcArgs& a, const TcTp* tpx, size_t smem, int grid, int nb, bool fp16, int epi, bool norm,
+          cudaStream_t s) {
   if (fp16) {
     switch (nb) {
-      case 1: return tc_epi<1, __half, KS>(a, smem, grid, epi, norm, s);
-      case 2: return tc_epi<2, __half, KS>(a, smem, grid, epi, norm, s);
-      default: return tc_epi<4, __half, KS>(a, smem, grid, epi, norm, s);
+      case 1: return tc_epi<1, __half, KS>(a, tpx, smem, grid, epi, norm, s);
+      case 2: return tc_epi<2, __half, KS>(a, tpx, smem, grid, epi, norm, s);
+      default: return tc_epi<4, __half, KS>(a, tpx, smem, grid, epi, norm, s);
     }
   }
   switch (nb) {
-    case 1: return tc_epi<1, float, KS>(a, smem, grid, epi, norm, s);
-    case 2: return tc_epi<2, float, KS>(a, smem, grid, epi, norm, s);
-    default: return tc_epi<4, float, KS>(a, smem, grid, epi, norm, s);
+    case 1: return tc_epi<1, float, KS>(a, tpx, smem, grid, epi, norm, s);
+    case 2: return tc_epi<2, float, KS>(a, tpx, smem, grid, epi, norm, s);
+    default: return tc_epi<4, float, KS>(a, tpx, smem, grid, epi, norm, s);
   }
 }
 
@@ -536,13 +565,15 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   a.fault = fault;
   a.spin = wait_spin_limit();
   if (pf) a.pf = *pf;
+  const TcTp* tpx = nullptr;
   if (tp && tp->tp > 1) {
     const bool producer = tp->push[0] != nullptr, consumer = tp->in_flags != nullptr;
-    if (producer == consumer || (producer && epi != EPI_STORE) || (consumer && !norm_w) || tp->tp > TCTP_MAX) {
+    if (producer == consumer || (producer && (epi != EPI_STORE || norm_w)) ||
+        (consumer && (!norm_w || (epi != EPI_SWIGLU && epi != EPI_ROPE_KV))) || tp->tp > TCTP_MAX) {
       set_error("gemv_tc: a fused exchange needs a storing producer or a normalizing consumer");
       return LUMINA_E_ARG;
     }
-    a.tp = *tp;
+    tpx = tp;
   }
   const int es = w->fp16_scales ? 2 : 4;
   // whole tiles per CTA: the smallest grid with the smallest per-CTA share
@@ -562,9 +593,9 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
     a.stage_bytes = (ks * 512 + groups * 16 * es + 127) / 128 * 128;
     const size_t smem = (size_t)a.x_bytes + (size_t)TW * TS * a.stage_bytes + TW * TS * 8;
     if (smem > budget) continue;
-    if (ks == 8) return tc_nb<8>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
-    if (ks == 6) return tc_nb<6>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
-    return tc_nb<4>(a, smem, grid, NB, w->fp16_scales, epi, norm, s);
+    if (ks == 8) return tc_nb<8>(a, tpx, smem, grid, NB, w->fp16_scales, epi, norm, s);
+    if (ks == 6) return tc_nb<6>(a, tpx, smem, grid, NB, w->fp16_scales, epi, norm, s);
+    return tc_nb<4>(a, tpx, smem, grid, NB, w->fp16_scales, epi, norm, s);
   }
   return LUMINA_E_UNSUPPORTED;
 }

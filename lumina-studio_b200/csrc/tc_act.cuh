@@ -99,9 +99,10 @@ __device__ __forceinline__ void tq_add8(float (&v)[8], const float* p, int k0, i
 }
 
 // the input rows: x, plus (n_add > 0) the rank-ordered sum of the add[]
-// rows; `xout` (may be null) receives them before any normalization
+// rows; `xout` (may be null) receives them before any normalization.
+// tq_run takes it by pointer: null (every one-GPU launch) compiles it out
 struct TqSum {
-  const float* const* add = nullptr;
+  const float* add[TQ_MAX_ADD] = {};
   int n_add = 0;
   float* xout = nullptr;
 };
@@ -111,7 +112,7 @@ struct TqSum {
 template <int NB, int NW, bool NORM>
 __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, int P, const float* nw, float eps,
                                        const float (&w)[TQ_CH][8], uint4* xb, int2* fq, float* red,
-                                       const TqSum& sum = TqSum{}) {
+                                       const TqSum* sum = nullptr) {
   constexpr int NC = 2 * NB;
   const int n_items = NB * P * 8, per_pass = TQ_CH * (int)blockDim.x;
   const bool vec_x = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
@@ -128,9 +129,11 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
       if (b < nb)
         for (int k = threadIdx.x; k < K; k += blockDim.x) {
           float v = x[(size_t)b * ldx + k];
+          if (sum) {
 #pragma unroll
-          for (int r = 0; r < TQ_MAX_ADD; ++r)
-            if (r < sum.n_add) v += __ldcg(sum.add[r] + (size_t)b * ldx + k);
+            for (int r = 0; r < TQ_MAX_ADD; ++r)
+              if (r < sum->n_add) v += __ldcg(sum->add[r] + (size_t)b * ldx + k);
+          }
           ss[b] = fmaf(v, v, ss[b]);
         }
     }
@@ -149,18 +152,18 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
       for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
       if (i < n_items && b < nb) tq_load8(v[u], x + (size_t)b * ldx, k0, K, vec_x);
     }
-    if (sum.n_add > 0) {
+    if (sum && sum->n_add > 0) {
       // x + rank 0 + rank 1 + ... (the same order on every rank)
 #pragma unroll
       for (int r = 0; r < TQ_MAX_ADD; ++r) {
-        if (r >= sum.n_add) break;
+        if (r >= sum->n_add) break;
 #pragma unroll
         for (int u = 0; u < TQ_CH; ++u) {
           const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
-          if (i < n_items && row[u] < nb) tq_add8(v[u], sum.add[r] + (size_t)row[u] * ldx, (i % (P * 8)) * 8, K, vec_x);
+          if (i < n_items && row[u] < nb) tq_add8(v[u], sum->add[r] + (size_t)row[u] * ldx, (i % (P * 8)) * 8, K, vec_x);
         }
       }
-      if (sum.xout && blockIdx.x == 0) {
+      if (sum->xout && blockIdx.x == 0) {
 #pragma unroll
         for (int u = 0; u < TQ_CH; ++u) {
           const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
@@ -168,7 +171,7 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
           if (i < n_items && row[u] < nb)
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              if (k0 + j < K) sum.xout[(size_t)row[u] * ldx + k0 + j] = v[u][j];
+              if (k0 + j < K) sum->xout[(size_t)row[u] * ldx + k0 + j] = v[u][j];
         }
       }
     }

@@ -24,17 +24,20 @@ void set_error(const char* fmt, ...) {
 }
 const char* get_error() { return g_err; }
 
+// per device, filled on first use (atomics: host threads may race to fill
+// a slot; every one of them writes the same value)
 int sm_count() {
-  static int n[64] = {0};
+  static std::atomic<int> n[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (!n[dev]) {
-    int v = 0;
+  int v = n[dev].load(std::memory_order_relaxed);
+  if (!v) {
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    n[dev] = v > 0 ? v : 148;
+    if (v <= 0) v = 148;
+    n[dev].store(v, std::memory_order_relaxed);
   }
-  return n[dev];
+  return v;
 }
 
 // Dynamic shared-memory limits are a per-device attribute of a kernel: the
@@ -211,7 +214,9 @@ int fault_error(const char* what, int word) {
 static int ensure_levels() {
   int dev = 0;
   cudaGetDevice(&dev);
+  static std::mutex mu;
   static bool done[64] = {false};
+  std::lock_guard<std::mutex> lk(mu);
   if (dev >= 0 && dev < 64 && done[dev]) return LUMINA_OK;
   double h[4][16] = {};
   for (int b = 1; b <= 4; ++b) linspace_levels(b, h[b - 1]);

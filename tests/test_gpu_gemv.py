@@ -167,6 +167,36 @@ def test_gemv_fragment_layout(torch_cuda, monkeypatch, group, N, K, batch):
     np.testing.assert_allclose(y[:, rows], km, rtol=TIGHT, atol=TIGHT * np.abs(km).max())
 
 
+def test_gemv_fragment_layout_two_devices(torch_cuda, monkeypatch):
+    """One process, the tensor-pipe GEMV on device 0 and then on device 1:
+    the kernel's raised shared-memory limit is a per-device setting, so the
+    launch on the second device must raise it there too; both devices give
+    the same bits."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    monkeypatch.setenv("LUMINA_INT4_LAYOUT", "mma")
+    from lumina_b200.cuda import Weight
+    rng = np.random.default_rng(11)
+    N, K, group = 4096, 4096, 64
+    codes = rng.integers(0, 16, (N, K)).astype(np.uint8)
+    scales = (np.abs(rng.standard_normal((N, K // group))) * 0.02 + 1e-3).astype(np.float16).astype(np.float32)
+    x = rng.standard_normal((1, K)).astype(np.float32)
+    outs = []
+    for dev in (0, 1):
+        w = Weight.upload("int4", group, "nibble", lf.pack_codes_nibble(codes), scales, N, K, device=dev)
+        with torch.cuda.device(dev):
+            xd = torch.from_numpy(x).to(f"cuda:{dev}")
+            yd = torch.empty((1, N), dtype=torch.float32, device=f"cuda:{dev}")
+            w.gemv(xd.data_ptr(), 1, K, yd.data_ptr(), N)
+            torch.cuda.synchronize(dev)
+            outs.append(yd.cpu().numpy())
+        w.free()
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    W = np.repeat(scales, group, axis=1) * lf.levels(4).astype(np.float32)[codes]
+    assert rel_l2(outs[1], ref_gemv(x, W)) < REL_L2
+
+
 def test_fp32_scales_path(torch_cuda):
     rng = np.random.default_rng(3)
     N, K = 300, 640
