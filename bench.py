@@ -310,7 +310,13 @@ def run_sweep(args):
     os.environ["LUMINA_INT4_LAYOUT"] = "mma"  # int4 in the decode model's tensor-pipe layout
     rng = np.random.default_rng(0)
     cpu_cache = {}
-    for kind, bits, group in SWEEP_KINDS:
+    # narrow kinds twice: packed row-major (CUDA-core kernels) and one code
+    # per nibble in the fragment layout (the tensor-pipe kernels)
+    cases = [(kind, bits, group, lay) for kind, bits, group in SWEEP_KINDS
+             for lay in (("mma",) if bits == 4 else ("row", "mma"))]
+    for kind, bits, group, lay in cases:
+        if bits < 4:
+            os.environ["LUMINA_NARROW_LAYOUT"] = lay
         for N, K in SWEEP_SHAPES:
             ng = -(-K // group)
             if kind == "binary":
@@ -347,7 +353,11 @@ def run_sweep(args):
                     del g
                 ms = float(np.median(times))
                 b = sweep_bytes(N, K, bits, group, batch)
+                db = ws[0].info()["device_bytes"] + batch * K * 4 + batch * N * 4
                 print(json.dumps({"sweep": "gemv", "kind": kind, "group": group, "N": N, "K": K, "batch": batch,
+                                  "layout": "fragment (one code per nibble)" if lay == "mma" and bits < 4 else
+                                  ("fragment" if lay == "mma" else "row-major packed"),
+                                  "device_bytes_per_call": db,
                                   "us_per_call": ms * 1e3, "bytes_per_call": b, "gbs": b / (ms * 1e-3) / 1e9,
                                   "frac": b / (ms * 1e-3) / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
                                   "weight_copies": copies,

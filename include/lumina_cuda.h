@@ -64,7 +64,13 @@ typedef struct lumina_weight lumina_weight;
  * GEMV and are never expanded to floating point. Replaces the per-tensor
  * unpack + dequant of LuminaAdapter.load (adapters/lumina.py:122-151).
  * For kind BINARY `cols` must be the logical width (the reference loader
- * requires it to be ceil(cols/group)*group, lumina.py:143-148). */
+ * requires it to be ceil(cols/group)*group, lumina.py:143-148).
+ * Device layout: row-major packed codes; with LUMINA_INT4_LAYOUT=mma in the
+ * environment int4 codes, and with LUMINA_NARROW_LAYOUT=mma int3 / int2 /
+ * binary codes (one per nibble: 4 bits of device memory per code), go to
+ * the tensor-core fragment layout that the tensor-pipe GEMVs read (group a
+ * multiple of 64: 64, 128 or 256). A model takes narrow codes row-major
+ * only. */
 int lumina_weight_upload(int device, int kind, int group_size, int pack,
                          const uint8_t* codes_host, size_t codes_len,
                          const float* scales_host, size_t n_scales,
@@ -84,8 +90,8 @@ int lumina_weight_dequant(const lumina_weight* w, float* out_dev, void* stream);
  * GEMV that replaces `h @ W(name)` in ChatModel._layer (chat.py:239-243,282,
  * 300-303; W = dequantized Lumina weight). x rows have stride ldx floats, y
  * rows stride ldy floats. Uses the library's per-device activation scratch
- * for batches the fused kernels do not take (calls that overlap on the GPU on
- * one device race on it). */
+ * for batches the fused kernels do not take, and for 5..16 rows over the
+ * fragment layout (calls that overlap on the GPU on one device race on it). */
 int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx,
                 float* y_dev, int ldy, void* stream);
 /* y[m, n] = sum_k x[m, k] * W[n, k] for `rows` hidden rows at once (any

@@ -382,7 +382,7 @@ static int mma_epi(const MmaArgs& a, int epi, bool norm, cudaStream_t s) {
 // batch in tiles of 8 (the MMA's N); each tile quantizes its own rows
 int gemv_mma_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
                     float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk) {
-  if (!w->mma) return LUMINA_E_UNSUPPORTED;
+  if (!w->mma || w->bits != 4) return LUMINA_E_UNSUPPORTED;
   if ((epi == EPI_SWIGLU || epi == EPI_ROPE_KV) && (w->rows & 1)) {
     set_error("gemv: paired epilogue needs an even row count");
     return LUMINA_E_ARG;

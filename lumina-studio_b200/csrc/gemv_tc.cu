@@ -9,6 +9,8 @@
 // fragment holds Dh = sum c*qh and Dl = sum c*ql over the 64 columns, exact.
 // Per row and pair: T = 2*(256*Dh + Dl) - 15*sum(q), y += T * sx * s, and
 // y /= 15 at the end (adapters/lumina.py:135-139: level = (2c - 15) / 15).
+// Narrow codes stored one per nibble (int3 / int2 / binary, the same
+// layout) use their own level count L = 2^bits - 1 in place of 15.
 // The A operand takes the code bytes straight from the fragment layout
 // (weights.cuh, mma = 1): low nibbles = the tile's rows 0..7, high nibbles =
 // rows 8..15 times 16; that factor 16 is folded exactly into the fp32 scale.
@@ -82,6 +84,7 @@ struct TcArgs {
   int* fault;
   long long spin;  // polls before a wait on a ring stage gives up (wait_spin_limit())
   L2Prefetch pf;   // the next kernel's bytes, pulled into L2 while this one runs
+  int lv;          // levels - 1 of the codes: 15 (int4), 7, 3, 1 (narrow codes one per nibble)
 };
 
 // The fused tensor-parallel exchange of a launch, a kernel parameter of its
@@ -122,7 +125,7 @@ __device__ __forceinline__ void load_scale_pair(const uint8_t* p, float& s0, flo
 }
 
 // Epilogue of one finished 16-row tile for batch row t (lane t of each row
-// group g): v0 = row g, v1 = row g + 8, already / 15. Paired epilogues (rows
+// group g): v0 = row g, v1 = row g + 8, already / L. Paired epilogues (rows
 // 2i, 2i+1) take the odd row from the neighbouring row group's lane.
 // ep_s: the operands staged in shared memory by the prologue -- residual
 // rows [res0, res0 + MT*16) of each batch row (EPI_RESID), or the RoPE
@@ -226,7 +229,7 @@ gemv_tc_kernel(TcArgs a, TpParam<TPX> tp) {
   const int n_mine = wu1 - wu0;
 
   extern __shared__ __align__(128) uint8_t smem[];
-  // [B fragments: P x NC x 4 lanes x 16 B][(sx, -15*sum q): P x NB x 8 B]
+  // [B fragments: P x NC x 4 lanes x 16 B][(sx, -L*sum q): P x NB x 8 B]
   // [tile counters: MT ints][partials: TW x 2 x 16 x NB floats]
   // [rings: TW x TS x stage_bytes][mbarriers: TW x TS]
   uint4* xb = reinterpret_cast<uint4*>(smem);
@@ -336,9 +339,9 @@ gemv_tc_kernel(TcArgs a, TpParam<TPX> tp) {
       sum.n_add = tp.v.tp;
       sum.xout = tp.v.xout;
     }
-    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, &sum);
+    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, a.lv, &sum);
   } else {
-    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red);
+    tq_run<NB, TW, NORM>(a.x, a.ldx, a.nb, a.cols, P, a.norm_w, a.eps, wpre, xb, fq, red, a.lv);
   }
   if constexpr (EPI == EPI_RESID) cp_async_wait<0>();
   __syncthreads();
@@ -435,7 +438,7 @@ gemv_tc_kernel(TcArgs a, TpParam<TPX> tp) {
         }
       }
     }
-    if (have) tc_epilogue<NB, EPI, TPX>(a, tp, tile * 16, v0 / 15.f, v1 / 15.f, lane, ep_blk, ep_off, ep_s, ctile0 * 16);
+    if (have) tc_epilogue<NB, EPI, TPX>(a, tp, tile * 16, v0 / (float)a.lv, v1 / (float)a.lv, lane, ep_blk, ep_off, ep_s, ctile0 * 16);
     acc0 = acc1 = 0.f;
     ++tile;
   }
@@ -530,7 +533,7 @@ int tc_nb(const TcArgs& a, const TcTp* tpx, size_t smem, int grid, int nb, bool 
 int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, const float* norm_w, float eps,
                    float* y, int ldy, int epi, const float* resid, int ldr, cudaStream_t s, const RopeKV* rk,
                    const L2Prefetch* pf, const TcTp* tp) {
-  if (!w->mma || w->bits != 4 || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
+  if (!w->mma || (w->group % 64) || batch < 1 || batch > 4) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;  // groups of 64, 128, 256 (a unit holds whole groups)
   if ((epi == EPI_SWIGLU || epi == EPI_ROPE_KV) && (w->rows & 1)) {
@@ -562,6 +565,7 @@ int gemv_tc_launch(const lumina_weight* w, const float* x, int ldx, int batch, c
   a.ldr = ldr;
   if (rk) a.rk = *rk;
   a.nb = batch;
+  a.lv = (1 << w->bits) - 1;
   a.fault = fault;
   a.spin = wait_spin_limit();
   if (pf) a.pf = *pf;

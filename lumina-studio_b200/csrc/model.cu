@@ -59,6 +59,7 @@ struct lumina_model {
   float *x = nullptr, *qkv_buf = nullptr, *q_buf = nullptr, *attn = nullptr, *ffn_buf = nullptr;
   float *g_buf = nullptr, *u_buf = nullptr, *part = nullptr, *logits = nullptr;
   __half* x16 = nullptr;  // fp16 activation rows of the tcgen05 projections
+  size_t x16_bytes = 0;   // (also the int16 fragments of the batched tensor-pipe GEMV)
   SplitWork split;        // partials of split-K projections and split-key attention
   ActQ aq{};
   void* kv_tmp = nullptr;
@@ -398,6 +399,9 @@ int peer_exchange(lumina_model* m, int slot, int mode, size_t n, float* out) {
 // rows from which a projection runs as a tcgen05 GEMM instead of the
 // batched tensor-pipe GEMV
 constexpr int TC05_MIN_ROWS = 8;
+// rows up to which a projection runs on the batched tensor-pipe GEMV
+// (gemv_tcb.cu) before the tcgen05 GEMM
+constexpr int TCB_MAX_ROWS = 32;
 
 // `exact_rows`: keep several-row projections on the int16-activation path
 // (about 5e-5 relative) instead of the fp16-activation tcgen05 GEMM (about
@@ -417,6 +421,21 @@ int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, i
   if (w->mma) {
     if (n <= 4) {
       const int rc = gemv_tc_launch(w, x, ldx, n, norm, m->c.eps, y, ldy, epi, resid, ldr, m->stream, rk, pf);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    }
+    if (n <= TCB_MAX_ROWS && m->x16) {
+      // 5..32 rows (decode batches, tree verification): the batched
+      // tensor-pipe GEMV, int16 activations like the decode GEMV; the fused
+      // q/k/v rows go to qkv_buf in their original order for the RoPE + KV
+      // append kernel
+      const bool qkv = epi == EPI_ROPE_KV;
+      const int width = rk ? (rk->nh + 2 * rk->nkv) * rk->hd : 0;
+      int rc = gemv_tcb_launch(w, x, ldx, n, norm, m->c.eps, m->x16, m->x16_bytes, qkv ? m->qkv_buf : y,
+                               qkv ? width : ldy, qkv ? EPI_STORE : epi, resid, ldr,
+                               qkv ? (rk->nh + rk->nkv) * rk->hd : 0, rk ? rk->hd : 0, m->stream);
+      if (rc == LUMINA_OK && qkv)
+        rc = launch_rope_append(rk->kv_fp16, m->qkv_buf, rk->nh, rk->nkv, rk->hd, rk->cos_t, rk->sin_t, rk->row_pos,
+                                m->P_dev, rk->block_table, rk->bs, rk->kcache, rk->vcache, rk->q_out, n, m->stream);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     if (n >= TC05_MIN_ROWS && m->x16 && !exact_rows) {
@@ -898,6 +917,9 @@ int lumina_model_set_weight(lumina_model* m, const char* name, lumina_weight* w)
   LUMINA_CHECK_ARG(m && name && w, "model_set_weight: null pointer");
   LUMINA_CHECK_ARG(!m->finalized, "model_set_weight: model already finalized");
   LUMINA_CHECK_ARG(w->device == m->device, "model_set_weight: weight on device %d, model on %d", w->device, m->device);
+  LUMINA_CHECK_ARG(!w->mma || w->bits == 4,
+                   "model_set_weight: int%d codes in the fragment layout serve lumina_gemv only; a model takes them "
+                   "row-major", w->bits);
   int l = -1;
   std::string what;
   if (!parse_layer_name(name, &l, &what) || l < 0 || l >= m->c.n_layer) {
@@ -1128,7 +1150,8 @@ int lumina_model_finalize(lumina_model* m) {
   const int kmax = std::max(std::max(m->d, qw), m->ffn);
   const int nblk_pad = ((kmax + 31) / 32 + 4) / 4 * 4;  // whole chunks for every kind
   if (R >= TC05_MIN_ROWS) {
-    TRY(dalloc(m, (void**)&m->x16, gemm_tc05_x16_elems(R, kmax) * 2));
+    m->x16_bytes = gemm_tc05_x16_elems(R, kmax) * 2;
+    TRY(dalloc(m, (void**)&m->x16, m->x16_bytes));
     TRY(dalloc(m, (void**)&m->split.ws, SPLIT_WS_ELEMS * sizeof(float)));
     TRY(dalloc(m, (void**)&m->split.cnt, SPLIT_COUNTERS * sizeof(int)));
     LUMINA_CUDA_TRY(cudaMemset(m->split.cnt, 0, SPLIT_COUNTERS * sizeof(int)));
@@ -1276,9 +1299,12 @@ int lumina_model_init_peers(lumina_model* m, const uint8_t* handles) {
     m->peer_exch[r] = static_cast<char*>(p);
   }
   m->peers_ready = true;
-  // the decode step fuses its exchanges when every projection it needs runs
-  // on the tensor-pipe GEMV (int4 fragment layout, fused q/k/v and gate/up)
-  m->tp_fusable = getenv("LUMINA_TP_EXCHANGE_KERNELS") == nullptr;
+  // LUMINA_TP_FUSED_EXCHANGE=1: the decode step fuses its exchanges into the
+  // GEMVs when every projection it needs runs on the tensor-pipe GEMV (int4
+  // fragment layout, fused q/k/v and gate/up). Off by default: measured at
+  // 447 tok/s against 523 for the exchange kernels on two B200s (7B int4).
+  const char* fe = getenv("LUMINA_TP_FUSED_EXCHANGE");
+  m->tp_fusable = fe && fe[0] == '1';
   for (const Layer& Ly : m->L) {
     const lumina_weight* ws[4] = {Ly.qkv, Ly.o, Ly.gu, Ly.down};
     for (const lumina_weight* w : ws)

@@ -108,10 +108,10 @@ struct TqSum {
 };
 
 // NB rows (nb live, row stride ldx) -> xb [P][2 NB][4 lanes] uint4 and
-// fq [P][NB]; NW warps; the caller syncs the CTA before reading xb / fq
+// fq [P][NB] (sx, -lv * sum q; lv = levels - 1 of the codes); NW warps; the caller syncs the CTA before reading xb / fq
 template <int NB, int NW, bool NORM>
 __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, int P, const float* nw, float eps,
-                                       const float (&w)[TQ_CH][8], uint4* xb, int2* fq, float* red,
+                                       const float (&w)[TQ_CH][8], uint4* xb, int2* fq, float* red, int lv,
                                        const TqSum* sum = nullptr) {
   constexpr int NC = 2 * NB;
   const int n_items = NB * P * 8, per_pass = TQ_CH * (int)blockDim.x;
@@ -252,7 +252,7 @@ __device__ __forceinline__ void tq_run(const float* x, int ldx, int nb, int K, i
         xw[(tt0 + e) * 4 + comp] = hw[e];
         xw[16 + (tt0 + e) * 4 + comp] = lw[e];
       }
-      if (oc == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -15 * qs);
+      if (oc == 0) fq[(size_t)p * NB + b] = make_int2(__float_as_int(sxv), -lv * qs);
     }
   }
 }

@@ -205,9 +205,9 @@ int clear_fault_async(cudaStream_t s) {
 }
 
 int fault_error(const char* what, int word) {
-  set_error("%s: a device wait timed out (fault word %#x:%s%s%s%s)", what, word,
+  set_error("%s: a device wait timed out (fault word %#x:%s%s%s%s%s)", what, word,
             (word & 1) ? " gemv_fused_kernel" : "", (word & 2) ? " gemv_tc_kernel" : "",
-            (word & 4) ? " peer exchange" : "", (word & 8) ? " gemm_tc05_kernel" : "");
+            (word & 4) ? " peer exchange" : "", (word & 8) ? " gemm_tc05_kernel" : "", (word & 16) ? " gemv_tcb_kernel" : "");
   return LUMINA_E_CUDA;
 }
 
@@ -410,11 +410,15 @@ int lumina_weight_upload(int device, int kind, int group_size, int pack, const u
   L.spr = (n_groups * es + 15) / 16 * 16;
   std::vector<uint8_t> sdev;
   // int4 goes to the tensor-core fragment layout when LUMINA_INT4_LAYOUT=mma
-  // (gemv_tc.cu for batch <= 8, gemv_mma.cu beyond); a model converts its
-  // own int4 projections to that layout when it is finalized
-  const char* lay = getenv("LUMINA_INT4_LAYOUT");
+  // (gemv_tc.cu for batch <= 4, gemv_tcb.cu for 5..32, gemv_mma.cu beyond);
+  // a model converts its own int4 projections to that layout when it is
+  // finalized. int3 / int2 / binary go there too, one code per nibble, when
+  // LUMINA_NARROW_LAYOUT=mma: 4 bits of device memory per code instead of
+  // 3 / 2 / 1, for the tensor-pipe GEMVs of lumina_gemv (batch <= 16)
+  const char* lay = getenv(bits == 4 ? "LUMINA_INT4_LAYOUT" : "LUMINA_NARROW_LAYOUT");
   const bool want_mma = lay && strcmp(lay, "mma") == 0;
-  if (bits == 4 && group_size % 64 == 0 && want_mma) {
+  const int gpw = group_size / 64;
+  if (group_size % 64 == 0 && (gpw & (gpw - 1)) == 0 && gpw <= 4 && want_mma) {
     // tensor-core fragment layout (gemv_mma.cu): built from the row-major codes
     L.mma = 1;
     const int nbp = (L.nblk + 1) / 2 * 2;
@@ -425,9 +429,10 @@ int lumina_weight_upload(int device, int kind, int group_size, int pack, const u
     M.row_bytes = nbp * 16;
     M.rows_pad = rows32;
     for (int r = 0; r < rows; ++r) {
-      const uint8_t* src = dev.data() + (size_t)r * L.row_bytes;  // nibble row
+      const uint8_t* src = dev.data() + (size_t)r * L.row_bytes;  // int4: the nibble row
+      const uint8_t* fsrc = codes_host + (size_t)r * stride;       // narrow kinds: the file row
       for (int k = 0; k < cols; ++k) {
-        const int c = (src[k >> 1] >> (4 * (k & 1))) & 0xF;
+        const int c = bits == 4 ? (src[k >> 1] >> (4 * (k & 1))) & 0xF : file_code(kind, pack, fsrc, k);
         int nib = 0;
         const size_t o = mma_code_byte(M, r, k, &nib);
         m[o] |= (uint8_t)(c << (4 * nib));
@@ -537,6 +542,14 @@ int lumina_gemv(const lumina_weight* w, const float* x_dev, int batch, int ldx, 
   if (w->mma) {
     if (batch <= 4) {
       const int rc = gemv_tc_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s, nullptr);
+      if (rc != LUMINA_E_UNSUPPORTED) return rc;
+    } else {
+      // 5..16 rows: the batched tensor-pipe GEMV (gemv_tcb.cu)
+      void* frag = nullptr;
+      const size_t fb = gemv_tcb_frag_bytes(batch, w->cols);
+      int rc = tcb_frag_scratch(w->device, fb, &frag);
+      if (rc) return rc;
+      rc = gemv_tcb_launch(w, x_dev, ldx, batch, nullptr, 0.f, frag, fb, y_dev, ldy, EPI_STORE, nullptr, 0, 0, 0, s);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     return gemv_mma_launch(w, x_dev, ldx, batch, nullptr, 0.f, y_dev, ldy, EPI_STORE, nullptr, 0, s);

@@ -236,6 +236,23 @@ int gemm_tc05_launch(const lumina_weight* w, const float* x, int ldx, int M, con
 int dense_tc05_launch(const __half* W, int rows, int K, const float* x, int ldx, int M, __half* x16, float* y,
                       int ldy, cudaStream_t s, const SplitWork* sw = nullptr);
 
+// int4 GEMV on the tensor pipe for 1..32 activation rows (gemv_tcb.cu),
+// weights in the fragment layout: x (M rows, stride ldx; RMSNorm fused when
+// norm_w is given) -> int16 B fragments in `frag` (gemv_tcb_frag_bytes(M,
+// cols) bytes, 16-byte aligned) -> y. Epilogues EPI_STORE (rows < qk_rows of
+// a fused q/k/v weight are stored at their un-permuted index, head size hd),
+// EPI_RESID, EPI_SWIGLU. K is split over the CTAs of a thread-block
+// cluster (partials combined over distributed shared memory, in slice
+// order) when the fragments of a whole row do not fit a CTA's shared memory
+// or the grid would leave SMs idle. LUMINA_E_UNSUPPORTED when the weight or
+// the shape does not fit.
+size_t gemv_tcb_frag_bytes(int M, int cols);
+int gemv_tcb_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
+                    void* frag, size_t frag_bytes, float* y, int ldy, int epi, const float* resid, int ldr,
+                    int qk_rows, int hd, cudaStream_t s);
+// per-device fragment scratch for the library's own entry points
+int tcb_frag_scratch(int device, size_t bytes, void** out);
+
 // Per-device activation scratch owned by the library (grown on demand).
 int scratch_actq(int device, int batch, int nblk_pad, ActQ* out);
 // Bytes of, and carving of, one activation scratch region at `base`.

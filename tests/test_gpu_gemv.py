@@ -141,12 +141,14 @@ def test_gemv_7b_shapes(torch_cuda, kind, group, N, K, batch):
 
 @pytest.mark.parametrize("group,N,K", [(64, 4096, 4096), (64, 12288, 4096), (128, 4096, 11008), (64, 300, 640),
                                          (64, 4096, 11008)])
-@pytest.mark.parametrize("batch", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 9, 16])
 def test_gemv_fragment_layout(torch_cuda, monkeypatch, group, N, K, batch):
     """int4 in the tensor-core fragment layout: the tensor-pipe decode GEMV
-    (batch <= 4: units split over CTAs and warps, shared-tile combine; 64-
-    column activation blocks) and the batched fragment-layout GEMV (batch 8)
-    give their exact-model results, and the same bits on a repeated call."""
+    (batch <= 4: units split over CTAs and warps, shared-tile combine) and
+    the batched tensor-pipe GEMV (5..16: activation fragments in global
+    memory, K split over CTAs with an ordered combine) give the exact-model
+    results of their arithmetic (64-column activation blocks), and the same
+    bits on a repeated call."""
     monkeypatch.setenv("LUMINA_INT4_LAYOUT", "mma")
     rng = np.random.default_rng(N + K + batch)
     codes = rng.integers(0, 16, (N, K)).astype(np.uint8)
@@ -162,8 +164,40 @@ def test_gemv_fragment_layout(torch_cuda, monkeypatch, group, N, K, batch):
     W = np.repeat(scales, group, axis=1)[:, :K] * lf.levels(4).astype(np.float32)[codes]
     assert rel_l2(y, ref_gemv(x, W)) < REL_L2
     rows = np.r_[0:128, N - 128:N]
-    arith = kernel_model.TENSOR_PIPE if batch <= 4 else kernel_model.CUDA_CORE
-    km = kernel_model.gemv(codes[rows], scales[rows], group, 4, x, **arith)
+    km = kernel_model.gemv(codes[rows], scales[rows], group, 4, x, **kernel_model.TENSOR_PIPE)
+    np.testing.assert_allclose(y[:, rows], km, rtol=TIGHT, atol=TIGHT * np.abs(km).max())
+
+
+@pytest.mark.parametrize("kind,group,N,K", [("int3", 64, 4096, 4096), ("int2", 128, 11008, 4096),
+                                            ("binary", 128, 4096, 11008), ("int2", 128, 300, 640)])
+@pytest.mark.parametrize("batch", [1, 3, 4, 7, 16])
+def test_gemv_narrow_fragment_layout(torch_cuda, monkeypatch, kind, group, N, K, batch):
+    """int3 / int2 / binary codes stored one per nibble in the fragment
+    layout (LUMINA_NARROW_LAYOUT=mma): the unpack gate returns the file's
+    codes, and the tensor-pipe GEMVs (decode for batch <= 4, batched for
+    5..16) give the exact-model results with the kind's own level count."""
+    monkeypatch.setenv("LUMINA_NARROW_LAYOUT", "mma")
+    torch = torch_cuda
+    bits = lf.KIND_BITS[kind]
+    rng = np.random.default_rng(N + K + batch + bits)
+    codes = rng.integers(0, 1 << bits, (N, K)).astype(np.uint8)
+    ng = (K + group - 1) // group
+    scales = (np.abs(rng.standard_normal((N, ng))) * 0.02 + 1e-3).astype(np.float16).astype(np.float32)
+    w = upload(kind, group, codes, scales, N, K)
+    rows32, nbp = -(-N // 32) * 32, (-(-K // 32) + 1) // 2 * 2
+    assert w.info()["device_bytes"] == rows32 * nbp * 16 + rows32 * ng * 2  # one code per nibble
+    out = torch.empty(N * K, dtype=torch.uint8, device="cuda")
+    w.unpack(out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().reshape(N, K), codes)
+    x = rng.standard_normal((batch, K)).astype(np.float32)
+    y = device_gemv(torch, w, x)
+    y2 = device_gemv(torch, w, x)
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
+    W = np.repeat(scales, group, axis=1)[:, :K] * lf.levels(bits).astype(np.float32)[codes]
+    assert rel_l2(y, ref_gemv(x, W)) < REL_L2
+    rows = np.r_[0:128, N - 128:N]
+    km = kernel_model.gemv(codes[rows], scales[rows], group, bits, x, **kernel_model.TENSOR_PIPE)
     np.testing.assert_allclose(y[:, rows], km, rtol=TIGHT, atol=TIGHT * np.abs(km).max())
 
 
