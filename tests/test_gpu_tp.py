@@ -113,3 +113,48 @@ def test_tp2_matches_reference_and_tp1(tiny_file, tmp_path):
         for s in range(4):
             assert rel_l2(a[f"step{s}"], c[f"step{s}"]) < 1e-4, (k, s)
         assert np.array_equal(a["greedy"], c["greedy"]), k
+
+
+
+def test_tp4_matches_reference(tiny_file, tmp_path):
+    """Four ranks (skipped on boxes with fewer GPUs), one head of the tiny
+    model per rank and an uneven FFN split (11 groups of 64 over 4 ranks):
+    the reference's logits within the bar, and on every rank the greedy
+    tokens of one GPU."""
+    import torch
+    world = 4
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    golden = os.path.join(GOLDEN, "tiny_decode.npz")
+    out = str(tmp_path / f"tp{world}")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+                        "--master-addr=127.0.0.1", f"--master-port={port}",
+                        os.path.join(REPO, "tests", "tp_worker.py"), tiny_file, golden, out],
+                       env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    g = np.load(golden)
+    res = [np.load(f"{out}.rank{k}.npz") for k in range(world)]
+    for k in range(world):
+        assert rel_l2(res[k]["prefill"], g["logits_prefill_last"]) < REL_L2
+        for s in range(4):
+            if f"logits_step{s}" in g:
+                assert rel_l2(res[k][f"step{s}"], g[f"logits_step{s}"]) < REL_L2, (k, s)
+        assert np.array_equal(res[0]["greedy"], res[k]["greedy"])
+    from lumina_b200.engine import CudaChatModel
+    m = CudaChatModel.from_lumina(tiny_file, synthetic.hf_cfg(synthetic.TINY), StubTok(),
+                                  theta=synthetic.TINY["rope_theta"], max_seq=512, max_rows=128)
+    try:
+        prompt = [int(t) for t in g["prompt"]]
+        m.forward(prompt, 0)
+        for tk in g["forced"][:4]:
+            m.decode_step(int(tk), want_logits=False)
+        m.kv_truncate(len(prompt))
+        greedy = m.decode_greedy(int(g["forced"][0]), 24)
+    finally:
+        m.close()
+    assert list(res[0]["greedy"]) == greedy
