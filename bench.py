@@ -624,7 +624,9 @@ def main(argv=None):
                 extra = synthetic.prompt_ids(cfg, T, seed=1)[model.kv_length():T]
                 model.forward(extra, model.kv_length())
             model.kv_truncate(T)
+            torch.cuda.nvtx.range_push(f"attention_T{T}")  # ncu --nvtx-include "attention_T4096/"
             ms_a, by_a = model.profile_attention(4)
+            torch.cuda.nvtx.range_pop()
             attn[f"T{T}"] = {"us_per_launch": ms_a * 1e3, "bytes_per_launch": by_a,
                              "GB/s": by_a / (ms_a * 1e-3) / 1e9, "frac": by_a / (ms_a * 1e-3) / 1e9 / peak_a}
         model.kv_truncate(PROMPT)
