@@ -36,7 +36,9 @@ Besides the device-chained loop the line carries
 
 ``--impl reference`` runs only that CPU path (rank 0; other ranks exit 0).
 ``--moe`` measures the same decode on the virtual-MoE variant of the 7B
-shape (every SwiGLU split into 8 routed experts of 1376, top-2; one GPU).
+shape (every SwiGLU split into 8 routed experts of 1376, top-2); with
+``--gpus N`` the attention is tensor-parallel and the experts are split over
+the ranks (E/N each, expert parallelism).
 ``--tiny`` runs the reference's CPU-runnable tiny configuration (64-token
 prompt, 128 greedy tokens) on the device and the reference's algorithm on
 the host.
@@ -81,7 +83,7 @@ def workload(cfg, tp, moe=False):
             "heads": cfg["num_attention_heads"], "head_dim": cfg["hidden_size"] // cfg["num_attention_heads"],
             "ffn": cfg["intermediate_size"], "vocab": cfg["vocab_size"], "batch": 1, "prompt": PROMPT,
             "l2": "no flush: each token streams 3.7 GB of weights, > 126 MB L2",
-            "parallelism": f"tp{tp}"}
+            "parallelism": f"tp{tp}" + (f" attention, ep{tp} experts" if moe and tp > 1 else "")}
 
 
 # ---------------------------------------------------------------------------
@@ -529,8 +531,6 @@ def main(argv=None):
     ap.add_argument("--moe", action="store_true",
                     help="the virtual-MoE 7B shape (8 experts x 1376, top-2) instead of the dense model")
     args = ap.parse_args(argv)
-    if args.moe and args.gpus > 1:
-        ap.error("--moe runs on one GPU (virtual-MoE layers are not tensor-parallel)")
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     from lumina_b200 import synthetic
@@ -642,7 +642,9 @@ def main(argv=None):
         if args.moe:
             # the touched experts' gate/up/down codes + fp16 scales, and the fp32 router
             ie, d = cfg["intermediate_size"] // MOE_EXPERTS, cfg["hidden_size"]
-            tok_bytes += cfg["num_hidden_layers"] * (MOE_TOP_K * 3 * ie * (d // 2 + d // 64 * 2)
+            # (per rank: a rank streams the picks among its E / N experts,
+            # top_k / N of them on average)
+            tok_bytes += cfg["num_hidden_layers"] * (MOE_TOP_K * 3 * ie * (d // 2 + d // 64 * 2) / world
                                                      + MOE_EXPERTS * d * 4)
         cb = None
         if world == 1 and not args.no_cpu_baseline and not args.moe:

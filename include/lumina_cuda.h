@@ -201,8 +201,11 @@ int lumina_model_set_tensor(lumina_model* m, const char* name, const float* host
  *   "model.layers.L.mlp.experts.down_proj"     packed int4 (experts*ie, d)
  *   "model.layers.L.mlp.gate.weight"           raw router (experts, d)
  *   "model.layers.L.mlp.gate_bias"             raw router bias (experts), optional
- * int4 with groups of 64k, d % 64 == 0, experts <= 64, top_k <= 8; not
- * under tensor parallelism (LUMINA_E_UNSUPPORTED at finalize). */
+ * int4 with groups of 64k, d % 64 == 0, experts <= 64, top_k <= 8. Under
+ * tensor parallelism (tp_size > 1) the experts are sharded: rank r passes
+ * the rows of experts [r E/tp, (r+1) E/tp) (E divisible by tp) and the full
+ * router; each rank computes its experts' share of the routed MLP and the
+ * shares are summed over peer memory like a row-parallel down_proj. */
 int lumina_model_set_moe(lumina_model* m, int layer, int experts, int ie, int top_k);
 /* Check every tensor is present, allocate KV pages and buffers, build the
  * fused projection layouts. */

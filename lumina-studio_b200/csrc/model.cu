@@ -26,6 +26,7 @@ struct Layer {
   lumina_weight *moe_gu = nullptr, *moe_down = nullptr;
   float *router_w = nullptr, *router_b = nullptr;
   int moe_e = 0, moe_ie = 0, moe_k = 0;
+  int moe_e_lo = 0, moe_e_n = 0;  // this rank's experts (expert parallelism under TP)
   int router_rows = 0, router_blen = 0;  // as set, checked against moe_e at finalize
 };
 
@@ -571,7 +572,14 @@ int run_layer(lumina_model* m, int l, int n, const float* bias) {
   if (Ly.moe_e) {
     MoeLayerArgs ma{Ly.moe_gu, Ly.moe_down, Ly.router_w, Ly.router_b, Ly.post_norm, m->c.eps,
                     Ly.moe_e, Ly.moe_ie, Ly.moe_k, d};
-    return launch_moe(ma, n, m->moe, m->x, s);
+    ma.e_lo = Ly.moe_e_lo;
+    ma.e_n = Ly.moe_e_n;
+    if (!tp) return launch_moe(ma, n, m->moe, m->x, s);
+    // expert parallelism: this rank's experts' share of the MLP, then the
+    // ranks' shares summed into the residual like a row-parallel down_proj
+    ma.out = exch_slot_ptr(m, 1);
+    TRY(launch_moe(ma, n, m->moe, m->x, s));
+    return peer_exchange(m, 1, PEER_SUM, (size_t)n * d, m->x);
   }
   // 4) rmsnorm -> SwiGLU MLP (chat.py:284, 300-304)
   if (Ly.gu) {
@@ -955,10 +963,16 @@ int lumina_model_set_moe(lumina_model* m, int layer, int experts, int ie, int to
                        top_k <= MOE_MAX_K,
                    "model_set_moe: experts %d / ie %d / top_k %d outside 1..%d / >= 1 / 1..min(experts, %d)",
                    experts, ie, top_k, MOE_MAX_E, MOE_MAX_K);
+  // under tensor parallelism the experts are sharded: rank r holds the
+  // contiguous experts [r E / tp, (r + 1) E / tp)
+  const int tp = std::max(1, m->c.tp_size);
+  LUMINA_CHECK_ARG(experts % tp == 0, "model_set_moe: %d experts do not split over %d ranks", experts, tp);
   Layer& Ly = m->L[layer];
   Ly.moe_e = experts;
   Ly.moe_ie = ie;
   Ly.moe_k = top_k;
+  Ly.moe_e_n = experts / tp;
+  Ly.moe_e_lo = m->c.tp_rank * Ly.moe_e_n;
   return LUMINA_OK;
 }
 
@@ -1065,11 +1079,8 @@ int lumina_model_finalize(lumina_model* m) {
       return LUMINA_E_ARG;
     }
     if (moe) {
-      // virtual-MoE MLP: one GPU holds every expert (no expert parallelism)
-      if (c.tp_size > 1) {
-        set_error("model_finalize: virtual-MoE layer %d under tensor parallelism is not built", l);
-        return LUMINA_E_UNSUPPORTED;
-      }
+      // virtual-MoE MLP: under tensor parallelism each rank holds E / tp of
+      // the experts (lumina_model_set_moe) and the full router
       if (Ly.router_rows != Ly.moe_e || (Ly.router_b && Ly.router_blen != Ly.moe_e)) {
         set_error("model_finalize: layer %d router has %d rows / %d biases for %d experts", l, Ly.router_rows,
                   Ly.router_blen, Ly.moe_e);
@@ -1077,6 +1088,8 @@ int lumina_model_finalize(lumina_model* m) {
       }
       MoeLayerArgs ma{Ly.moe_gu, Ly.moe_down, Ly.router_w, Ly.router_b, Ly.post_norm, c.eps,
                       Ly.moe_e, Ly.moe_ie, Ly.moe_k, m->d};
+      ma.e_lo = Ly.moe_e_lo;
+      ma.e_n = Ly.moe_e_n;
       TRY(moe_check(ma));
       any_moe = true;
       moe_k = std::max(moe_k, Ly.moe_k);

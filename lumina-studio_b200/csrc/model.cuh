@@ -99,6 +99,10 @@ struct MoeLayerArgs {
   const float* norm_w;           // post-attention RMSNorm weight
   float eps;
   int E, Ie, K, d;
+  // expert parallelism: this rank holds experts [e_lo, e_lo + e_n) (rows of
+  // gate_up / down, in order); the router covers all E
+  int e_lo = 0, e_n = 0;
+  float* out = nullptr;  // null: x += MLP(x); else out = this rank's share of MLP(x)
 };
 struct MoeScratch {
   float* h;                 // (rows, d) normalized rows

@@ -178,8 +178,10 @@ struct PassPicks {
   int nt;
 };
 
+// Only this rank's experts [e_lo, e_lo + e_n) count as touched (all E
+// without expert parallelism).
 __device__ __forceinline__ void pass_picks(const float* __restrict__ score, int r0, int pr, int E, int K,
-                                           PassPicks& pp) {
+                                           int e_lo, int e_n, PassPicks& pp) {
   if (threadIdx.x == 0) {
     unsigned long long used = 0ull;
     for (int q = 0; q < pr; ++q) {
@@ -187,7 +189,7 @@ __device__ __forceinline__ void pass_picks(const float* __restrict__ score, int 
       for (int j = 0; j < K; ++j) used |= 1ull << pp.pick[q][j];
     }
     int nt = 0;
-    for (int e = 0; e < E; ++e)
+    for (int e = e_lo; e < e_lo + e_n; ++e)
       if ((used >> e) & 1ull) {
         for (int q = 0; q < MOE_ROWS; ++q) {
           signed char j = -1;
@@ -212,7 +214,7 @@ __device__ __forceinline__ void pass_picks(const float* __restrict__ score, int 
 template <typename ST, int PR>
 __global__ void __launch_bounds__(MOE_THREADS, PR == 1 ? 3 : 1)
 moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, const float* __restrict__ score,
-              int E, int K, int Ie, float* __restrict__ act) {
+              int E, int K, int Ie, int e_lo, int e_n, float* __restrict__ act) {
   extern __shared__ __align__(16) float sm[];
   // hsw: PR rows of h, 4 pad floats after every 32 (conflict-free 16-byte
   // reads when lanes take consecutive chunks); hsum: per row and chunk
@@ -228,7 +230,7 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
   for (int r0 = 0; r0 < n; r0 += PR) {
     const int rows = min(PR, n - r0);
     __syncthreads();  // the previous pass is done with pp / hsw
-    pass_picks(score, r0, rows, E, K, pp);
+    pass_picks(score, r0, rows, E, K, e_lo, e_n, pp);
     if ((int)blockIdx.x >= pp.nt) continue;
     const int e = pp.touched[blockIdx.x];
     int sl[PR];
@@ -253,7 +255,7 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
     }
     __syncthreads();
     if (i >= Ie) continue;
-    const int rg = e * 2 * Ie + i, ru = rg + Ie;
+    const int rg = (e - e_lo) * 2 * Ie + i, ru = rg + Ie;  // the rank's rows of expert e
     float ag[PR], au[PR];
 #pragma unroll
     for (int q = 0; q < PR; ++q) ag[q] = au[q] = 0.f;
@@ -329,8 +331,8 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
 template <typename ST, int PR>
 __global__ void __launch_bounds__(MOE_THREADS, PR == 1 ? 4 : 1)
 moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ score, int E, int K, int Ie,
-                const float* __restrict__ act, float* __restrict__ part, unsigned int* __restrict__ counters,
-                float* __restrict__ x) {
+                int e_lo, int e_n, const float* __restrict__ act, float* __restrict__ part,
+                unsigned int* __restrict__ counters, float* __restrict__ x, float* __restrict__ out) {
   __shared__ float red[MOE_WARPS][PR][64];
   __shared__ PassPicks pp;
   __shared__ int last;
@@ -352,14 +354,14 @@ moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ s
 #pragma unroll
       for (int t = 0; t < 8; ++t) acc[q][t] = 0.f;
     __syncthreads();  // the previous pass is done with pp / red
-    pass_picks(score, r0, rows, E, K, pp);
+    pass_picks(score, r0, rows, E, K, e_lo, e_n, pp);
     // (touched expert, neuron) pairs of this CTA's range, flattened so that
     // the loads of every touched expert are in flight together
     const int total = pp.nt * range;
 #pragma unroll 4
     for (int t = warp * 4 + rsub; t < total; t += 4 * MOE_WARPS) {
       const int xe = t / range, i = ib + (t - xe * range);
-      const int R = pp.touched[xe] * Ie + i;
+      const int R = (pp.touched[xe] - e_lo) * Ie + i;  // the rank's row of expert touched[xe]
       const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(w.codes + (size_t)R * w.row_bytes + coff));
       const float s = moe_scale<ST>(w, R, grp);
       float coef[PR];
@@ -410,7 +412,8 @@ moe_down_kernel(const lumina_weight w, int d, int n, const float* __restrict__ s
     const int r = idx >> 6, col = c0 + (idx & 63);
     float v = 0.f;
     for (int s2 = 0; s2 < S; ++s2) v += __ldcg(part + ((size_t)s2 * n + r) * d + col);
-    x[(size_t)r * d + col] += v;
+    if (out) out[(size_t)r * d + col] = v;  // this rank's share, summed over the ranks afterwards
+    else x[(size_t)r * d + col] += v;
   }
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
 }
@@ -431,9 +434,13 @@ int moe_check(const MoeLayerArgs& a) {
               a.Ie, MOE_MAX_E, MOE_MAX_K);
     return LUMINA_E_ARG;
   }
-  if (gu->rows != a.E * 2 * a.Ie || dn->rows != a.E * a.Ie || gu->cols != a.d || dn->cols != a.d) {
-    set_error("virtual-MoE layer: gate_up (%d, %d) / down (%d, %d) do not match E %d, ie %d, d %d", gu->rows,
-              gu->cols, dn->rows, dn->cols, a.E, a.Ie, a.d);
+  if (a.e_n < 1 || a.e_lo < 0 || a.e_lo + a.e_n > a.E) {
+    set_error("virtual-MoE layer: local experts [%d, %d) outside 0..%d", a.e_lo, a.e_lo + a.e_n, a.E);
+    return LUMINA_E_ARG;
+  }
+  if (gu->rows != a.e_n * 2 * a.Ie || dn->rows != a.e_n * a.Ie || gu->cols != a.d || dn->cols != a.d) {
+    set_error("virtual-MoE layer: gate_up (%d, %d) / down (%d, %d) do not match %d local experts, ie %d, d %d",
+              gu->rows, gu->cols, dn->rows, dn->cols, a.e_n, a.Ie, a.d);
     return LUMINA_E_ARG;
   }
   if (gu->bits != 4 || dn->bits != 4 || gu->mma || dn->mma || gu->group % 64 || dn->group % 64 ||
@@ -465,12 +472,14 @@ namespace {
 template <typename ST, int PR>
 int launch_experts(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
   // a pass of PR rows touches at most min(E, PR * K) experts
-  const dim3 ggu(std::min(a.E, PR * a.K), (a.Ie + MOE_PPC - 1) / MOE_PPC);
+  const dim3 ggu(std::min(a.e_n, PR * a.K), (a.Ie + MOE_PPC - 1) / MOE_PPC);
   LUMINA_CUDA_TRY(launch_pdl(moe_gu_kernel<ST, PR>, ggu, dim3(MOE_THREADS), gu_smem_bytes(a.d, PR), s, *a.gate_up,
-                             (const float*)sc.h, a.d, n, (const float*)sc.score, a.E, a.K, a.Ie, sc.act));
+                             (const float*)sc.h, a.d, n, (const float*)sc.score, a.E, a.K, a.Ie, a.e_lo, a.e_n,
+                             sc.act));
   const dim3 gdn(a.d / 64, moe_splits(n));
   LUMINA_CUDA_TRY(launch_pdl(moe_down_kernel<ST, PR>, gdn, dim3(MOE_THREADS), 0, s, *a.down, a.d, n,
-                             (const float*)sc.score, a.E, a.K, a.Ie, (const float*)sc.act, sc.part, sc.counters, x));
+                             (const float*)sc.score, a.E, a.K, a.Ie, a.e_lo, a.e_n, (const float*)sc.act, sc.part,
+                             sc.counters, x, a.out));
   return LUMINA_OK;
 }
 

@@ -298,8 +298,6 @@ class CudaChatModel:
                     obj._set_tensor(p + nm, recs[p + nm].data)
                 mlp = ("mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")
                 if l in moe:
-                    if tp_size > 1:
-                        raise LuminaError(4, f"layer {l}: virtual-MoE layers under tensor parallelism are not built")
                     mc = moe[l]
                     check(obj.lib.lumina_model_set_moe(obj.h, l, mc["experts"], mc["ie"], mc["top_k"]), obj.lib)
                     obj._set_tensor(p + "mlp.gate.weight", recs[p + "mlp.gate.weight"].data)
@@ -309,6 +307,8 @@ class CudaChatModel:
                         rec = recs[p + nm]
                         if rec.kind == "raw":
                             raise LuminaError(3, f"{p + nm} is stored raw; only packed experts are built")
+                        if not presharded:  # expert parallelism: this rank's experts
+                            rec = sharding.expert_shard(rec, mc["experts"], tp_rank, tp_size)
                         obj._set_weight(p + nm, upload_record(rec, device))
                     mlp = ()
                 for nm in ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",

@@ -6,6 +6,8 @@ slices, lm_head by vocab. Row-parallel (columns split at scale-group
 boundaries, so no group is ever cut): o by heads, down by the same FFN
 slices as gate/up. When the FFN group count does not divide by the TP size
 (11008 / 64 = 172 groups at TP 8) the first ranks take one group more.
+Virtual-MoE layers split by experts (expert parallelism): each rank keeps
+E/tp whole experts of gate_up and down and the whole router.
 """
 from __future__ import annotations
 
@@ -65,6 +67,21 @@ def shard_record(rec: Record, what: str, rank: int, tp: int, head_dim: int) -> R
         c0, c1 = ffn_bounds(cols, rec.group, rank, tp)
         return _cols(rec, c0, c1)
     raise ValueError("no shard rule for " + what)
+
+
+def expert_shard(rec: Record, experts: int, rank: int, tp: int) -> Record:
+    """Expert parallelism for a virtual-MoE layer: rank r keeps the rows of
+    experts [r E/tp, (r+1) E/tp) of the flat experts.gate_up_proj (E*2Ie
+    rows) or experts.down_proj (E*Ie rows); the router stays whole."""
+    if tp <= 1:
+        return rec
+    if experts % tp:
+        raise ValueError(f"{rec.name}: {experts} experts do not split over {tp} ranks")
+    rows = rec.shape[0]
+    if rows % experts:
+        raise ValueError(f"{rec.name}: {rows} rows are not {experts} experts")
+    per = rows // experts * (experts // tp)
+    return _rows(rec, rank * per, (rank + 1) * per)
 
 
 def vocab_shard(head: np.ndarray, rank: int, tp: int) -> np.ndarray:

@@ -3,7 +3,8 @@
 ``write_tp_shards`` reads a `.lumina` model once and writes, for each of
 ``tp`` ranks, a `.lumina` file holding only that rank's slice of every
 projection (the column / row split of ``sharding.shard_record``, packed codes
-copied as stored, never dequantized), its vocab slice of ``lm_head``, and the
+copied as stored, never dequantized), its experts of every virtual-MoE layer
+(``sharding.expert_shard``), its vocab slice of ``lm_head``, and the
 replicated raw tensors (embedding, norms, routers). The header carries
 ``"tp_shard": {"rank": r, "size": tp}``; ``CudaChatModel.from_lumina`` then
 loads the file as that rank's shard without slicing again, so each rank reads
@@ -61,6 +62,8 @@ def write_tp_shards(path: str, tp: int, head_dim: int, out_dir: str) -> list[str
     out = []
     with LuminaFile(path) as f:
         names = f.names()
+        from .engine import moe_map_from_header
+        moe = moe_map_from_header(f.header)  # virtual-MoE layers split by experts
         for r in range(tp):
             header = {k: v for k, v in f.header.items() if k not in ("tensors", "matrices")}
             header["matrices"] = []
@@ -71,6 +74,9 @@ def write_tp_shards(path: str, tp: int, head_dim: int, out_dir: str) -> list[str
                 part = _layer_part(n)
                 if rec.kind != "raw" and part in _SHARDED:
                     rec = sharding.shard_record(rec, part, r, tp, head_dim)
+                elif rec.kind != "raw" and part in ("mlp.experts.gate_up_proj", "mlp.experts.down_proj"):
+                    layer = int(n.split(".")[2])
+                    rec = sharding.expert_shard(rec, moe[layer]["experts"], r, tp)
                 elif rec.kind == "raw" and n == "lm_head.weight":
                     rec = Record(n, "raw", rec.shape, data=sharding.vocab_shard(np.asarray(rec.data), r, tp))
                 e, b = _entry(rec, f.tensors[n], off)

@@ -158,3 +158,45 @@ def test_tp4_matches_reference(tiny_file, tmp_path):
     finally:
         m.close()
     assert list(res[0]["greedy"]) == greedy
+
+
+def test_tp2_moe_expert_parallel_matches_reference(tiny_moe_file, tmp_path):
+    """Virtual-MoE layers under tensor parallelism (expert parallelism): two
+    ranks, 4 of the 8 experts each, the router on both, the ranks' shares of
+    every routed MLP summed over peer memory. The reference's recorded
+    logits of the MoE model within the bar (tests/golden/tiny_moe.npz), and
+    on both ranks the greedy tokens of the one-GPU MoE model."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    golden = os.path.join(GOLDEN, "tiny_moe.npz")
+    out = str(tmp_path / "tp_moe")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", f"--master-port={port}",
+                        os.path.join(REPO, "tests", "tp_worker.py"), tiny_moe_file, golden, out],
+                       env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    g = np.load(golden)
+    res = [np.load(f"{out}.rank{k}.npz") for k in range(2)]
+    for k in range(2):
+        assert rel_l2(res[k]["prefill"], g["logits_prefill_last"]) < REL_L2
+        assert rel_l2(res[k]["step0"], g["logits_step0"]) < REL_L2
+    assert np.array_equal(res[0]["greedy"], res[1]["greedy"])
+    from lumina_b200.engine import CudaChatModel
+    m = CudaChatModel.from_lumina(tiny_moe_file, synthetic.hf_cfg(synthetic.TINY), StubTok(),
+                                  theta=synthetic.TINY["rope_theta"], max_seq=512, max_rows=128)
+    try:
+        prompt = [int(t) for t in g["prompt"]]
+        m.forward(prompt, 0)
+        for tk in g["forced"][:4]:
+            m.decode_step(int(tk), want_logits=False)
+        m.kv_truncate(len(prompt))
+        greedy = m.decode_greedy(int(g["forced"][0]), 24)
+    finally:
+        m.close()
+    assert list(res[0]["greedy"]) == greedy

@@ -134,3 +134,73 @@ def test_shard_files_hold_each_ranks_slice(tiny_file, tmp_path):
                         w = sharding.shard_record(a, part, r, tp, 64) if part in _SHARDED else a
                         assert (b.kind, b.shape, b.group, b.pack) == (w.kind, w.shape, w.group, w.pack), n
                         assert np.array_equal(b.codes, w.codes) and np.array_equal(b.scales, w.scales), n
+
+
+def test_expert_shards_sum_to_the_routed_mlp(tiny_moe_file):
+    """Expert parallelism (sharding.expert_shard): at TP 2 and 4 each rank
+    keeps E/tp whole experts of gate_up and down; the ranks' shares of the
+    routed MLP (the top-k experts a rank holds, others contributing zero)
+    add up to the full routed MLP of the oracle for a random normalized
+    row, and the shard rows concatenate to the full records."""
+    from lumina_b200.engine import moe_map_from_header
+    rng = np.random.default_rng(7)
+    with LuminaFile(tiny_moe_file) as f:
+        mm = moe_map_from_header(f.header)[0]
+        E, ie, K = mm["experts"], mm["ie"], mm["top_k"]
+        gu = f.record("model.layers.0.mlp.experts.gate_up_proj")
+        dn = f.record("model.layers.0.mlp.experts.down_proj")
+        router = np.asarray(f.record("model.layers.0.mlp.gate.weight").data, np.float64)
+    h = rng.standard_normal(gu.shape[1])
+    score = 1.0 / (1.0 + np.exp(-(router @ h)))
+    picks = np.argsort(-score)[:K]
+
+    def mlp_share(gu_w, dn_w, experts):
+        y = np.zeros(dn_w.shape[1])
+        for j, e in enumerate(experts):
+            if e not in picks:
+                continue
+            g = gu_w[2 * ie * j:2 * ie * j + ie] @ h
+            u = gu_w[2 * ie * j + ie:2 * ie * (j + 1)] @ h
+            a = g / (1.0 + np.exp(-np.clip(g, -40, 40))) * u
+            y += dn_w[ie * j:ie * (j + 1)].T @ a
+        return y
+
+    full = mlp_share(_deq(gu).astype(np.float64), _deq(dn).astype(np.float64), list(range(E)))
+    for tp in (2, 4):
+        parts, rows_gu, rows_dn = [], [], []
+        for r in range(tp):
+            g_r = sharding.expert_shard(gu, E, r, tp)
+            d_r = sharding.expert_shard(dn, E, r, tp)
+            assert g_r.shape == (E // tp * 2 * ie, gu.shape[1]) and d_r.shape == (E // tp * ie, dn.shape[1])
+            rows_gu.append(_deq(g_r))
+            rows_dn.append(_deq(d_r))
+            parts.append(mlp_share(rows_gu[-1].astype(np.float64), rows_dn[-1].astype(np.float64),
+                                   list(range(r * E // tp, (r + 1) * E // tp))))
+        assert np.array_equal(np.concatenate(rows_gu), _deq(gu))
+        assert np.array_equal(np.concatenate(rows_dn), _deq(dn))
+        np.testing.assert_allclose(sum(parts), full, rtol=1e-12, atol=1e-12)
+    with pytest.raises(ValueError, match="do not split"):
+        sharding.expert_shard(gu, E, 0, 3)
+
+
+def test_shard_files_hold_each_ranks_experts(tiny_moe_file, tmp_path):
+    """write_tp_shards on a virtual-MoE model: each rank's file holds its
+    experts' rows of gate_up and down (expert_shard), the whole router, and
+    the virtual_moe header map the loader reads."""
+    from lumina_b200.engine import moe_map_from_header
+    from lumina_b200.shards import write_tp_shards
+    paths = write_tp_shards(tiny_moe_file, 2, HD, str(tmp_path / "moe_tp2"))
+    with LuminaFile(tiny_moe_file) as full:
+        moe = moe_map_from_header(full.header)
+        for r, p in enumerate(paths):
+            with LuminaFile(p) as f:
+                assert moe_map_from_header(f.header) == moe
+                for l, mm in moe.items():
+                    for nm in ("mlp.experts.gate_up_proj", "mlp.experts.down_proj"):
+                        n = f"model.layers.{l}.{nm}"
+                        w = sharding.expert_shard(full.record(n), mm["experts"], r, 2)
+                        b = f.record(n)
+                        assert b.shape == w.shape and np.array_equal(b.codes, w.codes), n
+                        assert np.array_equal(b.scales, w.scales), n
+                    n = f"model.layers.{l}.mlp.gate.weight"
+                    assert np.array_equal(f.record(n).data, full.record(n).data)
