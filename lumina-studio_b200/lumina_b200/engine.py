@@ -474,7 +474,14 @@ def make_pick(temperature=0.0, top_p=1.0, top_k=0, min_p=0.0, typical_p=1.0, rep
     def greedy_only():
         return temperature <= 0 and top_k <= 1 and min_p <= 0 and typical_p >= 1.0 and repeat_penalty == 1.0
 
+    fast_greedy = greedy_only()
+
     def pick(lg, seen):
+        if fast_greedy:
+            # no penalty and no sampling: the argmax of the logits as given
+            # (widening to float64 first, as below, is exact and keeps the
+            # order, so the first maximum is the same index)
+            return int(np.argmax(lg))
         lg = np.asarray(lg, dtype=np.float64)
         if repeat_penalty != 1.0 and seen:
             lg = lg.copy()
