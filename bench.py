@@ -44,6 +44,9 @@ prompt, 128 greedy tokens) on the device and the reference's algorithm on
 the host.
 ``--verify`` times the EAGLE tree verification of a 32-node draft tree over a
 4096-token prompt, and the prefill of that prompt.
+``--shared-prefix`` decodes 8 sequences over one 2048-token shared prefix
+(with ``--moe`` the virtual-MoE shape; ``--gpus N`` TP attention and
+expert-parallel experts).
 ``--sweep`` prints one line per case of the decode-only GEMV sweep (int4 /
 int3 / int2 / binary x the four 7B projection shapes x batch 1, 4, 16).
 """
@@ -514,6 +517,78 @@ def run_verify(args):
     return 0
 
 
+SHARED_PREFIX, SHARED_SEQS, SHARED_SUFFIX, SHARED_TOKENS = 2048, 8, 16, 128
+
+
+def run_shared(args, cfg):
+    """Several sequences over a shared prefix on the 7B shape (the virtual-
+    MoE variant with --moe): a 2048-token random prefix prefilled once,
+    8 sequences that add 16 random tokens each, then 128 greedy tokens per
+    sequence through engine.generate_shared_prefix (one forward of the
+    live sequences per step; attention over the shared cache with a
+    per-sequence bias). With --gpus N the attention is tensor-parallel and
+    the experts expert-parallel. Wall clock around the synchronous decode
+    steps (logits of every row to the host included), max over ranks; the
+    prefix prefill is reported beside it. Prints one JSON line."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from lumina_b200 import synthetic
+    from lumina_b200.engine import CudaChatModel, generate_shared_prefix
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
+    moe = (MOE_EXPERTS, MOE_TOP_K) if args.moe else None
+    recs = synthetic.QuantizedRecords(cfg, bits=4, group=64, seed=0, device=local, moe=moe)
+    max_seq = SHARED_PREFIX + SHARED_SEQS * (SHARED_SUFFIX + SHARED_TOKENS) + 64
+    model = CudaChatModel._from_records(recs, synthetic.hf_cfg(cfg), None, 32, 32, 1e-6, 1e4, local, True,
+                                        max_seq, 512, 16, rank, world, moe_map=recs.moe_map)
+    model.init_tp()
+    try:
+        rng = np.random.default_rng(3)
+        prefix = synthetic.prompt_ids(cfg, SHARED_PREFIX, seed=2)
+        sfx = [[int(t) for t in rng.integers(0, cfg["vocab_size"], SHARED_SUFFIX)] for _ in range(SHARED_SEQS)]
+        generate_shared_prefix(model, prefix[:256], sfx, max_tokens=4)  # warm every kernel shape
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.kv_truncate(0)
+        model.forward(prefix, 0)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        res = generate_shared_prefix(model, prefix, sfx, max_tokens=SHARED_TOKENS, timed=True)
+        dt = res["decode_s"]
+        if world > 1:
+            t = torch.tensor([dt, prefill_s], dtype=torch.float64, device=f"cuda:{local}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt, prefill_s = float(t[0]), float(t[1])
+        decoded = sum(len(t) - 1 for t in res["tokens"])  # tokens the timed decode steps produced
+        if rank == 0:
+            mlp = (f"virtual-MoE ({MOE_EXPERTS} experts of {cfg['intermediate_size'] // MOE_EXPERTS}, "
+                   f"top-{MOE_TOP_K})" if args.moe else "dense")
+            print(json.dumps({
+                "bench": "shared_prefix_batch",
+                "workload": f"llama2-7b-shape {mlp} int4 g64, fp16 KV, {SHARED_SEQS} sequences over a "
+                            f"{SHARED_PREFIX}-token shared prefix + {SHARED_SUFFIX} own tokens, "
+                            f"{SHARED_TOKENS} greedy tokens each",
+                "n_gpus": world,
+                "parallelism": f"tp{world}" + (f" attention, ep{world} experts" if args.moe and world > 1 else ""),
+                "decode_tokens_per_s": decoded / dt, "ms_per_step": dt / max(1, res["steps"]) * 1e3,
+                "steps": res["steps"], "sequences": SHARED_SEQS,
+                "prefix_prefill_tokens_per_s": SHARED_PREFIX / prefill_s, "prefix_prefill_s": prefill_s,
+                "timing": "wall clock around synchronous engine calls (bias build, every row's logits to the "
+                          "host included), max over ranks"}), flush=True)
+    finally:
+        model.close()
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--sweep", action="store_true",
@@ -528,6 +603,9 @@ def main(argv=None):
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (development only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shared-prefix", action="store_true",
+                    help="8 sequences over a 2048-token shared prefix, 128 greedy tokens each (with --moe: "
+                         "the virtual-MoE shape; --gpus N: TP attention, expert-parallel experts)")
     ap.add_argument("--moe", action="store_true",
                     help="the virtual-MoE 7B shape (8 experts x 1376, top-2) instead of the dense model")
     args = ap.parse_args(argv)
@@ -543,6 +621,8 @@ def main(argv=None):
         return run_sweep(args)
     if args.verify:
         return run_verify(args)
+    if args.shared_prefix:
+        return run_shared(args, cfg)
     if args.tiny:
         return run_tiny(args)
 

@@ -261,7 +261,11 @@ int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int po
  * 379-402) with the head GEMV of :388 (no final norm). With
  * pos_override_host (n positions) and bias_host ((n, len+n) additive, 0 /
  * -inf) it is the tree-verification forward of eagle.verify_tree
- * (eagle.py:259-291); both may be NULL. */
+ * (eagle.py:259-291); both may be NULL. A key is visible to a row when its
+ * position (a cached key's: its row index) is not past the row's, as in
+ * chat.py:264-274; a positive bias entry, which the reference never
+ * passes, admits the key whatever its position (several sequences sharing
+ * one cache: engine.generate_shared_prefix). */
 int lumina_forward(lumina_model* m, const int* tokens_host, int n, int pos0,
                    const int* pos_override_host, const float* bias_host,
                    float* logits_host, int all_rows);

@@ -3,7 +3,9 @@
 // j visible to row r iff its position (j itself for a cached key, else the
 // position of the input row it came from) is <= row r's position, plus
 // min(0, bias[r, j]) when a bias is given (the tree ancestry mask of
-// eagle.py:259-291), softmax over the keys, times V.
+// eagle.py:259-291), softmax over the keys, times V. A positive bias entry
+// (which the reference never passes) admits the key whatever its position:
+// several sequences sharing one cache, whose rows sit side by side.
 //
 // One CTA per (head, block of AR_BR = 64 query rows), four warps of 16 rows
 // each. The CTA streams the keys in tiles of AR_BC = 64 through shared
@@ -271,10 +273,14 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
           const int j = 8 * nt + 2 * t + (e & 1);
           const bool rowb = e >= 2;
           const int rp = rowb ? pb : pa;
+          // a positive bias admits the key whatever its position (rows of
+          // one sequence among several sharing the cache); otherwise the
+          // position rule and min(0, bias) as the reference applies them
+          const float bv = bias ? bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j] : 0.f;
           float v = -INFINITY;
-          if (rp >= 0 && kp[j] <= rp) {
+          if (rp >= 0 && (kp[j] <= rp || bv > 0.f)) {
             v = __fdiv_rn(s[nt][e], sdiv);
-            if (bias) v += fminf(0.f, bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j]);
+            v += fminf(0.f, bv);
           }
           s[nt][e] = v;
           if (rowb) mxb = fmaxf(mxb, v); else mxa = fmaxf(mxa, v);

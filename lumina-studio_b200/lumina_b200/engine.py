@@ -785,3 +785,88 @@ def commit_verified(model: CudaChatModel, pos: int, toks, parents, depths, cur_l
     pos += len(path)
     lg = model.forward([accepted[-1]], pos)[0]
     return False, pos + 1, lg, accepted[-1]
+
+
+# ---------------------------------------------------------------------------
+# several sequences over one shared prefix (no reference counterpart: the
+# reference serves one sequence per generate call and reuses a prefix
+# through its prefix cache, chat.py:418-551)
+# ---------------------------------------------------------------------------
+def generate_shared_prefix(model: CudaChatModel, prefix_ids, suffixes, max_tokens: int = 32,
+                           stop_ids: tuple = (), timed: bool = False):
+    """Greedy decode of B sequences ``prefix_ids + suffixes[b]`` that share
+    the prefix's KV rows on the device. The prefix is prefilled once; the
+    suffixes go in forwards of up to 64 rows, and every decode step is one
+    forward of the B (<= 64) live sequences' rows. Rows of all sequences live in the one KV cache
+    side by side; each row attends to the prefix and to its own sequence's
+    rows only (an additive -inf bias on the others, the tree-verification
+    forward of ``verify_tree``) at its own true position, so sequence b sees
+    exactly what ``generate(prefix + suffixes[b])`` would.
+
+    Returns ``{"tokens": [list per sequence], "first_logits": (B, vocab)}``
+    (the logits after each full prompt); with ``timed`` also the wall time of
+    the decode steps ("decode_s") and the number of steps."""
+    prefix = [int(t) for t in prefix_ids]
+    sfx = [[int(t) for t in s] for s in suffixes]
+    B = len(sfx)
+    if B < 1 or any(len(s) < 1 for s in sfx) or not prefix:
+        raise LuminaError(1, "generate_shared_prefix: a non-empty prefix and non-empty suffixes are needed")
+    chunk = min(64, model.max_rows)  # rows of one biased forward (the library's bias buffer holds 64)
+    if B > chunk:
+        raise LuminaError(1, "generate_shared_prefix: %d sequences, at most %d" % (B, chunk))
+    P = len(prefix)
+    model.kv_truncate(0)
+    model.forward(prefix, 0)
+    rows = [[] for _ in range(B)]  # KV rows of each sequence after the prefix
+    pos = [P] * B                  # next position of each sequence
+
+    def step(toks_per_seq, live):
+        """One forward of the given rows: live[i] is the sequence of row i.
+        A row admits the prefix, its sequence's cached rows (bias +1: their
+        cache index can exceed the row's position) and its sequence's rows
+        of this forward up to itself; every other key gets -inf."""
+        T = model.kv_length()
+        n = len(live)
+        bias = np.full((n, T + n), -np.inf, dtype=np.float32)
+        bias[:, :P] = 0.0
+        po = np.empty(n, np.int32)
+        for i, b in enumerate(live):
+            if rows[b]:
+                bias[i, rows[b]] = 1.0
+        for i, b in enumerate(live):
+            rows[b].append(T + i)
+            po[i] = pos[b]
+            pos[b] += 1
+            bias[i, [T + j for j in range(i + 1) if live[j] == b]] = 0.0
+        return model.forward(list(toks_per_seq), T, all_rows=True, pos_override=po, attn_bias=bias)
+
+    # the suffixes: forwards of up to `chunk` rows, causal within a suffix
+    # (a later chunk sees its sequences' earlier rows as cached rows)
+    live = [b for b in range(B) for _ in sfx[b]]
+    toks = [t for b in range(B) for t in sfx[b]]
+    lg = np.concatenate([step(toks[c:c + chunk], live[c:c + chunk]) for c in range(0, len(toks), chunk)])
+    ends = np.cumsum([len(s) for s in sfx]) - 1
+    first_logits = lg[ends].copy()
+    nxt = [int(np.argmax(first_logits[b])) for b in range(B)]
+    out = [[] for _ in range(B)]
+    done = [False] * B
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        for b in range(B):
+            if not done[b]:
+                out[b].append(nxt[b])
+                if nxt[b] in stop_ids or len(out[b]) >= max_tokens:
+                    done[b] = True
+        live = [b for b in range(B) if not done[b]]
+        if not live:
+            break
+        lg = step([nxt[b] for b in live], live)
+        steps += 1
+        for i, b in enumerate(live):
+            nxt[b] = int(np.argmax(lg[i]))
+    res = {"tokens": out, "first_logits": first_logits}
+    if timed:
+        res["decode_s"] = time.perf_counter() - t0
+        res["steps"] = steps
+    return res
