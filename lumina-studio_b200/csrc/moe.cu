@@ -30,11 +30,13 @@
 //    lower expert index (numpy's sort is not stable, so the reference orders
 //    exact ties by its sort algorithm; both pick the same score values), and
 //    the distinct experts the pass touches.
-//  * moe_gu_kernel, grid (touched-expert slot, tile of MOE_PPC neuron pairs):
-//    CTA x works for the x-th expert the pass touches, so only touched
-//    experts stream from HBM and, at decode, every CTA has work. One warp
-//    per (gate, up) row pair, each lane a 16-byte chunk (32 codes) per row;
-//    the codes are widened to fp32 once and dotted against every picking row
+//  * moe_gu_kernel, grid (touched-expert slot, tile of neuron pairs): CTA x
+//    works for the x-th expert the pass touches, so only touched experts
+//    stream from HBM and, at decode, every CTA has work. A tile is MOE_PPC
+//    pairs at decode and 8 x MOE_PPC for passes of several rows (the rows
+//    are staged once per CTA). One warp per (gate, up) row pair at a time,
+//    each lane a 16-byte chunk (32 codes) per row; the codes are widened to
+//    fp32 once and dotted against every picking row
 //    held in shared memory:
 //      sum_k h_k * level(c_k) = s/15 * (2 * sum h_k c_k - 15 * sum h_k)
 //    per 32-column chunk (one scale; level(c) = (2c - 15)/15,
@@ -214,7 +216,7 @@ __device__ __forceinline__ void pass_picks(const float* __restrict__ score, int 
 template <typename ST, int PR>
 __global__ void __launch_bounds__(MOE_THREADS, PR == 1 ? 3 : 1)
 moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, const float* __restrict__ score,
-              int E, int K, int Ie, int e_lo, int e_n, float* __restrict__ act) {
+              int E, int K, int Ie, int e_lo, int e_n, int ppw, float* __restrict__ act) {
   extern __shared__ __align__(16) float sm[];
   // hsw: PR rows of h, 4 pad floats after every 32 (conflict-free 16-byte
   // reads when lanes take consecutive chunks); hsum: per row and chunk
@@ -223,7 +225,9 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
   float* hsum = sm + PR * ldh;
   __shared__ PassPicks pp;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int i = blockIdx.y * MOE_PPC + warp;  // this warp's neuron pair
+  // this CTA's neuron pairs: ppw rounds of MOE_PPC (one per warp); several
+  // rounds let a CTA stage a pass's rows once for many pairs
+  const int i0 = blockIdx.y * MOE_PPC * ppw + warp;
   // everything below reads the router's outputs (scores, h)
   pdl_launch_dependents();
   pdl_wait();
@@ -254,73 +258,76 @@ moe_gu_kernel(const lumina_weight w, const float* __restrict__ h, int d, int n, 
       if (lane == 0) hsum[q * nch + c] = v;
     }
     __syncthreads();
-    if (i >= Ie) continue;
-    const int rg = (e - e_lo) * 2 * Ie + i, ru = rg + Ie;  // the rank's rows of expert e
-    float ag[PR], au[PR];
+    for (int rr = 0; rr < ppw; ++rr) {
+      const int i = i0 + rr * MOE_PPC;  // this warp's neuron pair of round rr
+      if (i >= Ie) break;
+      const int rg = (e - e_lo) * 2 * Ie + i, ru = rg + Ie;  // the rank's rows of expert e
+      float ag[PR], au[PR];
 #pragma unroll
-    for (int q = 0; q < PR; ++q) ag[q] = au[q] = 0.f;
-    for (int cb = 0; cb < nch; cb += 128) {
-      uint4 wg[4], wu[4];
+      for (int q = 0; q < PR; ++q) ag[q] = au[q] = 0.f;
+      for (int cb = 0; cb < nch; cb += 128) {
+        uint4 wg[4], wu[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = cb + u * 32 + lane;
-        if (c < nch) {
-          wg[u] = ldg_stream(w.codes + code_offset(w, rg, c));
-          wu[u] = ldg_stream(w.codes + code_offset(w, ru, c));
+        for (int u = 0; u < 4; ++u) {
+          const int c = cb + u * 32 + lane;
+          if (c < nch) {
+            wg[u] = ldg_stream(w.codes + code_offset(w, rg, c));
+            wu[u] = ldg_stream(w.codes + code_offset(w, ru, c));
+          }
         }
-      }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = cb + u * 32 + lane;
-        if (c >= nch) continue;
-        const int grp = (c << 5) / w.group;
-        const float sg = moe_scale<ST>(w, rg, grp), su = moe_scale<ST>(w, ru, grp);
-        const uint32_t gw[4] = {wg[u].x, wg[u].y, wg[u].z, wg[u].w};
-        const uint32_t uw[4] = {wu[u].x, wu[u].y, wu[u].z, wu[u].w};
-        float dg[PR], du[PR];
+        for (int u = 0; u < 4; ++u) {
+          const int c = cb + u * 32 + lane;
+          if (c >= nch) continue;
+          const int grp = (c << 5) / w.group;
+          const float sg = moe_scale<ST>(w, rg, grp), su = moe_scale<ST>(w, ru, grp);
+          const uint32_t gw[4] = {wg[u].x, wg[u].y, wg[u].z, wg[u].w};
+          const uint32_t uw[4] = {wu[u].x, wu[u].y, wu[u].z, wu[u].w};
+          float dg[PR], du[PR];
 #pragma unroll
-        for (int q = 0; q < PR; ++q) dg[q] = du[q] = 0.f;
+          for (int q = 0; q < PR; ++q) dg[q] = du[q] = 0.f;
 #pragma unroll
-        for (int qw = 0; qw < 4; ++qw) {
-          // word qw = columns 8qw .. 8qw+7: low nibbles even, high nibbles odd
-          const uint32_t glo = gw[qw] & 0x0F0F0F0Fu, ghi = (gw[qw] >> 4) & 0x0F0F0F0Fu;
-          const uint32_t ulo = uw[qw] & 0x0F0F0F0Fu, uhi = (uw[qw] >> 4) & 0x0F0F0F0Fu;
-          float cg[8], cu[8];
+          for (int qw = 0; qw < 4; ++qw) {
+            // word qw = columns 8qw .. 8qw+7: low nibbles even, high nibbles odd
+            const uint32_t glo = gw[qw] & 0x0F0F0F0Fu, ghi = (gw[qw] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t ulo = uw[qw] & 0x0F0F0F0Fu, uhi = (uw[qw] >> 4) & 0x0F0F0F0Fu;
+            float cg[8], cu[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            cg[2 * j] = byte_to_float(glo, j);
-            cg[2 * j + 1] = byte_to_float(ghi, j);
-            cu[2 * j] = byte_to_float(ulo, j);
-            cu[2 * j + 1] = byte_to_float(uhi, j);
+            for (int j = 0; j < 4; ++j) {
+              cg[2 * j] = byte_to_float(glo, j);
+              cg[2 * j + 1] = byte_to_float(ghi, j);
+              cu[2 * j] = byte_to_float(ulo, j);
+              cu[2 * j + 1] = byte_to_float(uhi, j);
+            }
+#pragma unroll
+            for (int q = 0; q < PR; ++q) {
+              if (sl[q] < 0) continue;
+              const float* hv = hsw + q * ldh + c * 36 + 8 * qw;
+              const float4 h0 = *reinterpret_cast<const float4*>(hv);
+              const float4 h1 = *reinterpret_cast<const float4*>(hv + 4);
+              const float hh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                dg[q] = fmaf(hh[t], cg[t], dg[q]);
+                du[q] = fmaf(hh[t], cu[t], du[q]);
+              }
+            }
           }
 #pragma unroll
           for (int q = 0; q < PR; ++q) {
             if (sl[q] < 0) continue;
-            const float* hv = hsw + q * ldh + c * 36 + 8 * qw;
-            const float4 h0 = *reinterpret_cast<const float4*>(hv);
-            const float4 h1 = *reinterpret_cast<const float4*>(hv + 4);
-            const float hh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              dg[q] = fmaf(hh[t], cg[t], dg[q]);
-              du[q] = fmaf(hh[t], cu[t], du[q]);
-            }
+            const float m15 = -15.f * hsum[q * nch + c];
+            ag[q] = fmaf(sg, fmaf(2.f, dg[q], m15), ag[q]);
+            au[q] = fmaf(su, fmaf(2.f, du[q], m15), au[q]);
           }
         }
-#pragma unroll
-        for (int q = 0; q < PR; ++q) {
-          if (sl[q] < 0) continue;
-          const float m15 = -15.f * hsum[q * nch + c];
-          ag[q] = fmaf(sg, fmaf(2.f, dg[q], m15), ag[q]);
-          au[q] = fmaf(su, fmaf(2.f, du[q], m15), au[q]);
-        }
       }
-    }
 #pragma unroll
-    for (int q = 0; q < PR; ++q) {
-      if (sl[q] < 0) continue;
-      const float g = warp_sum(ag[q]) / 15.f, u = warp_sum(au[q]) / 15.f;
-      if (lane == 0) act[((size_t)(r0 + q) * K + sl[q]) * Ie + i] = silu_mul(g, u);
+      for (int q = 0; q < PR; ++q) {
+        if (sl[q] < 0) continue;
+        const float g = warp_sum(ag[q]) / 15.f, u = warp_sum(au[q]) / 15.f;
+        if (lane == 0) act[((size_t)(r0 + q) * K + sl[q]) * Ie + i] = silu_mul(g, u);
+      }
     }
   }
 }
@@ -472,9 +479,13 @@ namespace {
 template <typename ST, int PR>
 int launch_experts(const MoeLayerArgs& a, int n, const MoeScratch& sc, float* x, cudaStream_t s) {
   // a pass of PR rows touches at most min(E, PR * K) experts
-  const dim3 ggu(std::min(a.e_n, PR * a.K), (a.Ie + MOE_PPC - 1) / MOE_PPC);
+  // one round of MOE_PPC neuron pairs per CTA for a decode row (several
+  // small CTAs per SM); 8 rounds for passes of several rows, so a CTA stages
+  // the pass's rows once for 64 pairs
+  const int ppw = PR == 1 ? 1 : 8;
+  const dim3 ggu(std::min(a.e_n, PR * a.K), (a.Ie + MOE_PPC * ppw - 1) / (MOE_PPC * ppw));
   LUMINA_CUDA_TRY(launch_pdl(moe_gu_kernel<ST, PR>, ggu, dim3(MOE_THREADS), gu_smem_bytes(a.d, PR), s, *a.gate_up,
-                             (const float*)sc.h, a.d, n, (const float*)sc.score, a.E, a.K, a.Ie, a.e_lo, a.e_n,
+                             (const float*)sc.h, a.d, n, (const float*)sc.score, a.E, a.K, a.Ie, a.e_lo, a.e_n, ppw,
                              sc.act));
   const dim3 gdn(a.d / 64, moe_splits(n));
   LUMINA_CUDA_TRY(launch_pdl(moe_down_kernel<ST, PR>, gdn, dim3(MOE_THREADS), 0, s, *a.down, a.d, n,
