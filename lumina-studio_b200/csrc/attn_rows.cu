@@ -8,7 +8,8 @@
 // several sequences sharing one cache, whose rows sit side by side.
 //
 // One CTA per (head, block of AR_BR = 64 query rows), four warps of 16 rows
-// each. The CTA streams the keys in tiles of AR_BC = 64 through shared
+// each (with 16 or 32 rows in all, the warps split each key tile instead:
+// the key groups of attn_rows_kernel's G). The CTA streams the keys in tiles of AR_BC = 64 through shared
 // memory (double-buffered; fp16 cache rows by cp.async, fp32 cache rows
 // converted to fp16 on the way), so every K/V row is read once per 64 query
 // rows. Each warp computes its 16 x 64 score tile with mma.sync m16n8k16
@@ -86,7 +87,12 @@ __device__ __forceinline__ uint32_t pack_hl(float a, float b, uint32_t& lo) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int HD, typename KT>
+// G key groups: with few rows (G = 4: up to 16 rows, G = 2: up to 32) warp
+// w takes rows 16 (w % RW) .. + 15 of the block and keys (w / RW) KPW ..
+// + KPW - 1 of every tile, RW = 4 / G, KPW = 64 / G, so every warp has
+// work; the G per-warp softmax states of a row merge in shared memory in
+// key-group order after the key loop. G = 1 is the one-group kernel.
+template <int HD, typename KT, int G>
 __global__ void __launch_bounds__(AR_THREADS, AR_CTAS_PER_SM)
 attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restrict__ kcache,
                  const KT* __restrict__ vcache, const int* __restrict__ block_table, int bs,
@@ -95,8 +101,11 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   using C = ArCfg<HD>;
   constexpr int NKK = HD / 16;  // k-steps of q.K^T
   constexpr int NDT = HD / 8;   // n-tiles of P.V
+  constexpr int RW = 4 / G;     // row warps
+  constexpr int KPW = AR_BC / G, NTW = KPW / 8, NPW = KPW / 16;  // a warp's keys, n-tiles, 16-key steps
   const int h = blockIdx.x, r0 = blockIdx.y * AR_BR;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rw = warp % RW, kg = warp / RW;  // row warp, key group
   const int g = lane >> 2, t = lane & 3;
   pdl_launch_dependents();
   pdl_wait();
@@ -205,13 +214,13 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     *reinterpret_cast<uint2*>(Qs + rr * C::ROW + c4 * 8) = make_uint2(h0, h1);
     *reinterpret_cast<uint2*>(Ql + rr * C::ROW + c4 * 8) = make_uint2(l0, l1);
   }
-  const int ra = r0 + 16 * warp + g, rb = ra + 8;  // this lane's two rows
+  const int ra = r0 + 16 * rw + g, rb = ra + 8;  // this lane's two rows
   const int pa = ra < n ? row_pos[ra] : -1, pb = rb < n ? row_pos[rb] : -1;
   __syncthreads();
   uint32_t qa[NKK][4], ql[NKK][4];
 #pragma unroll
   for (int kk = 0; kk < NKK; ++kk) {
-    const int off = (16 * warp + (lane & 15)) * C::ROW + (16 * kk + 8 * (lane >> 4)) * 2;
+    const int off = (16 * rw + (lane & 15)) * C::ROW + (16 * kk + 8 * (lane >> 4)) * 2;
     ldsm_x4(qa[kk], Qs + off);
     ldsm_x4(ql[kk], Ql + off);
   }
@@ -232,34 +241,35 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     __syncthreads();
     // a warp whose 16 rows are all past n (tree verification: 31 rows in a
     // 64-row block) only helps load the tiles
-    if (r0 + 16 * warp < n) {
+    if (r0 + 16 * rw < n) {
       const int b = kt & 1;
       const uint8_t* ks = KVs + (size_t)b * 2 * C::KV_BYTES;
       const uint8_t* vs = ks + C::KV_BYTES;
       const int* kp = kpos_s + b * AR_BC;
       const float* bt = bias_s + (size_t)b * AR_BR * AR_BC;
-      // scores: 16 rows x 64 keys, n-tile nt = keys 8nt .. 8nt + 7; the
-      // k-step loop is outside so that consecutive MMAs feed 8 different
-      // accumulators (a chain of dependent mma.sync would stall on each)
-      float s[8][4];
+      // scores: 16 rows x this warp's KPW keys, n-tile nt = keys kg KPW +
+      // 8nt .. + 7; the k-step loop is outside so that consecutive MMAs feed
+      // different accumulators (a chain of dependent mma.sync would stall
+      // on each)
+      float s[NTW][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      for (int nt = 0; nt < NTW; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < NKK; ++kk) {
         // matrices of pair np: keys 16np.. x dims lo / hi, keys 16np+8.. x dims lo / hi
-        uint32_t kb[4][4];
+        uint32_t kb[NPW][4];
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          const int key = 16 * np + (lane & 7) + 8 * (lane >> 4);
+        for (int np = 0; np < NPW; ++np) {
+          const int key = kg * KPW + 16 * np + (lane & 7) + 8 * (lane >> 4);
           ldsm_x4(kb[np], ks + key * C::ROW + (16 * kk + 8 * ((lane >> 3) & 1)) * 2);
         }
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int np = 0; np < NPW; ++np) {
           mma_f16(s[2 * np], qa[kk], kb[np][0], kb[np][1]);
           mma_f16(s[2 * np + 1], qa[kk], kb[np][2], kb[np][3]);
         }
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int np = 0; np < NPW; ++np) {
           mma_f16(s[2 * np], ql[kk], kb[np][0], kb[np][1]);
           mma_f16(s[2 * np + 1], ql[kk], kb[np][2], kb[np][3]);
         }
@@ -267,16 +277,16 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       // mask, scale, online softmax (rows a = g, b = g + 8 of this warp)
       float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NTW; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int j = 8 * nt + 2 * t + (e & 1);
+          const int j = kg * KPW + 8 * nt + 2 * t + (e & 1);
           const bool rowb = e >= 2;
           const int rp = rowb ? pb : pa;
           // a positive bias admits the key whatever its position (rows of
           // one sequence among several sharing the cache); otherwise the
           // position rule and min(0, bias) as the reference applies them
-          const float bv = bias ? bt[(16 * warp + g + (rowb ? 8 : 0)) * AR_BC + j] : 0.f;
+          const float bv = bias ? bt[(16 * rw + g + (rowb ? 8 : 0)) * AR_BC + j] : 0.f;
           float v = -INFINITY;
           if (rp >= 0 && (kp[j] <= rp || bv > 0.f)) {
             v = __fdiv_rn(s[nt][e], sdiv);
@@ -294,7 +304,7 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
       const float aa = na == -INFINITY ? 1.f : expf(ma - na), ab = nb == -INFINITY ? 1.f : expf(mb - nb);
       float sa = 0.f, sb = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NTW; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const bool rowb = e >= 2;
@@ -319,9 +329,10 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         o[i][2] *= ab;
         o[i][3] *= ab;
       }
-      // P.V: k-step kk = keys 16kk .. 16kk + 15 (score n-tiles 2kk, 2kk + 1)
+      // P.V: k-step kk = this warp's keys 16kk .. 16kk + 15 (score n-tiles
+      // 2kk, 2kk + 1), tile keys kg KPW + 16kk ..
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < NPW; ++kk) {
         uint32_t pa4[4], pl4[4];
         pa4[0] = pack_hl(s[2 * kk][0], s[2 * kk][1], pl4[0]);
         pa4[1] = pack_hl(s[2 * kk][2], s[2 * kk][3], pl4[1]);
@@ -335,7 +346,8 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
           uint32_t vb[2][4];
 #pragma unroll
           for (int u = 0; u < 2; ++u)
-            ldsm_x4_t(vb[u], vs + (16 * kk + (lane & 15)) * C::ROW + (8 * (nd + 2 * u) + 8 * (lane >> 4)) * 2);
+            ldsm_x4_t(vb[u], vs + (kg * KPW + 16 * kk + (lane & 15)) * C::ROW +
+                                 (8 * (nd + 2 * u) + 8 * (lane >> 4)) * 2);
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             mma_f16(o[nd + 2 * u], pa4, vb[u][0], vb[u][1]);
@@ -351,15 +363,58 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
     }
     __syncthreads();  // buffer b is free for tile kt + 2
   }
+  if constexpr (G > 1) {
+    // key groups 1 .. G-1 leave their states in the free K/V buffers; the
+    // group-0 warp of each row warp adds them in group order
+    constexpr int SLOT = (4 * NDT + 4) * 32;  // floats: o, then (ma, la, mb, lb), lane-minor
+    float* st = reinterpret_cast<float*>(KVs);
+    if (kg > 0) {
+      float* my = st + (size_t)((kg - 1) * RW + rw) * SLOT;
+#pragma unroll
+      for (int nd = 0; nd < NDT; ++nd)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) my[(4 * nd + e) * 32 + lane] = o[nd][e];
+      my[(4 * NDT + 0) * 32 + lane] = ma;
+      my[(4 * NDT + 1) * 32 + lane] = la;
+      my[(4 * NDT + 2) * 32 + lane] = mb;
+      my[(4 * NDT + 3) * 32 + lane] = lb;
+    }
+    __syncthreads();
+    if (kg == 0) {
+#pragma unroll 1
+      for (int q = 1; q < G; ++q) {
+        const float* ot = st + (size_t)((q - 1) * RW + rw) * SLOT;
+        const float qma = ot[(4 * NDT + 0) * 32 + lane], qla = ot[(4 * NDT + 1) * 32 + lane];
+        const float qmb = ot[(4 * NDT + 2) * 32 + lane], qlb = ot[(4 * NDT + 3) * 32 + lane];
+        const float na = fmaxf(ma, qma), nb = fmaxf(mb, qmb);
+        const float fa0 = na == -INFINITY ? 0.f : expf(ma - na), fa1 = na == -INFINITY ? 0.f : expf(qma - na);
+        const float fb0 = nb == -INFINITY ? 0.f : expf(mb - nb), fb1 = nb == -INFINITY ? 0.f : expf(qmb - nb);
+        la = la * fa0 + qla * fa1;
+        lb = lb * fb0 + qlb * fb1;
+#pragma unroll
+        for (int nd = 0; nd < NDT; ++nd) {
+          o[nd][0] = o[nd][0] * fa0 + ot[(4 * nd + 0) * 32 + lane] * fa1;
+          o[nd][1] = o[nd][1] * fa0 + ot[(4 * nd + 1) * 32 + lane] * fa1;
+          o[nd][2] = o[nd][2] * fb0 + ot[(4 * nd + 2) * 32 + lane] * fb1;
+          o[nd][3] = o[nd][3] * fb0 + ot[(4 * nd + 3) * 32 + lane] * fb1;
+        }
+        ma = na;
+        mb = nb;
+      }
+    }
+  }
+  // only the group-0 warps hold final states from here on
+  const bool writer = kg == 0;
+  const bool va = writer && ra < n, vb = writer && rb < n;  // rows this lane writes
   // out[row][h][d] = o / l: lane holds rows a (o[.][0..1]) and b (o[.][2..3]), dims 8nd + 2t, +1
   if (ks == 1) {
     const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
 #pragma unroll
     for (int nd = 0; nd < NDT; ++nd) {
       const int d = 8 * nd + 2 * t;
-      if (ra < n)
+      if (va)
         *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(o[nd][0] * ia, o[nd][1] * ia);
-      if (rb < n)
+      if (vb)
         *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(o[nd][2] * ib, o[nd][3] * ib);
     }
     return;
@@ -372,12 +427,12 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
 #pragma unroll
   for (int nd = 0; nd < NDT; ++nd) {
     const int d = 8 * nd + 2 * t;
-    if (ra < n) *reinterpret_cast<float2*>(part_o + ia_idx * HD + d) = make_float2(o[nd][0], o[nd][1]);
-    if (rb < n) *reinterpret_cast<float2*>(part_o + ib_idx * HD + d) = make_float2(o[nd][2], o[nd][3]);
+    if (va) *reinterpret_cast<float2*>(part_o + ia_idx * HD + d) = make_float2(o[nd][0], o[nd][1]);
+    if (vb) *reinterpret_cast<float2*>(part_o + ib_idx * HD + d) = make_float2(o[nd][2], o[nd][3]);
   }
   if (t == 0) {
-    if (ra < n) part_ml[ia_idx] = make_float2(ma, la);
-    if (rb < n) part_ml[ib_idx] = make_float2(mb, lb);
+    if (va) part_ml[ia_idx] = make_float2(ma, la);
+    if (vb) part_ml[ib_idx] = make_float2(mb, lb);
   }
   __threadfence();
   __syncthreads();
@@ -390,15 +445,15 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
   // merge in z order
   float Ma = -INFINITY, Mb = -INFINITY;
   for (int zz = 0; zz < ks; ++zz) {
-    if (ra < n) Ma = fmaxf(Ma, __ldcg(&part_ml[((size_t)zz * n + ra) * nh + h].x));
-    if (rb < n) Mb = fmaxf(Mb, __ldcg(&part_ml[((size_t)zz * n + rb) * nh + h].x));
+    if (va) Ma = fmaxf(Ma, __ldcg(&part_ml[((size_t)zz * n + ra) * nh + h].x));
+    if (vb) Mb = fmaxf(Mb, __ldcg(&part_ml[((size_t)zz * n + rb) * nh + h].x));
   }
   float accA[NDT][2], accB[NDT][2], La = 0.f, Lb = 0.f;
 #pragma unroll
   for (int nd = 0; nd < NDT; ++nd) accA[nd][0] = accA[nd][1] = accB[nd][0] = accB[nd][1] = 0.f;
   for (int zz = 0; zz < ks; ++zz) {
     const size_t ja = ((size_t)zz * n + ra) * nh + h, jb = ((size_t)zz * n + rb) * nh + h;
-    if (ra < n && Ma != -INFINITY) {
+    if (va && Ma != -INFINITY) {
       const float2 ml = __ldcg(&part_ml[ja]);
       const float f = ml.x == -INFINITY ? 0.f : expf(ml.x - Ma);
       La += ml.y * f;
@@ -409,7 +464,7 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
         accA[nd][1] += v.y * f;
       }
     }
-    if (rb < n && Mb != -INFINITY) {
+    if (vb && Mb != -INFINITY) {
       const float2 ml = __ldcg(&part_ml[jb]);
       const float f = ml.x == -INFINITY ? 0.f : expf(ml.x - Mb);
       Lb += ml.y * f;
@@ -425,19 +480,19 @@ attn_rows_kernel(const float* __restrict__ q, int nh, int nkv, const KT* __restr
 #pragma unroll
   for (int nd = 0; nd < NDT; ++nd) {
     const int d = 8 * nd + 2 * t;
-    if (ra < n)
+    if (va)
       *reinterpret_cast<float2*>(out + ((size_t)ra * nh + h) * HD + d) = make_float2(accA[nd][0] * ia, accA[nd][1] * ia);
-    if (rb < n)
+    if (vb)
       *reinterpret_cast<float2*>(out + ((size_t)rb * nh + h) * HD + d) = make_float2(accB[nd][0] * ib, accB[nd][1] * ib);
   }
   if (tid == 0) cnt[tile] = 0;
 }
 
-template <int HD, typename KT>
+template <int HD, typename KT, int G>
 int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc, const int* bt, int bs,
                 const int* row_pos, const float* bias, const DevParams* P, float* out, int max_n, float sdiv,
                 int t_tot, const SplitWork* sw, cudaStream_t s) {
-  auto kern = attn_rows_kernel<HD, KT>;
+  auto kern = attn_rows_kernel<HD, KT, G>;
   const size_t smem = bias ? ArCfg<HD>::SMEM_BIAS : ArCfg<HD>::SMEM_NOBIAS;
   const int rc = set_smem_limit((const void*)kern, smem, "attention (rows)");
   if (rc) return rc;
@@ -463,6 +518,19 @@ int launch_rows(const float* q, int nh, int nkv, const void* kc, const void* vc,
   return LUMINA_OK;
 }
 
+// few rows leave warps of the 64-row block idle: split each tile's keys
+// over them instead (4 key groups up to 16 rows, 2 up to 32)
+template <int HD, typename KT>
+int launch_rows_g(const float* q, int nh, int nkv, const void* kc, const void* vc, const int* bt, int bs,
+                  const int* row_pos, const float* bias, const DevParams* P, float* out, int max_n, float sdiv,
+                  int t_tot, const SplitWork* sw, cudaStream_t s) {
+  if (max_n <= 16)
+    return launch_rows<HD, KT, 4>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+  if (max_n <= 32)
+    return launch_rows<HD, KT, 2>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+  return launch_rows<HD, KT, 1>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+}
+
 }  // namespace
 
 int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, const void* kc, const void* vc,
@@ -470,11 +538,15 @@ int launch_attention_rows(bool fp16, int hd, const float* q, int nh, int nkv, co
                           int max_n, int t_tot, const SplitWork* sw, cudaStream_t s) {
   const float sdiv = std::max(sqrtf((float)hd), 1e-6f);  // max(hd ** 0.5, 1e-6), chat.py:278
   if (hd == 128)
-    return fp16 ? launch_rows<128, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s)
-                : launch_rows<128, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+    return fp16 ? launch_rows_g<128, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot,
+                                             sw, s)
+                : launch_rows_g<128, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot,
+                                            sw, s);
   if (hd == 64)
-    return fp16 ? launch_rows<64, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s)
-                : launch_rows<64, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot, sw, s);
+    return fp16 ? launch_rows_g<64, __half>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot,
+                                            sw, s)
+                : launch_rows_g<64, float>(q, nh, nkv, kc, vc, bt, bs, row_pos, bias, P, out, max_n, sdiv, t_tot,
+                                           sw, s);
   set_error("attention: head_dim %d not built (64, 128)", hd);
   return LUMINA_E_UNSUPPORTED;
 }
