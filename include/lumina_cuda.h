@@ -251,7 +251,8 @@ int lumina_kv_attend(lumina_model* m, int layer, const float* q_host, float* out
  * updated in place): the drop-in for ChatModel._layer(x, lyr, cache, pos0,
  * attn_bias, pos_override) (chat.py:232-304). Appends n KV rows at the
  * current length. pos_override_host (n ints) and bias_host ((n, len+n) fp32,
- * 0 / -inf) may be NULL. */
+ * 0 / -inf; a positive entry admits its key whatever the key's position, as
+ * for lumina_forward) may be NULL. */
 int lumina_layer_forward(lumina_model* m, int layer, float* x_dev, int n, int pos0,
                          const int* pos_override_host, const float* bias_host,
                          void* stream);
