@@ -190,7 +190,8 @@ struct TcbArgs {
   int ldy;
   const float* resid;
   int ldr;
-  int epi;      // EPI_STORE, EPI_RESID, EPI_SWIGLU
+  int epi;      // EPI_STORE, EPI_RESID, EPI_SWIGLU, EPI_ROPE_KV
+  RopeKV rk;    // EPI_ROPE_KV: RoPE + paged KV append of the fused q/k/v rows
   int qk_rows;  // EPI_STORE: rows < qk_rows of a fused q/k/v weight go to their un-permuted index
   int hd;
   int S;        // K slices = the cluster size (the S CTAs of a cluster share their super-tiles)
@@ -212,11 +213,66 @@ __device__ __forceinline__ int tcb_out_row(const TcbArgs& a, int row) {
   return h * a.hd + (rr >> 1) + (rr & 1) * (a.hd >> 1);
 }
 
+// RoPE + paged KV append of the fused q/k/v rows (row, row + 1) = (x1, x2)
+// of activation row b: q and k rows hold rotation pairs side by side, so the
+// pair rotates by the row's position (chat.py:99-100, fp32 products rounded
+// separately) into q_out or the K cache; v rows go to the V cache.
+__device__ __forceinline__ void tcb_rope_store(const TcbArgs& a, int row, int b, float x1, float x2) {
+  const RopeKV& k = a.rk;
+  const int qrows = k.nh * k.hd, krows = k.nkv * k.hd, half = k.hd / 2;
+  const int tt = *k.t_prev + k.row_base + b;
+  const size_t blk = k.block_table[tt / k.bs], off = tt % k.bs;
+  if (row < qrows + krows) {
+    const bool isq = row < qrows;
+    const int rr = isq ? row : row - qrows;
+    const int hh = rr / k.hd, p = (rr % k.hd) >> 1;
+    const size_t ci = (size_t)k.row_pos[b] * half + p;
+    const float c = k.cos_t[ci], s = k.sin_t[ci];
+    const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    const float o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+    if (isq) {
+      float* q = k.q_out + (size_t)b * qrows + (size_t)hh * k.hd;
+      q[p] = o1;
+      q[p + half] = o2;
+    } else {
+      const size_t base = ((blk * k.nkv + hh) * k.bs + off) * k.hd;
+      if (k.kv_fp16) {
+        __half* kc = static_cast<__half*>(k.kcache) + base;
+        kc[p] = __float2half_rn(o1);
+        kc[p + half] = __float2half_rn(o2);
+      } else {
+        float* kc = static_cast<float*>(k.kcache) + base;
+        kc[p] = o1;
+        kc[p + half] = o2;
+      }
+    }
+  } else {
+    const float vv[2] = {x1, x2};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int rr = row + e - qrows - krows;
+      const size_t idx = ((blk * k.nkv + rr / k.hd) * k.bs + off) * k.hd + rr % k.hd;
+      if (k.kv_fp16) static_cast<__half*>(k.vcache)[idx] = __float2half_rn(vv[e]);
+      else static_cast<float*>(k.vcache)[idx] = vv[e];
+    }
+  }
+}
+
 // Epilogue of one finished value pair of this lane: rows r0 (+0, +8) of
 // activation row b; v[0] = row r0 + g, v[1] = row r0 + g + 8 (already / L).
-// SwiGLU pairs rows 2i, 2i+1: the odd row lives in the lane 4 above.
+// SwiGLU and RoPE pair rows 2i, 2i+1: the odd row lives in the lane 4 above.
 __device__ __forceinline__ void tcb_emit(const TcbArgs& a, int r0, int b, float v0, float v1, int lane) {
   const int g = lane >> 2;
+  if (a.epi == EPI_ROPE_KV) {
+    const float n0 = __shfl_down_sync(0xffffffffu, v0, 4), n1 = __shfl_down_sync(0xffffffffu, v1, 4);
+    if (b >= a.nb || (g & 1)) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r0 + g + 8 * h;
+      if (row + 1 < a.rows) tcb_rope_store(a, row, b, h ? v1 : v0, h ? n1 : n0);
+    }
+    return;
+  }
   if (a.epi == EPI_SWIGLU) {
     const float n0 = __shfl_down_sync(0xffffffffu, v0, 4), n1 = __shfl_down_sync(0xffffffffu, v1, 4);
     if (b >= a.nb || (g & 1)) return;
@@ -439,6 +495,8 @@ __global__ void __launch_bounds__(BW * 32, 1) gemv_tcb_kernel(TcbArgs a) {
             const float e2 = expf(-fminf(fmaxf(v0, -40.f), 40.f));  // chat.py:300-302, the +-40 clip
             a.y[(size_t)b * a.ldy + (row >> 1)] = v0 / (1.0f + e2) * v1;
           }
+        } else if (a.epi == EPI_ROPE_KV) {
+          if (row + 1 < a.rows) tcb_rope_store(a, row, b, v0, v1);
         } else {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -536,13 +594,14 @@ size_t gemv_tcb_frag_bytes(int M, int cols) {
 
 int gemv_tcb_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                     void* frag, size_t frag_bytes, float* y, int ldy, int epi, const float* resid, int ldr,
-                    int qk_rows, int hd, cudaStream_t s) {
+                    int qk_rows, int hd, cudaStream_t s, const RopeKV* rk) {
   if (!w->mma || (w->group % 64) || M < 1 || M > 32) return LUMINA_E_UNSUPPORTED;
   const int gp = w->group / 64;
   if ((gp & (gp - 1)) || gp > 4) return LUMINA_E_UNSUPPORTED;
-  if (epi != EPI_STORE && epi != EPI_RESID && epi != EPI_SWIGLU) return LUMINA_E_UNSUPPORTED;
-  if (epi == EPI_SWIGLU && (w->rows & 1)) {
-    set_error("gemv_tcb: SwiGLU needs an even row count");
+  if (epi != EPI_STORE && epi != EPI_RESID && epi != EPI_SWIGLU && (epi != EPI_ROPE_KV || !rk))
+    return LUMINA_E_UNSUPPORTED;
+  if ((epi == EPI_SWIGLU || epi == EPI_ROPE_KV) && (w->rows & 1)) {
+    set_error("gemv_tcb: a paired epilogue needs an even row count");
     return LUMINA_E_ARG;
   }
   const int NB = tcb_nb(M), P = w->n_chunks / 2;
@@ -572,6 +631,7 @@ int gemv_tcb_launch(const lumina_weight* w, const float* x, int ldx, int M, cons
   a.ldr = ldr;
   a.epi = epi;
   a.qk_rows = epi == EPI_STORE ? qk_rows : 0;
+  if (rk) a.rk = *rk;
   a.hd = hd > 0 ? hd : 1;
   a.fault = fault;
   a.spin = wait_spin_limit();

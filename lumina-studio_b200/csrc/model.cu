@@ -426,17 +426,10 @@ int gemv_any(lumina_model* m, const lumina_weight* w, const float* x, int ldx, i
     }
     if (n <= TCB_MAX_ROWS && m->x16) {
       // 5..32 rows (decode batches, tree verification): the batched
-      // tensor-pipe GEMV, int16 activations like the decode GEMV; the fused
-      // q/k/v rows go to qkv_buf in their original order for the RoPE + KV
-      // append kernel
-      const bool qkv = epi == EPI_ROPE_KV;
-      const int width = rk ? (rk->nh + 2 * rk->nkv) * rk->hd : 0;
-      int rc = gemv_tcb_launch(w, x, ldx, n, norm, m->c.eps, m->x16, m->x16_bytes, qkv ? m->qkv_buf : y,
-                               qkv ? width : ldy, qkv ? EPI_STORE : epi, resid, ldr,
-                               qkv ? (rk->nh + rk->nkv) * rk->hd : 0, rk ? rk->hd : 0, m->stream);
-      if (rc == LUMINA_OK && qkv)
-        rc = launch_rope_append(rk->kv_fp16, m->qkv_buf, rk->nh, rk->nkv, rk->hd, rk->cos_t, rk->sin_t, rk->row_pos,
-                                m->P_dev, rk->block_table, rk->bs, rk->kcache, rk->vcache, rk->q_out, n, m->stream);
+      // tensor-pipe GEMV, int16 activations like the decode GEMV, RoPE + KV
+      // append fused into its epilogue for the q/k/v rows
+      const int rc = gemv_tcb_launch(w, x, ldx, n, norm, m->c.eps, m->x16, m->x16_bytes, y, ldy, epi, resid, ldr, 0, 0,
+                                     m->stream, rk);
       if (rc != LUMINA_E_UNSUPPORTED) return rc;
     }
     if (n >= TC05_MIN_ROWS && m->x16 && !exact_rows) {

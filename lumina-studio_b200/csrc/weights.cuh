@@ -241,7 +241,7 @@ int dense_tc05_launch(const __half* W, int rows, int K, const float* x, int ldx,
 // norm_w is given) -> int16 B fragments in `frag` (gemv_tcb_frag_bytes(M,
 // cols) bytes, 16-byte aligned) -> y. Epilogues EPI_STORE (rows < qk_rows of
 // a fused q/k/v weight are stored at their un-permuted index, head size hd),
-// EPI_RESID, EPI_SWIGLU. K is split over the CTAs of a thread-block
+// EPI_RESID, EPI_SWIGLU, EPI_ROPE_KV (with `rk`, as the decode GEMV). K is split over the CTAs of a thread-block
 // cluster (partials combined over distributed shared memory, in slice
 // order) when the fragments of a whole row do not fit a CTA's shared memory
 // or the grid would leave SMs idle. LUMINA_E_UNSUPPORTED when the weight or
@@ -249,7 +249,7 @@ int dense_tc05_launch(const __half* W, int rows, int K, const float* x, int ldx,
 size_t gemv_tcb_frag_bytes(int M, int cols);
 int gemv_tcb_launch(const lumina_weight* w, const float* x, int ldx, int M, const float* norm_w, float eps,
                     void* frag, size_t frag_bytes, float* y, int ldy, int epi, const float* resid, int ldr,
-                    int qk_rows, int hd, cudaStream_t s);
+                    int qk_rows, int hd, cudaStream_t s, const RopeKV* rk = nullptr);
 // per-device fragment scratch for the library's own entry points
 int tcb_frag_scratch(int device, size_t bytes, void** out);
 
