@@ -139,42 +139,66 @@ def hf_cfg(cfg: dict) -> dict:
 _MULTIPLIERS = (1.0, 0.8, 0.65, 0.5, 0.4, 0.3, 0.2)  # ptq_ladder.py:235
 
 
+def _nearest_level(wn, lv, L: int):
+    """Index of the level nearest to each of `wn`, the first index winning a
+    tie: ``np.abs(wn[..., None] - lv).argmin(-1)`` of ptq_ladder.py:238-239,
+    314, without the (..., L + 1) distance tensor. The nearest level is one
+    of the three around ``floor((wn + 1) L / 2)`` (the floor can be off by
+    one where wn sits on a level); they are compared in index order."""
+    import torch
+    k = torch.clamp(torch.floor((wn + 1.0) * (L / 2.0)), 0, L).long()
+    best = torch.clamp(k - 1, 0, L)
+    best_d = (wn - lv[best]).abs()
+    for cand in (k, torch.clamp(k + 1, 0, L)):
+        d = (wn - lv[cand]).abs()
+        take = d < best_d
+        best = torch.where(take, cand, best)
+        best_d = torch.where(take, d, best_d)
+    return best
+
+
 def _quantize_gpu(w, bits: int, group: int):
-    """Lumina round-to-nearest codes with the MSE scale search of
-    ptq_ladder.py:215-249 (seven absmax multipliers, first minimum wins) in
-    fp32 on the GPU, scales rounded to fp16 values. `w` is a (rows, cols)
-    float32 CUDA tensor; a last group narrower than `group` is scored over
-    its own columns, as the reference does. Returns (codes uint8 (rows,
+    """Lumina codes and scales of one weight, the reference's RTN + MSE scale
+    search (ptq_ladder.py:215-249, 370-399 with H = I; seven absmax
+    multipliers, the first minimum wins) in fp64 on the weight's device:
+    codes are the nearest levels of w / s with the unrounded scale, and the
+    stored scale is s rounded to fp32 and then to fp16, as the file writer
+    does. `w` is a (rows, cols) float32 tensor; a last group narrower than
+    `group` is scored over its own columns. Returns (codes uint8 (rows,
     cols), scales float32 (rows, ceil(cols/group))). This makes benchmark
     inputs: it is the reference's quantizer restated in torch, not code
     under test."""
     import torch
     L = (1 << bits) - 1
+    # the reference's levels, np.linspace(-1, 1, 2^b) (ptq_ladder.py:58-59)
+    lv = torch.from_numpy(np.linspace(-1.0, 1.0, L + 1)).to(w.device)
     rows, cols = w.shape
     ng = -(-cols // group)
     pad = ng * group - cols
+    w = w.double()
     if pad:
         w = torch.nn.functional.pad(w, (0, pad))  # zeros never raise a group's absmax
     wg = w.view(rows, ng, group)
-    valid = torch.ones(ng, group, device=w.device, dtype=w.dtype)
+    valid = torch.ones(ng, group, device=w.device, dtype=torch.bool)
     if pad:
-        valid[-1, group - pad:] = 0.0
-    cnt = valid.sum(-1)
+        valid[-1, group - pad:] = False
+    cnt = valid.sum(-1).double()
     amax = wg.abs().amax(-1).clamp_min(1e-12)
     best_e = best_s = None
     for f in _MULTIPLIERS:
         s = (amax * f).clamp_min(1e-12)
         wn = wg / s[..., None]
-        c = torch.clamp(torch.round((wn + 1.0) * (L / 2.0)), 0, L)
-        e = (((wn - (c * (2.0 / L) - 1.0)) ** 2) * valid).sum(-1) / cnt
+        err = torch.where(valid, (wn - lv[_nearest_level(wn, lv, L)]) ** 2, 0.0)
+        e = err.sum(-1) / cnt
+        del wn, err
         if best_e is None:
             best_e, best_s = e, s
         else:
             take = e < best_e
             best_e = torch.where(take, e, best_e)
             best_s = torch.where(take, s, best_s)
-    s16 = best_s.half().float()
-    c = torch.clamp(torch.round((wg / s16[..., None] + 1.0) * (L / 2.0)), 0, L).to(torch.uint8)
+    c = _nearest_level(wg / best_s[..., None], lv, L).to(torch.uint8)
+    s16 = best_s.float().half().float()
     return c.view(rows, ng * group)[:, :cols].contiguous(), s16
 
 
