@@ -1,6 +1,6 @@
 """bench.py's byte accounting and argument rules (CPU): the config-3 sweep's
-bytes per call, the virtual-MoE records' shapes and map, and the refusal of
-invalid timing arguments."""
+bytes per call, the virtual-MoE records' shapes and map, the refusal of
+invalid timing arguments, and the CPU baseline's whole-token sample."""
 import numpy as np
 import pytest
 
@@ -49,3 +49,28 @@ def test_cpu_gemv_leg_times_and_memoises():
     t = bench.cpu_gemv_us(256, 512, 4, cache)
     assert t > 0 and cache == {(256, 512, 4): t}
     assert bench.cpu_gemv_us(256, 512, 4, cache) == t
+
+
+def test_cpu_sample_runs_every_layer_over_distinct_weight_sets():
+    """The CPU baseline's step is one whole token: every layer and the head.
+    Layers l and l + 4 share one fp32 weight set, neighbouring layers do
+    not, so a set is re-read from DRAM only after the other sets' bytes
+    have streamed through the caches; the step's token is the argmax of the
+    head over the last layer's output."""
+    cfg = dict(synthetic.TINY, num_hidden_layers=6)
+    s = bench.CpuDecodeSample(cfg, weight_sets=4)
+    w = s.m._wcache
+    q = [w[f"model.layers.{l}.self_attn.q_proj.weight"] for l in range(6)]
+    assert q[0] is q[4] and q[1] is q[5]
+    assert len({id(a) for a in q[:4]}) == 4
+    assert not any(np.shares_memory(a, b) for a in q[:4] for b in q[:4] if a is not b)
+    assert np.array_equal(q[0], q[1])  # equal values, distinct memory
+    tok0, pos0 = s.tok, s.pos
+    cache = {l: tuple(np.array(a, copy=True) for a in s.cache[l]) for l in range(6)}
+    h = s.emb[[tok0]]
+    for l in range(6):
+        h = s.m.layer(h, l, cache, pos0)
+    want = int(np.argmax((h[-1:] @ s.head_t)[0].astype(np.float64)))
+    dt = s.step()
+    assert dt > 0 and s.pos == pos0 + 1 and s.tok == want
+    assert "all 6" in s.describe(1) and "4 distinct weight sets" in s.describe(1)
