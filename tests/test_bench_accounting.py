@@ -1,5 +1,5 @@
-"""bench.py's byte accounting and argument rules (CPU): the config-3 sweep's
-bytes per call, the virtual-MoE records' shapes and map, the refusal of
+"""bench.py's byte accounting and argument rules (CPU): the GEMV sweep's bytes
+per call (7B shapes x int4/int3/int2/binary x batch 1/4/16), the virtual-MoE records' shapes and map, the refusal of
 invalid timing arguments, and the CPU baseline's whole-token sample."""
 import numpy as np
 import pytest
@@ -15,7 +15,7 @@ def test_sweep_bytes_formula():
     assert bench.sweep_bytes(32000, 4096, 1, 128, 16) == 32000 * 512 + 32000 * 32 * 2 + 16 * 4096 * 4 + 16 * 32000 * 4
 
 
-def test_sweep_covers_config3():
+def test_sweep_covers_7b_shapes_kinds_and_batches():
     assert set(bench.SWEEP_SHAPES) == {(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)}
     assert [k for k, _, _ in bench.SWEEP_KINDS] == ["int4", "int3", "int2", "binary"]
     assert bench.SWEEP_BATCHES == (1, 4, 16)
