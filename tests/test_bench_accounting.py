@@ -1,6 +1,7 @@
-"""bench.py's byte accounting and argument rules (CPU): the GEMV sweep's bytes
-per call (7B shapes x int4/int3/int2/binary x batch 1/4/16), the virtual-MoE records' shapes and map, the refusal of
-invalid timing arguments, and the CPU baseline's whole-token sample."""
+"""bench.py's byte accounting and argument rules (CPU): the GEMV sweep's
+bytes per call (7B shapes x int4/int3/int2/binary x batch 1/4/16), the
+virtual-MoE records' shapes and map, the refusal of invalid timing
+arguments, and the CPU baseline's whole-token sample."""
 import numpy as np
 import pytest
 
