@@ -797,11 +797,12 @@ def generate_shared_prefix(model: CudaChatModel, prefix_ids, suffixes, max_token
     """Greedy decode of B sequences ``prefix_ids + suffixes[b]`` that share
     the prefix's KV rows on the device. The prefix is prefilled once; the
     suffixes go in forwards of up to 64 rows, and every decode step is one
-    forward of the B (<= 64) live sequences' rows. Rows of all sequences live in the one KV cache
-    side by side; each row attends to the prefix and to its own sequence's
-    rows only (an additive -inf bias on the others, the tree-verification
-    forward of ``verify_tree``) at its own true position, so sequence b sees
-    exactly what ``generate(prefix + suffixes[b])`` would.
+    forward of the B (<= 64) live sequences' rows. Rows of all sequences
+    live in the one KV cache side by side; each row attends to the prefix
+    and to its own sequence's rows only (an additive -inf bias on the
+    others, the tree-verification forward of ``verify_tree``) at its own
+    true position, so sequence b sees exactly what ``generate(prefix +
+    suffixes[b])`` would. ``max_tokens`` >= 1 tokens per sequence.
 
     Returns ``{"tokens": [list per sequence], "first_logits": (B, vocab)}``
     (the logits after each full prompt); with ``timed`` also the wall time of
@@ -811,6 +812,8 @@ def generate_shared_prefix(model: CudaChatModel, prefix_ids, suffixes, max_token
     B = len(sfx)
     if B < 1 or any(len(s) < 1 for s in sfx) or not prefix:
         raise LuminaError(1, "generate_shared_prefix: a non-empty prefix and non-empty suffixes are needed")
+    if max_tokens < 1:
+        raise LuminaError(1, "generate_shared_prefix: max_tokens %d, at least 1" % max_tokens)
     chunk = min(64, model.max_rows)  # rows of one biased forward (the library's bias buffer holds 64)
     if B > chunk:
         raise LuminaError(1, "generate_shared_prefix: %d sequences, at most %d" % (B, chunk))

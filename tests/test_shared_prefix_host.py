@@ -90,3 +90,5 @@ def test_rejects_empty_and_too_many():
         generate_shared_prefix(m, [1, 2], [[3], []])
     with pytest.raises(Exception):
         generate_shared_prefix(m, [1, 2], [[3]] * 65)
+    with pytest.raises(Exception):
+        generate_shared_prefix(m, [1, 2], [[3]], max_tokens=0)
