@@ -218,6 +218,33 @@ class CpuDecodeSample:
                 f"length {PROMPT}; numpy fp32 BLAS over weights converted once")
 
 
+def cpu_numba_gemv(N=11008, K=4096, calls=5):
+    """The reference's numba int8 GEMV (fused._gemv_int8, restated in
+    oracle/tops.py) on one host core at the 7B gate/up shape, batch 1: the
+    kernel that serves fused_gemv_int8 when the compiled tops kernel is
+    absent (tops_int8.c is ARM-only). Median of `calls` after a compiling
+    call; bytes = int8 weights + row scales + activations + outputs."""
+    from oracle.tops import numba_gemv_int8, q8_repack
+    gemv = numba_gemv_int8()
+    if gemv is None:
+        return {"unavailable": "numba is not importable"}
+    rng = np.random.default_rng(0)
+    wq = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    ws = (rng.random(N, dtype=np.float32) * 0.01 + 1e-3).astype(np.float32)
+    xq, xs = q8_repack(rng.standard_normal(K).astype(np.float32))
+    out = np.empty(N, np.float32)
+    gemv(xq, xs, wq, ws, out)
+    ts = []
+    for _ in range(calls):
+        t0 = time.perf_counter()
+        gemv(xq, xs, wq, ws, out)
+        ts.append(time.perf_counter() - t0)
+    ms = float(np.median(ts)) * 1e3
+    nbytes = N * K + N * 4 + K + (K // 32) * 4 + N * 4
+    return {"shape": f"{N}x{K} int8, batch 1", "ms": ms, "gb_s": nbytes / ms / 1e6, "cores": 1,
+            "impl": "fused._gemv_int8 (fused.py:163-184) restated, numba"}
+
+
 def cpu_baseline(cfg, tokens=16, budget_s=20.0):
     s = CpuDecodeSample(cfg)
     s.step()  # converts the fp32 weights (outside the timing, as the reference caches them)
@@ -227,7 +254,7 @@ def cpu_baseline(cfg, tokens=16, budget_s=20.0):
         tot += s.step()
         n += 1
     return {"value": n / tot, "unit": UNIT, "cores": blas_threads(), "kind": "port",
-            "sample": s.describe(n)}
+            "sample": s.describe(n), "numba_gemv_int8": cpu_numba_gemv()}
 
 
 def run_reference(args, cfg):
@@ -243,7 +270,8 @@ def run_reference(args, cfg):
         tot += s.step()
     wall = time.perf_counter() - t0
     value = args.steps / tot
-    cb = {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port", "sample": s.describe(args.steps)}
+    cb = {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port", "sample": s.describe(args.steps),
+          "numba_gemv_int8": cpu_numba_gemv()}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",

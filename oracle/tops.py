@@ -13,8 +13,14 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
     ``TensorContainer`` payload that feeds ``fused_gemv_int8``)
   * ``self_test_inputs`` — the known-answer inputs of ``tops._self_test``
     (tops.py:152-238, seed 11, N=37, K=256)
+  * ``numba_gemv_int8`` — ``fused._gemv_int8`` (fused.py:163-184), the
+    numba kernel that serves ``fused_gemv_int8`` when the compiled tops
+    kernel is absent, restated with its loop order and fp32 rounding so that
+    the CPU baseline can time the reference's own GEMV path
 """
 from __future__ import annotations
+
+import functools
 
 import numpy as np
 
@@ -73,3 +79,30 @@ def self_test_inputs():
     q4 = ((codes[:, 0::2] & 15) | ((codes[:, 1::2] & 15) << 4)).astype(np.uint8)
     q4s = (np.abs(rng.standard_normal((N, K // 32))).astype(np.float32) + 0.01)
     return {"xq": xq, "xs": xs, "wq": wq, "ws": ws, "q4": q4, "q4s": q4s}
+
+
+@functools.lru_cache(maxsize=1)
+def numba_gemv_int8():
+    """The compiled ``gemv(xq, xs, wq, ws, out)`` of fused.py:163-184: one
+    core, rows in order; per row an int32 dot per 32-element block, and
+    ``acc += f32(dot) * f32(xs[b]) * f32(ws[n])`` in block order, all in
+    fp32. None when numba is not importable."""
+    try:
+        import numba
+    except ImportError:
+        return None
+
+    @numba.njit(cache=False)
+    def gemv(xq, xs, wq, ws, out):
+        nrows, k = wq.shape
+        for n in range(nrows):
+            s = np.float32(ws[n])
+            acc = np.float32(0.0)
+            for b in range(k // 32):
+                dot = np.int32(0)
+                for j in range(b * 32, b * 32 + 32):
+                    dot += np.int32(xq[j]) * np.int32(wq[n, j])
+                acc += np.float32(dot) * np.float32(xs[b]) * s
+            out[n] = acc
+
+    return gemv

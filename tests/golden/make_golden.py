@@ -278,6 +278,13 @@ def make_tops(ref):
     xb = rng.standard_normal((1, 512)).astype(np.float32)
     out["bin_S"], out["bin_s"], out["bin_x"] = S, s, xb
     out["bin_y"] = cpu_binary_gemv(xb, pack_signs(S), s, 512)
+    # the numba kernel behind fused_gemv_int8 (fused.py:163-184) on the KAT inputs
+    from lumina_framework import fused
+    if not fused._HAS_NUMBA:
+        raise SystemExit("numba is needed for the fused._gemv_int8 fixture")
+    y = np.empty(d["wq"].shape[0], np.float32)
+    fused._gemv_int8(d["xq"], d["xs"], d["wq"], d["ws"], y)
+    out["numba_gemv_int8"] = y
     np.savez_compressed(os.path.join(HERE, "tops_kat.npz"), **out)
     print("tops KAT written")
 

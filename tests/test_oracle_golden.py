@@ -301,3 +301,18 @@ def test_wide_oracle_matches_reference(golden, wide_oracle):
         pos += 1
         assert rel((hh @ head)[0], g[f"logits_step{s}"]) < 1e-5, s
     assert generate(m, prompt, len(g["tokens"])) == [int(t) for t in g["tokens"]]
+
+
+def test_numba_gemv_int8_port_matches_reference_kernel():
+    """The numba restatement of fused._gemv_int8 (the GEMV the CPU baseline
+    times): bit-equal to the reference's own kernel on the KAT inputs, and
+    within fp32 rounding of the int-exact ref_int8."""
+    gemv = tops.numba_gemv_int8()
+    if gemv is None:
+        pytest.skip("numba not importable")
+    g = np.load(os.path.join(GOLDEN, "tops_kat.npz"))
+    out = np.empty(g["wq"].shape[0], np.float32)
+    gemv(g["xq"], g["xs"], g["wq"], g["ws"], out)
+    assert np.array_equal(out, g["numba_gemv_int8"])
+    ref = g["ref_int8"]
+    assert np.allclose(out, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
