@@ -75,3 +75,14 @@ def test_cpu_sample_runs_every_layer_over_distinct_weight_sets():
     dt = s.step()
     assert dt > 0 and s.pos == pos0 + 1 and s.tok == want
     assert "all 6" in s.describe(1) and "4 distinct weight sets" in s.describe(1)
+
+
+def test_numba_leg_reports_failure_as_unavailable(monkeypatch):
+    """The numba GEMV leg sits beside the decode baseline: an error inside it
+    (numba missing or failing on the host) becomes an "unavailable" entry,
+    never an exception that would lose the bench line."""
+    def broken():
+        raise RuntimeError("no jit here")
+    monkeypatch.setattr(bench, "cpu_numba_gemv", broken)
+    got = bench.numba_leg()
+    assert got == {"unavailable": "RuntimeError: no jit here"}
